@@ -1,0 +1,264 @@
+/*
+ * vbsr_b200.h — C ABI of the B200-native variable-block sparse-row (VBSR) SpMM engine.
+ *
+ * Computes FP32, non-transpose C = A * B where A is a packed VBSR matrix (block heights and
+ * widths independently in {8,16,...,64}, blocks column-major, packed in row order) and B, C are
+ * dense column-major panels of width 8, 16, 32 or 64 (leading dimensions K and M, the scalar
+ * column and row counts of A).
+ *
+ * Every entry point takes plain pointers and sizes and returns a vbsr_status. On failure a
+ * human-readable message is kept per host thread and returned by vbsr_get_last_error().
+ *
+ * Reference interface each entry point replaces (King-Clawthorne/VarBlockSpMM):
+ *   vbsr_host_validate          HostMatrix::validate        include/varblockspmm/vbsr.hpp:28,
+ *                                                           src/format/vbsr.cpp:29-82
+ *   vbsr_matrix_create          Matrix::Matrix(HostMatrix)  vbsr.hpp:44, vbsr.cpp:84-113
+ *   vbsr_matrix_destroy         Matrix::~Matrix / release   vbsr.hpp:45, vbsr.cpp:114-127
+ *   vbsr_matrix_device_view     Matrix::device_view         vbsr.hpp:51, vbsr.cpp:163-166
+ *   vbsr_matrix_info            Matrix::scalar_rows/cols    vbsr.hpp:52-53
+ *   vbsr_plan_create            Plan::Plan                  vbsr.hpp:106, src/plan/plan.cpp:5-18
+ *   vbsr_plan_execute           Plan::execute               vbsr.hpp:110, plan.cpp:19-22
+ *   vbsr_plan_launch_count      Plan::launch_count          vbsr.hpp:112, plan.cpp:23-31
+ *   vbsr_launch_row_owned       launch_row_owned            vbsr.hpp:158-159,
+ *                                                           src/kernels/row_owned.cu:397-423
+ *   vbsr_launch_row_owned_scalar launch_row_owned_scalar    vbsr.hpp:161, row_owned.cu:376-395
+ *   vbsr_generate               generate(GeneratorOptions)  vbsr.hpp:69-80,
+ *                                                           src/format/generator.cpp:7-88
+ * Entry points with no single reference counterpart (the multi-GPU block-row partition, the
+ * on-device value generator, plan diagnostics) say so in their comments.
+ */
+#ifndef VBSR_B200_H
+#define VBSR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VBSR_B200_ABI_VERSION 1
+
+/* Status codes. The C++ drop-in header maps INVALID_ARGUMENT to std::invalid_argument and every
+ * other non-OK code to std::runtime_error, as the reference does (vbsr.cpp:13-17,32-80;
+ * plan.cpp:9-17; row_owned.cu:367-372). */
+typedef enum vbsr_status {
+  VBSR_OK = 0,
+  VBSR_INVALID_ARGUMENT = 1, /* malformed matrix, bad RHS width, rejected kernel, bad sizes */
+  VBSR_CUDA_ERROR = 2,       /* a CUDA runtime call failed; message is cudaGetErrorString  */
+  VBSR_TIMEOUT = 3,          /* a bounded in-kernel wait gave up (pipeline stalled)         */
+  VBSR_BOUNDS_VIOLATION = 4, /* the bounds-checked kernel found an out-of-range index      */
+  VBSR_OUT_OF_MEMORY = 5     /* host allocation failed                                     */
+} vbsr_status;
+
+/* cudaStream_t is a pointer to this opaque driver type; callers may pass a cudaStream_t, a
+ * torch.cuda.Stream.cuda_stream integer, or NULL for the legacy default stream. */
+typedef struct CUstream_st* vbsr_stream_t;
+
+/* Non-owning view of a host VBSR matrix: the fields of HostMatrix (vbsr.hpp:16-29) as pointers
+ * plus element counts, so that the size checks of HostMatrix::validate can be restated. */
+typedef struct vbsr_host_matrix_view {
+  int32_t block_rows, block_cols;
+  const int32_t* row_ptr;        size_t row_ptr_len;        /* block_rows + 1            */
+  const int32_t* block_col;      size_t block_col_len;      /* nnzb                      */
+  const int32_t* row_size;       size_t row_size_len;       /* block_rows                */
+  const int32_t* col_size;       size_t col_size_len;       /* block_cols                */
+  const int64_t* row_scalar_off; size_t row_scalar_off_len; /* block_rows + 1            */
+  const int64_t* col_scalar_off; size_t col_scalar_off_len; /* block_cols + 1            */
+  const int64_t* value_off;      size_t value_off_len;      /* nnzb + 1                  */
+  const float* values;           size_t values_len;         /* value_off[nnzb]; values may be
+                                                               NULL only where stated    */
+} vbsr_host_matrix_view;
+
+/* Non-owning device view in the reference's own layout (DeviceMatrix, vbsr.hpp:32-38). The
+ * pointers are device pointers owned by the vbsr_matrix they came from. `values` is in the
+ * engine's re-laid-out block format (each h x w block stored as h/8 row panels, each panel
+ * 8 x w column-major), not the reference's column-major block layout; the launchers below
+ * accept views produced by this library only. */
+typedef struct vbsr_device_matrix {
+  int32_t block_rows, block_cols, nnzb;
+  int64_t scalar_rows, scalar_cols;
+  const int32_t *row_ptr, *block_col, *row_size, *col_size;
+  const int64_t *row_scalar_off, *col_scalar_off, *value_off;
+  const float* values;
+} vbsr_device_matrix;
+
+typedef struct vbsr_matrix_info {
+  int32_t block_rows, block_cols;
+  int64_t nnzb;
+  int64_t scalar_rows, scalar_cols; /* M and K */
+  int64_t value_count;
+  int64_t device_bytes;             /* bytes of device memory owned by the matrix */
+  int32_t device;                   /* CUDA ordinal the matrix lives on           */
+  int32_t row_begin, row_end;       /* block-row range of the source view it holds */
+} vbsr_matrix_info;
+
+typedef struct vbsr_matrix vbsr_matrix; /* owning device copy (Matrix) */
+typedef struct vbsr_plan vbsr_plan;     /* execution plan (Plan)       */
+
+/* ---- Errors ------------------------------------------------------------------------------- */
+
+/* Message of the last failing call on this host thread ("" if none). Valid until the next call
+ * on this thread. */
+const char* vbsr_get_last_error(void);
+
+/* ---- Host format -------------------------------------------------------------------------- */
+
+/* HostMatrix::validate (vbsr.cpp:29-82): the same checks in the same order, with the same
+ * messages. Returns VBSR_INVALID_ARGUMENT on the first failing check. */
+vbsr_status vbsr_host_validate(const vbsr_host_matrix_view* host);
+
+/* ---- Owning device matrix ----------------------------------------------------------------- */
+
+/* Matrix::Matrix (vbsr.cpp:84-113): validates `host`, then builds the device format on
+ * `device` (-1 = the current device): the reference-layout metadata arrays, per-block and
+ * per-row descriptors used by the kernels, and the values re-laid-out into row panels by an
+ * on-device kernel. Uploads are synchronous; the call returns when the matrix is usable from
+ * any stream. */
+vbsr_status vbsr_matrix_create(const vbsr_host_matrix_view* host, int device, vbsr_matrix** out);
+
+/* Shard constructor for the multi-GPU block-row partition (no reference counterpart; the
+ * reference is single-GPU): holds block rows [row_begin, row_end) of `host` as a matrix with
+ * row_end - row_begin block rows and the full column structure. C for the shard has ld
+ * M_r = row_scalar_off[row_end] - row_scalar_off[row_begin]; B is the full K x N panel. */
+vbsr_status vbsr_matrix_create_rows(const vbsr_host_matrix_view* host, int32_t row_begin,
+                                    int32_t row_end, int device, vbsr_matrix** out);
+
+/* Like vbsr_matrix_create_rows, but `host->values` may be NULL: the values are produced on the
+ * device by the engine's counter-based generator (vbsr_fill_uniform with stream
+ * VBSR_STREAM_VALUES and `seed`), so a matrix of tens of GB needs no host copy. Value v of the
+ * full matrix (packed index v) equals what vbsr_fill_uniform gives for index v. No reference
+ * counterpart. */
+vbsr_status vbsr_matrix_create_rows_generated(const vbsr_host_matrix_view* host, int32_t row_begin,
+                                              int32_t row_end, uint64_t seed, int device,
+                                              vbsr_matrix** out);
+
+vbsr_status vbsr_matrix_destroy(vbsr_matrix* m);
+vbsr_status vbsr_matrix_info_get(const vbsr_matrix* m, vbsr_matrix_info* out);
+vbsr_status vbsr_matrix_device_view(const vbsr_matrix* m, vbsr_device_matrix* out);
+
+/* ---- Plans -------------------------------------------------------------------------------- */
+
+/* Kernel selection (Kernel, vbsr.hpp:91). SPLIT_ROW is rejected with VBSR_INVALID_ARGUMENT,
+ * as plan.cpp:13-17 does. */
+enum { VBSR_KERNEL_AUTO = 0, VBSR_KERNEL_ROW_OWNED = 1, VBSR_KERNEL_SPLIT_ROW = 2 };
+
+/* Plan flags (no reference counterpart). */
+enum {
+  VBSR_PLAN_BOUNDS_CHECK = 1u << 0, /* use the bounds-checked kernel build                  */
+  VBSR_PLAN_NO_SPLIT = 1u << 1      /* never split heavy block rows into column halves      */
+};
+
+/* Plan::Plan (plan.cpp:5-18): rhs must be 8, 16, 32 or 64. The plan schedules the block rows
+ * of `m` once (row-shape classes, heavy-row splitting, static load balance over the SMs) and
+ * uploads that schedule to the matrix's device; the matrix must outlive the plan. */
+vbsr_status vbsr_plan_create(const vbsr_matrix* m, int rhs, int kernel, vbsr_plan** out);
+vbsr_status vbsr_plan_create_ex(const vbsr_matrix* m, int rhs, int kernel, uint32_t flags,
+                                vbsr_plan** out);
+vbsr_status vbsr_plan_destroy(vbsr_plan* p);
+
+/* Plan::execute (plan.cpp:19-22): enqueues C = A * B on `stream` and returns. B is K x rhs and
+ * C is M x rhs, column-major device buffers on the matrix's device. C is fully overwritten
+ * (rows with no blocks become 0). No allocation, no host synchronisation, const on the plan:
+ * concurrent calls from several host threads or streams are safe as long as their C buffers
+ * differ. Launch failures return VBSR_CUDA_ERROR (cudaGetLastError right after the launch). */
+vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr_stream_t stream);
+
+/* Plan::launch_count (plan.cpp:23-31): kernel launches per execute (always 1 here). */
+vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out);
+
+/* Reads and clears the plan's device status word (no reference counterpart): synchronises
+ * `stream`, then returns VBSR_OK, VBSR_TIMEOUT or VBSR_BOUNDS_VIOLATION for the executions
+ * enqueued since the last check. */
+vbsr_status vbsr_plan_check_status(const vbsr_plan* p, vbsr_stream_t stream);
+
+/* Human-readable schedule summary: classes, tasks, split rows, shared memory per CTA. */
+vbsr_status vbsr_plan_describe(const vbsr_plan* p, char* buf, size_t buf_len);
+
+/* Test hook (no reference counterpart): makes the next executions stall one pipeline stage on
+ * purpose (the producer withholds one stage and issues no copy for it) and caps every in-kernel
+ * wait at `wait_limit_cycles` SM clocks, so that the timeout path can be exercised without
+ * hanging the GPU. drop_stage < 0 switches the hook off. */
+vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit_cycles);
+
+/* ---- Raw launchers kept for source compatibility ------------------------------------------ */
+
+/* launch_row_owned (row_owned.cu:397-423): C = A * B from a device view alone (no plan), one
+ * CTA per block row, register-tiled. The unused reference arguments (row_shape_order and the
+ * small/large counts) are accepted and ignored. */
+vbsr_status vbsr_launch_row_owned(const vbsr_device_matrix* a, const int32_t* row_shape_order,
+                                  int small_row_count, int large_row_count, const float* B,
+                                  float* C, int rhs, vbsr_stream_t stream);
+/* launch_row_owned_scalar (row_owned.cu:376-395): one output element per thread. */
+vbsr_status vbsr_launch_row_owned_scalar(const vbsr_device_matrix* a, const float* B, float* C,
+                                         int rhs, vbsr_stream_t stream);
+
+/* ---- Input generation --------------------------------------------------------------------- */
+
+enum {
+  VBSR_DIST_UNIFORM = 0,
+  VBSR_DIST_LOW_VARIANCE = 1,
+  VBSR_DIST_HIGH_VARIANCE = 2,
+  VBSR_DIST_BIMODAL = 3
+};
+
+/* PROFILE_REFERENCE reproduces generate() of the reference bit for bit (generator.cpp:7-88:
+ * its size tables, cyclic +-degree local window, std::mt19937_64 draw order and
+ * std::uniform_real_distribution<float>(-1,1) values). PROFILE_SPEC implements the block-size
+ * distributions and clamped local window of the benchmark specification, draws structure from
+ * std::mt19937_64(seed) and fills values with the counter-based generator, so any slice of the
+ * values can be regenerated independently (in parallel, or on the device). */
+enum { VBSR_PROFILE_REFERENCE = 0, VBSR_PROFILE_SPEC = 1 };
+
+typedef struct vbsr_generator_options {
+  int32_t block_rows, block_cols, degree;
+  int32_t rhs_width;    /* carried for parity with GeneratorOptions; unused */
+  int32_t distribution; /* VBSR_DIST_* */
+  int32_t local_columns;
+  uint64_t seed;
+  int32_t profile;      /* VBSR_PROFILE_* */
+  int32_t with_values;  /* 0: structure only (values empty; PROFILE_SPEC only) */
+  int32_t threads;      /* host threads for value generation (<= 0: all cores) */
+} vbsr_generator_options;
+
+typedef struct vbsr_host_matrix vbsr_host_matrix; /* owning host matrix (HostMatrix) */
+
+/* generate() (generator.cpp:7-88). Invalid dimensions give VBSR_INVALID_ARGUMENT with the
+ * reference's message. */
+vbsr_status vbsr_generate(const vbsr_generator_options* opts, vbsr_host_matrix** out);
+vbsr_status vbsr_host_matrix_view_get(const vbsr_host_matrix* h, vbsr_host_matrix_view* out);
+vbsr_status vbsr_host_matrix_free(vbsr_host_matrix* h);
+
+/* Counter-based U[-1,1) generator: out[i] = f(seed, stream, first + i). Used for PROFILE_SPEC
+ * values (stream VBSR_STREAM_VALUES) and dense panels (VBSR_STREAM_DENSE). Host version; the
+ * device version below gives bit-identical floats. */
+enum { VBSR_STREAM_VALUES = 0xA11CE, VBSR_STREAM_DENSE = 0xB0B };
+vbsr_status vbsr_fill_uniform(uint64_t seed, uint64_t stream, uint64_t first, uint64_t count,
+                              float* out, int threads);
+vbsr_status vbsr_fill_uniform_device(uint64_t seed, uint64_t stream, uint64_t first,
+                                     uint64_t count, float* out_device, vbsr_stream_t cuda_stream);
+
+/* std::mt19937(seed) + std::uniform_real_distribution<float>(-1,1), the dense input the
+ * reference's tests draw (tests/test_main.cpp:42-51). */
+vbsr_status vbsr_fill_mt19937(uint32_t seed, uint64_t count, float* out);
+
+/* ---- Multi-GPU block-row partition -------------------------------------------------------- */
+
+/* Splits the block rows into `parts` contiguous ranges of balanced cost (no reference
+ * counterpart). Cost of a row = 4 * its value count + 4 * rhs * (sum of its block widths), i.e.
+ * the A bytes it streams plus the B bytes it stages. bounds[0..parts] receives the range
+ * boundaries (bounds[0] = 0, bounds[parts] = block_rows). */
+vbsr_status vbsr_partition_rows(const vbsr_host_matrix_view* host, int parts, int rhs,
+                                int32_t* bounds);
+
+/* Byte counts of the benchmark's roofline: the compulsory bytes of the reference VBSR format,
+ * 4*sum(h*w) + 4*nnzb + 8*(nnzb+1) + 4*(R+1) + 4*R + 8*(R+1) + 4*S + 8*(S+1) + 4*K*N + 4*M*N,
+ * and the useful flops 2*sum(h*w)*N, for block rows [row_begin, row_end) (the full column
+ * structure and full B are counted). */
+vbsr_status vbsr_compulsory_bytes(const vbsr_host_matrix_view* host, int32_t row_begin,
+                                  int32_t row_end, int rhs, double* bytes, double* flops);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VBSR_B200_H */

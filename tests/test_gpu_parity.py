@@ -1,0 +1,209 @@
+"""Parity of the engine's CUDA path with the oracle, through the C ABI (Plan.execute).
+
+Bar: every element within |C - C_ref| <= 1e-5 * sum_k |a_ik||b_kj| (C_ref = the reference's
+double-accumulating CPU path, restated bit-exactly by the oracle), plus the reference test
+suite's own acceptance check (finite, max abs error <= 5e-4, relative L2 <= 5e-5).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import varblockspmm_b200 as vb
+from helpers import assert_within_bound, ref_case, reference_test_tolerance, run_plan, spec_case
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLDEN = json.load(open(os.path.join(HERE, "golden", "golden_cases.json")))["cases"]
+
+
+@pytest.mark.parametrize("case", GOLDEN, ids=lambda c: f"s{c['seed']}d{c['degree']}r{c['rhs']}")
+def test_reference_parameter_matrix(cuda, case):
+    """The reference suite's 64-case matrix (tests/test_main.cpp:145-161) and two 256-row cases,
+    on a non-default stream, for the planned kernel and both raw launchers."""
+    torch = cuda
+    host = ref_case(case["rows"], case["cols"], case["degree"], case["distribution"],
+                    case["local"], case["seed"])
+    rhs = case["rhs"]
+    B = vb.fill_mt19937(case["seed"], host.scalar_cols() * rhs)
+    ref = oracle.spmm(host, B, rhs)
+    stream = torch.cuda.Stream()
+    got = run_plan(torch, host, B, rhs, stream=stream)
+    reference_test_tolerance(ref, got)
+    assert_within_bound(host, B, rhs, got)
+
+    m = vb.Matrix(host)
+    dB = torch.from_numpy(B).cuda()
+    for launcher in (vb.launch_row_owned, vb.launch_row_owned_scalar):
+        dC = torch.full((host.scalar_rows() * rhs,), float("nan"), device="cuda")
+        launcher(m.device_view(), dB, dC, rhs, stream)
+        stream.synchronize()
+        out = dC.cpu().numpy()
+        reference_test_tolerance(ref, out)
+        assert_within_bound(host, B, rhs, out)
+
+
+def test_plan_rejects_bad_options(cuda):
+    """tests/test_main.cpp:132-142: RHS 7 and Kernel::SplitRow raise invalid_argument."""
+    m = vb.Matrix(ref_case(4, 4, 2, 2, True, 1))
+    with pytest.raises(vb.InvalidArgument, match="rhs_width must be 8,16,32,64"):
+        vb.Plan(m, vb.PlanOptions(7, vb.Kernel.RowOwned))
+    with pytest.raises(vb.InvalidArgument, match="split-row"):
+        vb.Plan(m, vb.PlanOptions(8, vb.Kernel.SplitRow))
+    p = vb.Plan(m, vb.PlanOptions(8, vb.Kernel.Auto))
+    assert p.launch_count() == 1
+
+
+def test_matrix_rejects_invalid_host(cuda):
+    bad = ref_case(4, 4, 2, 2, True, 1)
+    bad.row_ptr[-1] += 1
+    with pytest.raises(vb.InvalidArgument, match="bad row_ptr"):
+        vb.Matrix(bad)
+
+
+@pytest.mark.parametrize("cfg", [
+    ("C1", 256, 4, 0, True, 8),
+    ("C2", 1024, 16, 3, False, 64),
+    ("C3", 4096, 8, 2, False, 32),
+], ids=lambda c: c[0])
+def test_baseline_configs(cuda, cfg):
+    """BASELINE configs 1-3 at full size (seed 1), spec generator, B from the counter stream."""
+    _, rows, degree, dist, local, rhs = cfg
+    host = spec_case(rows, degree, dist, local, 1)
+    B = vb.fill_uniform(1, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    got = run_plan(cuda, host, B, rhs)
+    ratio = assert_within_bound(host, B, rhs, got)
+    assert ratio < 0.5, ratio  # comfortably inside the bound
+
+
+GRID = [(rhs, dist, deg, local) for rhs in (8, 16, 32, 64) for dist in range(4)
+        for deg in (1, 4, 8, 16) for local in (True, False)]
+
+
+@pytest.mark.parametrize("k", range(0, 128, 1), ids=lambda k: "g%d" % k)
+def test_regime_grid(cuda, k):
+    """the 128-case 1024-row grid, seeds 1..128 in enumeration order."""
+    rhs, dist, deg, local = GRID[k]
+    host = spec_case(1024, deg, dist, local, k + 1)
+    B = vb.fill_uniform(k + 1, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    got = run_plan(cuda, host, B, rhs)
+    assert_within_bound(host, B, rhs, got)
+
+
+@pytest.mark.parametrize("rhs", [8, 16, 32, 64])
+def test_bounds_checked_build_and_no_split(cuda, rhs):
+    host = spec_case(512, 16, 3, False, 77)
+    B = vb.fill_uniform(77, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    a = run_plan(cuda, host, B, rhs)
+    b = run_plan(cuda, host, B, rhs, flags=vb.PLAN_BOUNDS_CHECK)
+    c = run_plan(cuda, host, B, rhs, flags=vb.PLAN_NO_SPLIT)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert_within_bound(host, B, rhs, c)
+
+
+def _handmade(heights, widths, rows_cols, seed=0):
+    """A matrix from explicit per-row block column lists (possibly empty rows)."""
+    rng = np.random.default_rng(seed)
+    R, S = len(heights), len(widths)
+    row_ptr, block_col, value_off = [0], [], [0]
+    for i, cols in enumerate(rows_cols):
+        for c in sorted(cols):
+            block_col.append(c)
+            value_off.append(value_off[-1] + heights[i] * widths[c])
+        row_ptr.append(len(block_col))
+    return vb.HostMatrix(R, S, row_ptr, block_col, heights, widths,
+                         np.concatenate([[0], np.cumsum(heights)]),
+                         np.concatenate([[0], np.cumsum(widths)]), value_off,
+                         rng.uniform(-1, 1, value_off[-1]).astype(np.float32))
+
+
+@pytest.mark.parametrize("rhs", [8, 16, 32, 64])
+def test_edge_shapes(cuda, rhs):
+    """Empty block rows (C must become exactly 0), one-block rows, extreme 8/64 blocks, a row
+    with every column, and a matrix whose first and last rows are empty."""
+    heights = [8, 64, 64, 8, 40, 64, 16]
+    widths = [64, 8, 64, 8, 24, 56, 64, 8, 32]
+    rows_cols = [[], [0], [2], list(range(9)), [], [1, 3, 7], []]
+    host = _handmade(heights, widths, rows_cols, seed=rhs)
+    host.validate()
+    B = np.random.default_rng(1).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
+    got = run_plan(cuda, host, B, rhs)
+    assert_within_bound(host, B, rhs, got)
+    C = got.reshape(rhs, host.scalar_rows())
+    for i in (0, 4, 6):
+        r0, r1 = host.row_scalar_off[i], host.row_scalar_off[i + 1]
+        assert np.all(C[:, r0:r1] == 0)
+
+
+def test_heavy_rows_are_split(cuda):
+    """A few very heavy block rows among light ones: the planner splits them into RHS halves and
+    the result is unchanged."""
+    heights = [64] * 4 + [8] * 400
+    widths = [64] * 64
+    rows_cols = [list(range(64))] * 4 + [[i % 64] for i in range(400)]
+    host = _handmade(heights, widths, rows_cols, seed=3)
+    B = np.random.default_rng(2).uniform(-1, 1, host.scalar_cols() * 64).astype(np.float32)
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(64))
+    assert "split_rows=4" in p.describe(), p.describe()
+    got = run_plan(cuda, host, B, 64, matrix=m, plan=p)
+    assert_within_bound(host, B, 64, got)
+
+
+def test_unaligned_and_offset_buffers(cuda):
+    """B and C inside larger buffers at 16-byte and at 4-byte offsets."""
+    torch = cuda
+    host = spec_case(300, 8, 0, False, 5)
+    rhs = 16
+    B = vb.fill_uniform(5, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    for off in (4, 1):
+        bigB = torch.zeros(B.size + 64, device="cuda")
+        bigB[off:off + B.size] = torch.from_numpy(B).cuda()
+        bigC = torch.full((host.scalar_rows() * rhs + 64,), 7.0, device="cuda")
+        p.execute(bigB[off:].data_ptr(), bigC[off:].data_ptr())
+        torch.cuda.synchronize()
+        out = bigC.cpu().numpy()
+        assert np.all(out[:off] == 7.0) and np.all(out[off + host.scalar_rows() * rhs:] == 7.0)
+        assert_within_bound(host, B, rhs, out[off:off + host.scalar_rows() * rhs])
+
+
+def test_deterministic_and_concurrent_streams(cuda):
+    """Bitwise-identical results across runs, and two plans on two streams at once."""
+    torch = cuda
+    host = spec_case(2048, 8, 2, False, 11)
+    rhs = 32
+    B = torch.from_numpy(vb.fill_uniform(11, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)).cuda()
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    outs = [torch.empty(host.scalar_rows() * rhs, device="cuda") for _ in range(4)]
+    for i, o in enumerate(outs):
+        p.execute(B, o, s1 if i % 2 == 0 else s2)
+    torch.cuda.synchronize()
+    ref = outs[0].cpu().numpy().view(np.uint32)
+    for o in outs[1:]:
+        assert np.array_equal(o.cpu().numpy().view(np.uint32), ref)
+
+
+def test_stalled_pipeline_times_out_and_recovers(cuda):
+    """The producer withholds one stage on purpose; every wait is bounded, so the kernel returns,
+    the plan reports VBSR_TIMEOUT, and the same context keeps working afterwards."""
+    torch = cuda
+    host = spec_case(1024, 8, 2, False, 13)
+    rhs = 32
+    B = vb.fill_uniform(13, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    p.set_debug(drop_stage=3, wait_limit_cycles=2_000_000)  # ~1 ms per wait
+    dB = torch.from_numpy(B).cuda()
+    dC = torch.empty(host.scalar_rows() * rhs, device="cuda")
+    p.execute(dB, dC)
+    with pytest.raises(vb.TimeoutError_):
+        p.check_status()
+    p.set_debug(-1, 0)
+    got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
+    assert_within_bound(host, B, rhs, got)

@@ -1,0 +1,794 @@
+// vbsr_device.cu — device side of the engine: the owning device format (Matrix), the planner
+// (Plan), the execute path and the C-ABI entry points that touch a GPU.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <numeric>
+#include <queue>
+#include <string>
+#include <vector>
+
+#include "vbsr_internal.h"
+#include "vbsr_kernels.cuh"
+#include "vbsr_rng.h"
+#include "vbsr_tiles.h"
+
+namespace vbsr_b200 {
+vbsr_status validate_view(const vbsr_host_matrix_view* v, bool check_values);
+}
+
+using namespace vbsr_b200;
+
+namespace {
+
+// ---- error helpers -------------------------------------------------------------------------------
+
+#define VBSR_CUDA(call)                                                          \
+  do {                                                                           \
+    const cudaError_t e_ = (call);                                               \
+    if (e_ != cudaSuccess) return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e_)); \
+  } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (dev >= 0 && dev != prev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// ---- format kernels ------------------------------------------------------------------------------
+
+// Row of block b (binary search over the matrix-local row_ptr).
+__device__ __forceinline__ int block_row_of(const int32_t* row_ptr, int rows, int b) {
+  int lo = 0, hi = rows;  // row_ptr[lo] <= b < row_ptr[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (row_ptr[mid] <= b) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Re-lays blocks [b_begin, b_end) from the reference layout (column-major h x w, element (r,k) at
+// r + k*h) into row panels (panel r/8 is 8 x w column-major: element (r,k) at
+// (r/8)*8*w + k*8 + r%8). `src` holds values starting at value offset src_base.
+__global__ void relayout_blocks(const int32_t* row_ptr, int rows, const int32_t* row_size,
+                                const int64_t* value_off, const uint32_t* blk, int b_begin,
+                                const float* src, long long src_base, float* dst) {
+  const int b = b_begin + int(blockIdx.x);
+  const int h = row_size[block_row_of(row_ptr, rows, b)];
+  const int w = int((blk[b] & 7u) + 1u) * 8;
+  const long long vo = value_off[b];
+  const float* s = src + (vo - src_base);
+  float* d = dst + vo;
+  for (int i = threadIdx.x; i < h * w; i += blockDim.x) {
+    const int r = i % h, k = i / h;
+    d[(r >> 3) * 8 * w + k * 8 + (r & 7)] = s[i];
+  }
+}
+
+// Fills blocks in the panel layout with the counter-based generator: the element at reference
+// (packed) position global_base + value_off[b] + r + k*h gets rng_uniform(key, that position).
+__global__ void generate_blocks(const int32_t* row_ptr, int rows, const int32_t* row_size,
+                                const int64_t* value_off, const uint32_t* blk, int nnzb,
+                                uint64_t key, long long global_base, float* dst) {
+  for (int b = blockIdx.x; b < nnzb; b += gridDim.x) {
+    const int h = row_size[block_row_of(row_ptr, rows, b)];
+    const int w = int((blk[b] & 7u) + 1u) * 8;
+    const long long vo = value_off[b];
+    for (int i = threadIdx.x; i < h * w; i += blockDim.x) {
+      const int r = i % h, k = i / h;
+      dst[vo + (r >> 3) * 8 * w + k * 8 + (r & 7)] =
+          rng_uniform(key, uint64_t(global_base + vo + i));
+    }
+  }
+}
+
+__global__ void fill_uniform_kernel(uint64_t key, uint64_t first, uint64_t count, float* out) {
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride)
+    out[i] = rng_uniform(key, first + i);
+}
+
+// ---- raw launchers (reference launch_row_owned / launch_row_owned_scalar) --------------------------
+
+__device__ __forceinline__ float panel_value(const float* blockv, int w, int r, int k) {
+  return blockv[(r >> 3) * 8 * w + k * 8 + (r & 7)];
+}
+
+// One output element per thread; grid (block_rows, ceil(64*rhs/256)).
+__global__ void rowwise_scalar_kernel(vbsr_device_matrix a, const float* __restrict__ B,
+                                      float* __restrict__ C, int rhs) {
+  const int row = blockIdx.x;
+  const int h = a.row_size[row];
+  for (int idx = blockIdx.y * blockDim.x + threadIdx.x; idx < h * rhs;
+       idx += blockDim.x * gridDim.y) {
+    const int r = idx % h, n = idx / h;
+    float acc = 0.0f;
+    for (int b = a.row_ptr[row]; b < a.row_ptr[row + 1]; ++b) {
+      const int c = a.block_col[b];
+      const int w = a.col_size[c];
+      const float* av = a.values + a.value_off[b];
+      const float* bv = B + a.col_scalar_off[c] + (long long)n * a.scalar_cols;
+      float part = 0.0f;
+      for (int k = 0; k < w; ++k) part = fmaf(panel_value(av, w, r, k), bv[k], part);
+      acc += part;
+    }
+    C[a.row_scalar_off[row] + r + (long long)n * a.scalar_rows] = acc;
+  }
+}
+
+// One CTA per block row, 256 threads; thread = (local row, group of 8 RHS columns), B read through
+// the read-only cache. Used where no plan exists (a bare device view) and for B/C pointers that
+// are not 16-byte aligned.
+__global__ void rowwise_direct_kernel(vbsr_device_matrix a, const float* __restrict__ B,
+                                      float* __restrict__ C, int rhs) {
+  const int row = blockIdx.x;
+  const int h = a.row_size[row];
+  const int groups = rhs / 8;
+  for (int idx = threadIdx.x; idx < h * groups; idx += blockDim.x) {
+    const int r = idx % h, n0 = (idx / h) * 8;
+    float acc[8] = {};
+    for (int b = a.row_ptr[row]; b < a.row_ptr[row + 1]; ++b) {
+      const int c = a.block_col[b];
+      const int w = a.col_size[c];
+      const float* av = a.values + a.value_off[b];
+      const float* bv = B + a.col_scalar_off[c] + (long long)n0 * a.scalar_cols;
+      float part[8] = {};
+      for (int k = 0; k < w; ++k) {
+        const float x = panel_value(av, w, r, k);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) part[j] = fmaf(x, __ldg(bv + k + (long long)j * a.scalar_cols), part[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += part[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      C[a.row_scalar_off[row] + r + (long long)(n0 + j) * a.scalar_rows] = acc[j];
+  }
+}
+
+bool valid_rhs(int rhs) { return rhs == 8 || rhs == 16 || rhs == 32 || rhs == 64; }
+
+template <class T>
+vbsr_status upload(T** dst, const T* src, size_t n, int64_t* bytes) {
+  *dst = nullptr;
+  if (n == 0) return VBSR_OK;
+  VBSR_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), n * sizeof(T)));
+  *bytes += int64_t(n * sizeof(T));
+  if (src != nullptr) VBSR_CUDA(cudaMemcpy(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice));
+  return VBSR_OK;
+}
+
+void release(MatrixData& d) {
+  cudaFree(d.d_row_ptr);
+  cudaFree(d.d_block_col);
+  cudaFree(d.d_row_size);
+  cudaFree(d.d_col_size);
+  cudaFree(d.d_row_off);
+  cudaFree(d.d_col_off);
+  cudaFree(d.d_value_off);
+  cudaFree(d.d_values);
+  cudaFree(d.d_blk_desc);
+  d.d_row_ptr = d.d_block_col = d.d_row_size = d.d_col_size = nullptr;
+  d.d_row_off = d.d_col_off = d.d_value_off = nullptr;
+  d.d_values = nullptr;
+  d.d_blk_desc = nullptr;
+}
+
+// Builds the device format of block rows [r0, r1). mode 0: values from host; 1: generated.
+vbsr_status build_matrix(const vbsr_host_matrix_view* v, int r0, int r1, int mode, uint64_t seed,
+                         int device, vbsr_matrix** out) {
+  if (out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null output");
+  *out = nullptr;
+  vbsr_status st = validate_view(v, mode == 0);
+  if (st != VBSR_OK) return st;
+  if (r0 < 0 || r1 > v->block_rows || r0 >= r1)
+    return set_error(VBSR_INVALID_ARGUMENT, "bad block-row range");
+  const int64_t K = v->col_scalar_off[v->block_cols];
+  if (K >= (int64_t(1) << 31) - 64)
+    return set_error(VBSR_INVALID_ARGUMENT, "scalar column count exceeds the engine's 2^31 limit");
+  if (v->row_scalar_off[v->block_rows] >= (int64_t(1) << 31))
+    return set_error(VBSR_INVALID_ARGUMENT, "scalar row count exceeds the engine's 2^31 limit");
+
+  auto* m = new (std::nothrow) vbsr_matrix;
+  if (m == nullptr) return set_error(VBSR_OUT_OF_MEMORY, "host allocation failed");
+  MatrixData& d = m->d;
+  int dev = device;
+  if (dev < 0) cudaGetDevice(&dev);
+  DeviceGuard guard(dev);
+  d.device = dev;
+  const int R = r1 - r0, S = v->block_cols;
+  const int b0 = v->row_ptr[r0], b1 = v->row_ptr[r1];
+  const int64_t v0 = v->value_off[b0], v1 = v->value_off[b1];
+  d.block_rows = R;
+  d.block_cols = S;
+  d.row_begin = r0;
+  d.row_end = r1;
+  d.nnzb = b1 - b0;
+  d.M = v->row_scalar_off[r1] - v->row_scalar_off[r0];
+  d.K = K;
+  d.nvalues = v1 - v0;
+
+  try {
+    d.h_row_ptr.resize(size_t(R) + 1);
+    d.h_row_size.assign(v->row_size + r0, v->row_size + r1);
+    d.h_row_off.resize(size_t(R) + 1);
+    d.h_val_off_row.resize(R);
+    d.h_sum_w.resize(R);
+    for (int i = 0; i <= R; ++i) {
+      d.h_row_ptr[i] = v->row_ptr[r0 + i] - b0;
+      d.h_row_off[i] = v->row_scalar_off[r0 + i] - v->row_scalar_off[r0];
+    }
+    std::vector<int64_t> voff(size_t(d.nnzb) + 1);
+    std::vector<uint32_t> desc(d.nnzb);
+    for (int64_t b = 0; b <= d.nnzb; ++b) voff[b] = v->value_off[b0 + b] - v0;
+    for (int64_t b = 0; b < d.nnzb; ++b) {
+      const int c = v->block_col[b0 + b];
+      desc[b] = pack_block(v->col_scalar_off[c], v->col_size[c]);
+    }
+    for (int i = 0; i < R; ++i) {
+      d.h_val_off_row[i] = voff[d.h_row_ptr[i]];
+      int64_t sw = 0;
+      for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) sw += v->col_size[v->block_col[b0 + b]];
+      d.h_sum_w[i] = sw;
+    }
+
+    int64_t bytes = 0;
+#define VBSR_TRY(x)          \
+  do {                       \
+    st = (x);                \
+    if (st != VBSR_OK) {     \
+      release(d);            \
+      delete m;              \
+      return st;             \
+    }                        \
+  } while (0)
+    VBSR_TRY(upload(&d.d_row_ptr, d.h_row_ptr.data(), d.h_row_ptr.size(), &bytes));
+    VBSR_TRY(upload(&d.d_block_col, v->block_col + b0, size_t(d.nnzb), &bytes));
+    VBSR_TRY(upload(&d.d_row_size, d.h_row_size.data(), d.h_row_size.size(), &bytes));
+    VBSR_TRY(upload(&d.d_col_size, v->col_size, size_t(S), &bytes));
+    VBSR_TRY(upload(&d.d_row_off, d.h_row_off.data(), d.h_row_off.size(), &bytes));
+    VBSR_TRY(upload(&d.d_col_off, v->col_scalar_off, size_t(S) + 1, &bytes));
+    VBSR_TRY(upload(&d.d_value_off, voff.data(), voff.size(), &bytes));
+    VBSR_TRY(upload(&d.d_blk_desc, desc.data(), desc.size(), &bytes));
+    VBSR_TRY(upload<float>(&d.d_values, nullptr, size_t(d.nvalues), &bytes));
+
+    if (d.nnzb > 0 && mode == 0) {
+      // Upload in slices of whole blocks through a staging buffer and re-lay each slice.
+      const int64_t slice_cap = std::min<int64_t>(d.nvalues, int64_t(1) << 28);  // 1 GiB
+      float* staging = nullptr;
+      const cudaError_t e = cudaMalloc(&staging, size_t(slice_cap) * sizeof(float));
+      if (e != cudaSuccess) {
+        release(d);
+        delete m;
+        return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e));
+      }
+      int64_t b = 0;
+      while (b < d.nnzb) {
+        int64_t be = b;
+        while (be < d.nnzb && voff[be + 1] - voff[b] <= slice_cap) ++be;
+        const int64_t n = voff[be] - voff[b];
+        cudaError_t e2 = cudaMemcpy(staging, v->values + v0 + voff[b], size_t(n) * sizeof(float),
+                                    cudaMemcpyHostToDevice);
+        if (e2 == cudaSuccess) {
+          relayout_blocks<<<unsigned(be - b), 256>>>(d.d_row_ptr, R, d.d_row_size, d.d_value_off,
+                                                    d.d_blk_desc, int(b), staging, voff[b],
+                                                    d.d_values);
+          e2 = cudaGetLastError();
+        }
+        if (e2 == cudaSuccess) e2 = cudaDeviceSynchronize();
+        if (e2 != cudaSuccess) {
+          cudaFree(staging);
+          release(d);
+          delete m;
+          return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e2));
+        }
+        b = be;
+      }
+      cudaFree(staging);
+    } else if (d.nnzb > 0) {
+      generate_blocks<<<4096, 256>>>(d.d_row_ptr, R, d.d_row_size, d.d_value_off, d.d_blk_desc,
+                                     int(d.nnzb), rng_key(seed, VBSR_STREAM_VALUES), v0,
+                                     d.d_values);
+      cudaError_t e2 = cudaGetLastError();
+      if (e2 == cudaSuccess) e2 = cudaDeviceSynchronize();
+      if (e2 != cudaSuccess) {
+        release(d);
+        delete m;
+        return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e2));
+      }
+    }
+#undef VBSR_TRY
+    d.device_bytes = bytes;
+  } catch (const std::bad_alloc&) {
+    release(d);
+    delete m;
+    return set_error(VBSR_OUT_OF_MEMORY, "host allocation failed");
+  }
+  *out = m;
+  return VBSR_OK;
+}
+
+}  // namespace
+
+// ---- plan ------------------------------------------------------------------------------------------
+
+struct vbsr_plan {
+  const vbsr_matrix* m = nullptr;
+  int rhs = 32;
+  uint32_t flags = 0;
+  int device = 0;
+  int num_tasks = 0;
+  int smem_bytes = 0;
+  Item* d_items = nullptr;
+  Task* d_tasks = nullptr;
+  int* d_status = nullptr;
+  int drop_stage = -1;
+  long long wait_limit = 4000000000ll;  // ~2 s at 1.965 GHz
+  std::string summary;
+};
+
+namespace {
+
+constexpr int kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
+
+// Per-team time model of one item, in warp-issue cycles: FMAs per thread plus a per-chunk and
+// per-item overhead.
+double item_cost(int h, int nw, int64_t sum_w, int nblk) {
+  const TileCfg c = tile_cfg(h, nw);
+  const double chunks = double(sum_w + 31) / 32.0 + nblk;
+  return double(c.tm) * c.tn * double(sum_w) + 48.0 * chunks + 160.0;
+}
+
+template <int RHS>
+cudaError_t set_kernel_attrs() {
+  cudaError_t e = cudaFuncSetAttribute(spmm_kernel<RHS, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(spmm_kernel<RHS, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmemBudget);
+}
+
+vbsr_status build_schedule(vbsr_plan* p) {
+  const MatrixData& d = p->m->d;
+  const int rhs = p->rhs;
+  int num_sm = 148;
+  VBSR_CUDA(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, d.device));
+
+  struct Cand {
+    Item item;
+    double cost;
+    int warps;
+  };
+  std::vector<Cand> items;
+  items.reserve(size_t(d.block_rows) * 2);
+  auto make = [&](int i, int n0, int nw) {
+    Cand c;
+    c.item.val_off = d.h_val_off_row[i];
+    c.item.blk_begin = d.h_row_ptr[i];
+    c.item.nblk = d.h_row_ptr[i + 1] - d.h_row_ptr[i];
+    c.item.c_row = int(d.h_row_off[i]);
+    c.item.h = d.h_row_size[i];
+    c.item.n0 = n0;
+    c.item.nw = nw;
+    c.cost = item_cost(c.item.h, nw, d.h_sum_w[i], c.item.nblk);
+    c.warps = tile_cfg(c.item.h, nw).warps;
+    return c;
+  };
+  double total = 0.0;
+  for (int i = 0; i < d.block_rows; ++i) {
+    items.push_back(make(i, 0, rhs));
+    total += items.back().cost * items.back().warps;
+  }
+  // Heavy rows: split into two RHS-column halves when one item would take more than a quarter of
+  // the ideal per-SM time (the makespan bound a static schedule can reach).
+  int split_rows = 0;
+  if (!(p->flags & VBSR_PLAN_NO_SPLIT) && rhs >= 16) {
+    const double ideal_team = total / (double(num_sm) * kConsumerWarps);
+    std::vector<Cand> out;
+    out.reserve(items.size() + 64);
+    for (const Cand& c : items) {
+      if (c.cost > 0.25 * ideal_team * kConsumerWarps / c.warps && c.item.nblk > 0) {
+        const int i = int(&c - items.data());
+        out.push_back(make(i, 0, rhs / 2));
+        out.push_back(make(i, rhs / 2, rhs / 2));
+        ++split_rows;
+      } else {
+        out.push_back(c);
+      }
+    }
+    items.swap(out);
+  }
+
+  // Classes by team size; SMs shared out in proportion to each class's warp-time.
+  const int class_warps[3] = {1, 2, 4};
+  double class_work[3] = {0, 0, 0};
+  std::vector<int> class_items[3];
+  for (size_t k = 0; k < items.size(); ++k) {
+    const int cls = items[k].warps == 1 ? 0 : items[k].warps == 2 ? 1 : 2;
+    class_items[cls].push_back(int(k));
+    class_work[cls] += items[k].cost * items[k].warps;
+  }
+  double work_sum = class_work[0] + class_work[1] + class_work[2];
+  int ctas[3] = {0, 0, 0};
+  int nonempty = 0;
+  for (int c = 0; c < 3; ++c) nonempty += class_items[c].empty() ? 0 : 1;
+  const int sm_budget = std::max(num_sm, nonempty);
+  int assigned = 0;
+  double rem[3] = {0, 0, 0};
+  for (int c = 0; c < 3; ++c) {
+    if (class_items[c].empty()) continue;
+    const double share = work_sum > 0 ? sm_budget * class_work[c] / work_sum : 1.0;
+    const int nt = kConsumerWarps / class_warps[c];
+    // never more CTAs than the class has items to give one per team
+    const int cap = int((class_items[c].size() + nt - 1) / nt);
+    ctas[c] = std::max(1, std::min(cap, int(share)));
+    rem[c] = share - int(share);
+    assigned += ctas[c];
+  }
+  while (assigned < sm_budget) {
+    int best = -1;
+    for (int c = 0; c < 3; ++c) {
+      if (class_items[c].empty()) continue;
+      const int nt = kConsumerWarps / class_warps[c];
+      const int cap = int((class_items[c].size() + nt - 1) / nt);
+      if (ctas[c] >= cap) continue;
+      if (best < 0 || rem[c] > rem[best]) best = c;
+    }
+    if (best < 0) break;
+    ++ctas[best];
+    rem[best] -= 1.0;
+    ++assigned;
+  }
+  while (assigned > sm_budget) {  // only when rounding up the minimum of 1 overshot
+    int best = -1;
+    for (int c = 0; c < 3; ++c)
+      if (ctas[c] > 1 && (best < 0 || rem[c] < rem[best])) best = c;
+    if (best < 0) break;
+    --ctas[best];
+    rem[best] += 1.0;
+    --assigned;
+  }
+
+  std::vector<Item> h_items;
+  std::vector<Task> h_tasks;
+  h_items.reserve(items.size());
+  int max_smem = 0;
+  for (int c = 0; c < 3; ++c) {
+    if (class_items[c].empty()) continue;
+    const int tw = class_warps[c];
+    const int nt = kConsumerWarps / tw;
+    const int workers = ctas[c] * nt;
+    std::vector<int>& idx = class_items[c];
+    std::stable_sort(idx.begin(), idx.end(),
+                     [&](int a, int b) { return items[a].cost > items[b].cost; });
+    // LPT: each item goes to the least-loaded worker.
+    using Load = std::pair<double, int>;
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int w = 0; w < workers; ++w) heap.push({0.0, w});
+    std::vector<std::vector<int>> lists(workers);
+    for (int k : idx) {
+      Load l = heap.top();
+      heap.pop();
+      lists[l.second].push_back(k);
+      l.first += items[k].cost;
+      heap.push(l);
+    }
+    for (int t = 0; t < ctas[c]; ++t) {
+      Task task{};
+      int sf = 32;
+      for (int j = 0; j < nt; ++j) {
+        task.team_off[j] = int(h_items.size());
+        // rows in ascending order inside a team: neighbouring rows share nothing in general,
+        // but ascending order keeps C writes and descriptor reads sequential.
+        std::vector<int>& l = lists[t * nt + j];
+        std::sort(l.begin(), l.end());
+        for (int k : l) {
+          h_items.push_back(items[k].item);
+          sf = std::max(sf, stage_floats(items[k].item.h, items[k].item.nw));
+        }
+      }
+      for (int j = nt; j <= kConsumerWarps; ++j) task.team_off[j] = int(h_items.size());
+      task.team_warps = tw;
+      task.stage_floats = sf;
+      const int stages = std::min(kMaxStages, kSmemBudget / (nt * sf * 4));
+      if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
+      task.stages = stages;
+      max_smem = std::max(max_smem, nt * stages * sf * 4);
+      h_tasks.push_back(task);
+    }
+  }
+  // At least ~116 KB so that one CTA occupies one SM (the schedule is static per CTA).
+  p->smem_bytes = std::max(max_smem, 116 * 1024);
+  p->num_tasks = int(h_tasks.size());
+
+  char buf[512];
+  std::snprintf(buf, sizeof buf,
+                "rhs=%d items=%zu split_rows=%d tasks=%d (tw1=%d tw2=%d tw4=%d) smem=%d sms=%d",
+                rhs, h_items.size(), split_rows, p->num_tasks, ctas[0], ctas[1], ctas[2],
+                p->smem_bytes, num_sm);
+  p->summary = buf;
+
+  DeviceGuard guard(d.device);
+  VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, h_items.size()) * sizeof(Item)));
+  VBSR_CUDA(cudaMalloc(&p->d_tasks, std::max<size_t>(1, h_tasks.size()) * sizeof(Task)));
+  VBSR_CUDA(cudaMalloc(&p->d_status, kStatusWords * sizeof(int)));
+  if (!h_items.empty())
+    VBSR_CUDA(cudaMemcpy(p->d_items, h_items.data(), h_items.size() * sizeof(Item),
+                         cudaMemcpyHostToDevice));
+  if (!h_tasks.empty())
+    VBSR_CUDA(cudaMemcpy(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
+                         cudaMemcpyHostToDevice));
+  VBSR_CUDA(cudaMemset(p->d_status, 0, kStatusWords * sizeof(int)));
+  switch (rhs) {
+    case 8: VBSR_CUDA(set_kernel_attrs<8>()); break;
+    case 16: VBSR_CUDA(set_kernel_attrs<16>()); break;
+    case 32: VBSR_CUDA(set_kernel_attrs<32>()); break;
+    case 64: VBSR_CUDA(set_kernel_attrs<64>()); break;
+  }
+  return VBSR_OK;
+}
+
+void free_plan(vbsr_plan* p) {
+  if (p == nullptr) return;
+  DeviceGuard guard(p->device);
+  cudaFree(p->d_items);
+  cudaFree(p->d_tasks);
+  cudaFree(p->d_status);
+  delete p;
+}
+
+template <int RHS>
+void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
+  if (p->flags & VBSR_PLAN_BOUNDS_CHECK)
+    spmm_kernel<RHS, true><<<p->num_tasks, kThreads, p->smem_bytes, stream>>>(kp);
+  else
+    spmm_kernel<RHS, false><<<p->num_tasks, kThreads, p->smem_bytes, stream>>>(kp);
+}
+
+vbsr_status launch_view_kernel(const vbsr_device_matrix* a, const float* B, float* C, int rhs,
+                               cudaStream_t stream, bool scalar) {
+  if (a == nullptr || (a->block_rows > 0 && (B == nullptr || C == nullptr)))
+    return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  if (!valid_rhs(rhs)) return set_error(VBSR_INVALID_ARGUMENT, "unsupported rhs width");
+  if (a->block_rows == 0) return VBSR_OK;
+  if (scalar) {
+    const int per_row = (64 * rhs + 255) / 256;
+    rowwise_scalar_kernel<<<dim3(a->block_rows, per_row), 256, 0, stream>>>(*a, B, C, rhs);
+  } else {
+    rowwise_direct_kernel<<<a->block_rows, 256, 0, stream>>>(*a, B, C, rhs);
+  }
+  VBSR_CUDA(cudaGetLastError());
+  return VBSR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+vbsr_status vbsr_matrix_create(const vbsr_host_matrix_view* host, int device, vbsr_matrix** out) {
+  clear_error();
+  if (host == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null matrix view");
+  return build_matrix(host, 0, host->block_rows, 0, 0, device, out);
+}
+
+vbsr_status vbsr_matrix_create_rows(const vbsr_host_matrix_view* host, int32_t row_begin,
+                                    int32_t row_end, int device, vbsr_matrix** out) {
+  clear_error();
+  return build_matrix(host, row_begin, row_end, 0, 0, device, out);
+}
+
+vbsr_status vbsr_matrix_create_rows_generated(const vbsr_host_matrix_view* host, int32_t row_begin,
+                                              int32_t row_end, uint64_t seed, int device,
+                                              vbsr_matrix** out) {
+  clear_error();
+  return build_matrix(host, row_begin, row_end, 1, seed, device, out);
+}
+
+vbsr_status vbsr_matrix_destroy(vbsr_matrix* m) {
+  clear_error();
+  if (m == nullptr) return VBSR_OK;
+  {
+    DeviceGuard guard(m->d.device);
+    release(m->d);
+  }
+  delete m;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_matrix_info_get(const vbsr_matrix* m, vbsr_matrix_info* o) {
+  clear_error();
+  if (m == nullptr || o == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  const MatrixData& d = m->d;
+  o->block_rows = d.block_rows;
+  o->block_cols = d.block_cols;
+  o->nnzb = d.nnzb;
+  o->scalar_rows = d.M;
+  o->scalar_cols = d.K;
+  o->value_count = d.nvalues;
+  o->device_bytes = d.device_bytes;
+  o->device = d.device;
+  o->row_begin = d.row_begin;
+  o->row_end = d.row_end;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_matrix_device_view(const vbsr_matrix* m, vbsr_device_matrix* o) {
+  clear_error();
+  if (m == nullptr || o == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  const MatrixData& d = m->d;
+  o->block_rows = d.block_rows;
+  o->block_cols = d.block_cols;
+  o->nnzb = int32_t(d.nnzb);
+  o->scalar_rows = d.M;
+  o->scalar_cols = d.K;
+  o->row_ptr = d.d_row_ptr;
+  o->block_col = d.d_block_col;
+  o->row_size = d.d_row_size;
+  o->col_size = d.d_col_size;
+  o->row_scalar_off = d.d_row_off;
+  o->col_scalar_off = d.d_col_off;
+  o->value_off = d.d_value_off;
+  o->values = d.d_values;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_create_ex(const vbsr_matrix* m, int rhs, int kernel, uint32_t flags,
+                                vbsr_plan** out) {
+  clear_error();
+  if (m == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  // plan.cpp:9-17
+  if (!valid_rhs(rhs)) return set_error(VBSR_INVALID_ARGUMENT, "rhs_width must be 8,16,32,64");
+  if (kernel == VBSR_KERNEL_SPLIT_ROW)
+    return set_error(VBSR_INVALID_ARGUMENT,
+                     "split-row was not justified by the 1.0 regime map; use RowOwned or "
+                     "GroupedGemmPlan");
+  if (kernel != VBSR_KERNEL_AUTO && kernel != VBSR_KERNEL_ROW_OWNED)
+    return set_error(VBSR_INVALID_ARGUMENT, "unknown kernel");
+  auto* p = new (std::nothrow) vbsr_plan;
+  if (p == nullptr) return set_error(VBSR_OUT_OF_MEMORY, "host allocation failed");
+  p->m = m;
+  p->rhs = rhs;
+  p->flags = flags;
+  p->device = m->d.device;
+  vbsr_status st;
+  try {
+    st = build_schedule(p);
+  } catch (const std::bad_alloc&) {
+    st = set_error(VBSR_OUT_OF_MEMORY, "host allocation failed");
+  }
+  if (st != VBSR_OK) {
+    free_plan(p);
+    return st;
+  }
+  *out = p;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_create(const vbsr_matrix* m, int rhs, int kernel, vbsr_plan** out) {
+  return vbsr_plan_create_ex(m, rhs, kernel, 0u, out);
+}
+
+vbsr_status vbsr_plan_destroy(vbsr_plan* p) {
+  clear_error();
+  free_plan(p);
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr_stream_t stream) {
+  clear_error();
+  if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
+  if (B == nullptr || C == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null B or C");
+  const MatrixData& d = p->m->d;
+  DeviceGuard guard(p->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if ((reinterpret_cast<uintptr_t>(B) & 15u) || (reinterpret_cast<uintptr_t>(C) & 15u)) {
+    // TMA bulk copies and 16-byte stores need 16-byte aligned panels; unaligned caller buffers
+    // take the plain-load row kernel instead.
+    vbsr_device_matrix view;
+    vbsr_matrix_device_view(p->m, &view);
+    return launch_view_kernel(&view, B, C, p->rhs, s, false);
+  }
+  if (p->num_tasks == 0) return VBSR_OK;
+  KernelParams kp;
+  kp.items = p->d_items;
+  kp.tasks = p->d_tasks;
+  kp.blk = d.d_blk_desc;
+  kp.values = d.d_values;
+  kp.B = B;
+  kp.C = C;
+  kp.M = d.M;
+  kp.K = d.K;
+  kp.nvalues = d.nvalues;
+  kp.rhs = p->rhs;
+  kp.status = p->d_status;
+  kp.drop_stage = p->drop_stage;
+  kp.wait_limit = p->wait_limit;
+  switch (p->rhs) {
+    case 8: launch_spmm<8>(p, kp, s); break;
+    case 16: launch_spmm<16>(p, kp, s); break;
+    case 32: launch_spmm<32>(p, kp, s); break;
+    case 64: launch_spmm<64>(p, kp, s); break;
+  }
+  VBSR_CUDA(cudaGetLastError());
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out) {
+  clear_error();
+  if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  *out = 1;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_check_status(const vbsr_plan* p, vbsr_stream_t stream) {
+  clear_error();
+  if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
+  DeviceGuard guard(p->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int words[kStatusWords] = {0, 0, 0, 0};
+  VBSR_CUDA(cudaMemcpyAsync(words, p->d_status, sizeof words, cudaMemcpyDeviceToHost, s));
+  VBSR_CUDA(cudaMemsetAsync(p->d_status, 0, sizeof words, s));
+  VBSR_CUDA(cudaStreamSynchronize(s));
+  if (words[kStatusCode] == VBSR_TIMEOUT)
+    return set_error(VBSR_TIMEOUT, "pipeline wait timed out in CTA " + std::to_string(words[kStatusInfo]));
+  if (words[kStatusCode] == VBSR_BOUNDS_VIOLATION)
+    return set_error(VBSR_BOUNDS_VIOLATION, "index out of bounds in work item " + std::to_string(words[kStatusInfo]));
+  if (words[kStatusCode] != 0) return set_error(VBSR_CUDA_ERROR, "unknown device status");
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_describe(const vbsr_plan* p, char* buf, size_t len) {
+  clear_error();
+  if (p == nullptr || buf == nullptr || len == 0) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  std::snprintf(buf, len, "%s", p->summary.c_str());
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit_cycles) {
+  clear_error();
+  if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
+  p->drop_stage = drop_stage < 0 ? -1 : drop_stage;
+  p->wait_limit = wait_limit_cycles > 0 ? wait_limit_cycles : 4000000000ll;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_launch_row_owned(const vbsr_device_matrix* a, const int32_t* row_shape_order,
+                                  int small_row_count, int large_row_count, const float* B,
+                                  float* C, int rhs, vbsr_stream_t stream) {
+  clear_error();
+  (void)row_shape_order;
+  (void)small_row_count;
+  (void)large_row_count;
+  return launch_view_kernel(a, B, C, rhs, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+vbsr_status vbsr_launch_row_owned_scalar(const vbsr_device_matrix* a, const float* B, float* C,
+                                         int rhs, vbsr_stream_t stream) {
+  clear_error();
+  return launch_view_kernel(a, B, C, rhs, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+vbsr_status vbsr_fill_uniform_device(uint64_t seed, uint64_t stream, uint64_t first,
+                                     uint64_t count, float* out, vbsr_stream_t cuda_stream) {
+  clear_error();
+  if (count == 0) return VBSR_OK;
+  if (out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null output");
+  const uint64_t blocks = std::min<uint64_t>((count + 255) / 256, 65536);
+  fill_uniform_kernel<<<unsigned(blocks), 256, 0, reinterpret_cast<cudaStream_t>(cuda_stream)>>>(
+      rng_key(seed, stream), first, count, out);
+  VBSR_CUDA(cudaGetLastError());
+  return VBSR_OK;
+}
+
+}  // extern "C"
