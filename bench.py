@@ -248,6 +248,17 @@ def sampled_parity(host, rhs, row_range, dC, B_host, n_rows=12):
     return worst, bad
 
 
+def cta_time_stats(plan, B, C, stream):
+    """One extra execution with per-CTA timing: spread of CTA durations (load-balance check)."""
+    plan.enable_cta_timing(True)
+    plan.execute(B, C, stream)
+    t = plan.cta_timing(stream).astype(np.int64)
+    plan.enable_cta_timing(False)
+    dur = (t[:, 1] - t[:, 0]) / 1e3
+    return {"ctas": int(t.shape[0]), "min_us": float(dur.min()), "median_us": float(np.median(dur)),
+            "max_us": float(dur.max()), "span_us": float((t[:, 1].max() - t[:, 0].min()) / 1e3)}
+
+
 def time_headline(vb, torch, stream, peak, steps=200, warmup=10):
     """BASELINE config 3 on this GPU: per-launch device time with L2 flushed between launches."""
     host, rhs = make_structure("headline")
@@ -278,7 +289,8 @@ def time_headline(vb, torch, stream, peak, steps=200, warmup=10):
     return {"workload": WORKLOADS["headline"][5], "median_ms": med, "p95_ms": p95,
             "GBps": gbs, "frac_of_measured_hbm": gbs / peak, "compulsory_bytes": problem_bytes,
             "useful_TFLOPs": flops / (med * 1e-3) / 1e12, "l2": "flushed before every launch",
-            "plan": p.describe(), "parity_max_ratio": ratio, "parity_violations": bad}
+            "plan": p.describe(), "parity_max_ratio": ratio, "parity_violations": bad,
+            "cta_time": cta_time_stats(p, B, Cd, stream)}
 
 
 def run_gpu_arm(args):
@@ -360,6 +372,8 @@ def run_gpu_arm(args):
     total_ms, med_max, p95_max, _ = stats.tolist()
     ms_per_step = total_ms / args.steps if flush is None else med_max
 
+    cta_stats = cta_time_stats(plan, dB, dC, stream)
+
     # ---- end to end through the public API with host buffers ---------------------------------
     B_host = vb.fill_uniform(SEED, vb.STREAM_DENSE, 0, K * rhs)
     hB = torch.from_numpy(B_host).pin_memory()
@@ -425,7 +439,7 @@ def run_gpu_arm(args):
             "clocks": clocks.summary(),
             "parity": {"sampled_rows_max_err_over_bound": pr[0].item(),
                        "violations": int(pr[1].item())},
-            "setup_s": setup_s, "replicate_ms": replicate_ms,
+            "setup_s": setup_s, "replicate_ms": replicate_ms, "cta_time": cta_stats,
         }
         if headline:
             line["headline"] = headline

@@ -181,6 +181,15 @@ vbsr_status vbsr_plan_describe(const vbsr_plan* p, char* buf, size_t buf_len);
  * hanging the GPU. drop_stage < 0 switches the hook off. */
 vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit_cycles);
 
+/* Per-CTA timing (no reference counterpart; a tuning aid): enable != 0 makes the following
+ * executions record, for every CTA, its start and end on the GPU's global nanosecond timer.
+ * If `out` is not NULL, synchronises `stream` and copies up to out_len values (start, end pairs in
+ * CTA order) from the last timed execution. */
+vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int out_len,
+                                 vbsr_stream_t stream);
+/* Number of CTAs (tasks) one execution launches. */
+vbsr_status vbsr_plan_num_tasks(const vbsr_plan* p, int* out);
+
 /* ---- Raw launchers kept for source compatibility ------------------------------------------ */
 
 /* launch_row_owned (row_owned.cu:397-423): C = A * B from a device view alone (no plan), one

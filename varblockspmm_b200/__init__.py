@@ -26,7 +26,7 @@ LIB_PATH = os.path.join(_HERE, "libvbsr_b200.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
-        "libvbsr_b200.so is not built; run `python -m varblockspmm_b200.build` "
+        "libvbsr_b200.so is not built; run `python varblockspmm_b200/build.py` "
         "(or __graft_entry__.build()) first")
 _lib = C.CDLL(LIB_PATH)
 
@@ -138,6 +138,8 @@ _sig = {
     "vbsr_plan_check_status": [_vp, _vp],
     "vbsr_plan_describe": [_vp, C.c_char_p, C.c_size_t],
     "vbsr_plan_set_debug": [_vp, C.c_int, C.c_int64],
+    "vbsr_plan_cta_timing": [_vp, C.c_int, C.POINTER(C.c_uint64), C.c_int, _vp],
+    "vbsr_plan_num_tasks": [_vp, C.POINTER(C.c_int)],
     "vbsr_launch_row_owned": [C.POINTER(DeviceMatrix), _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp],
     "vbsr_launch_row_owned_scalar": [C.POINTER(DeviceMatrix), _vp, _vp, C.c_int, _vp],
     "vbsr_generate": [C.POINTER(GenOpts), C.POINTER(_vp)],
@@ -457,6 +459,22 @@ class Plan:
 
     def set_debug(self, drop_stage: int = -1, wait_limit_cycles: int = 0):
         _check(_lib.vbsr_plan_set_debug(self._h, drop_stage, wait_limit_cycles))
+
+    def num_tasks(self) -> int:
+        n = C.c_int()
+        _check(_lib.vbsr_plan_num_tasks(self._h, C.byref(n)))
+        return n.value
+
+    def enable_cta_timing(self, enable: bool = True):
+        _check(_lib.vbsr_plan_cta_timing(self._h, int(enable), None, 0, None))
+
+    def cta_timing(self, stream=None) -> np.ndarray:
+        """(start, end) global-timer ns per CTA of the last timed execution, shape (tasks, 2)."""
+        n = self.num_tasks()
+        out = np.zeros(2 * n, dtype=np.uint64)
+        _check(_lib.vbsr_plan_cta_timing(self._h, 1, out.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                         2 * n, _stream_ptr(stream)))
+        return out.reshape(n, 2)
 
     def close(self):
         if self._h:

@@ -1,6 +1,7 @@
 """Builds the engine's shared library in-tree: varblockspmm_b200/libvbsr_b200.so (sm_100a).
 
-Run `python -m varblockspmm_b200.build` or call build(). nvcc cross-compiles for sm_100a, so this
+Run `python varblockspmm_b200/build.py` or call build() (__graft_entry__.build() does both this
+and the oracle). nvcc cross-compiles for sm_100a, so this
 works on a machine without a GPU.
 """
 from __future__ import annotations

@@ -229,7 +229,8 @@ vbsr_status build_matrix(const vbsr_host_matrix_view* v, int r0, int r1, int mod
       d.h_row_off[i] = v->row_scalar_off[r0 + i] - v->row_scalar_off[r0];
     }
     std::vector<int64_t> voff(size_t(d.nnzb) + 1);
-    std::vector<uint32_t> desc(d.nnzb);
+    std::vector<uint32_t>& desc = d.h_blk_desc;
+    desc.resize(d.nnzb);
     for (int64_t b = 0; b <= d.nnzb; ++b) voff[b] = v->value_off[b0 + b] - v0;
     for (int64_t b = 0; b < d.nnzb; ++b) {
       const int c = v->block_col[b0 + b];
@@ -329,9 +330,12 @@ struct vbsr_plan {
   int device = 0;
   int num_tasks = 0;
   int smem_bytes = 0;
-  Item* d_items = nullptr;
+  int64_t stream_entries = 0;
+  unsigned long long* d_stream = nullptr;
   Task* d_tasks = nullptr;
   int* d_status = nullptr;
+  unsigned long long* d_timing = nullptr;  // allocated on first request
+  bool timing_on = false;
   int drop_stage = -1;
   long long wait_limit = 4000000000ll;  // ~2 s at 1.965 GHz
   std::string summary;
@@ -343,10 +347,9 @@ constexpr int kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
 
 // Per-team time model of one item, in warp-issue cycles: FMAs per thread plus a per-chunk and
 // per-item overhead.
-double item_cost(int h, int nw, int64_t sum_w, int nblk) {
+double item_cost(int h, int nw, int64_t sum_w, int nchunks) {
   const TileCfg c = tile_cfg(h, nw);
-  const double chunks = double(sum_w + 31) / 32.0 + nblk;
-  return double(c.tm) * c.tn * double(sum_w) + 48.0 * chunks + 160.0;
+  return double(c.tm) * c.tn * double(sum_w) + 160.0 * nchunks + 400.0;
 }
 
 template <int RHS>
@@ -363,25 +366,32 @@ vbsr_status build_schedule(vbsr_plan* p) {
   const int rhs = p->rhs;
   int num_sm = 148;
   VBSR_CUDA(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, d.device));
+  if (d.nvalues >= entry::kMaxVal || d.K >= entry::kMaxCol || d.M >= (int64_t(1) << 31))
+    return set_error(VBSR_INVALID_ARGUMENT, "matrix exceeds the schedule's index range");
 
   struct Cand {
-    Item item;
+    int row, n0, nw, warps, chunks;
     double cost;
-    int warps;
   };
+  std::vector<int> row_chunks(d.block_rows);
+  for (int i = 0; i < d.block_rows; ++i) {
+    int c = 0;
+    for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
+      const int w = int((d.h_blk_desc[b] & 7u) + 1u) * 8;
+      c += (w + kChunk - 1) / kChunk;
+    }
+    row_chunks[i] = c;
+  }
   std::vector<Cand> items;
   items.reserve(size_t(d.block_rows) * 2);
   auto make = [&](int i, int n0, int nw) {
     Cand c;
-    c.item.val_off = d.h_val_off_row[i];
-    c.item.blk_begin = d.h_row_ptr[i];
-    c.item.nblk = d.h_row_ptr[i + 1] - d.h_row_ptr[i];
-    c.item.c_row = int(d.h_row_off[i]);
-    c.item.h = d.h_row_size[i];
-    c.item.n0 = n0;
-    c.item.nw = nw;
-    c.cost = item_cost(c.item.h, nw, d.h_sum_w[i], c.item.nblk);
-    c.warps = tile_cfg(c.item.h, nw).warps;
+    c.row = i;
+    c.n0 = n0;
+    c.nw = nw;
+    c.warps = tile_cfg(d.h_row_size[i], nw).warps;
+    c.chunks = row_chunks[i];
+    c.cost = item_cost(d.h_row_size[i], nw, d.h_sum_w[i], c.chunks);
     return c;
   };
   double total = 0.0;
@@ -390,17 +400,16 @@ vbsr_status build_schedule(vbsr_plan* p) {
     total += items.back().cost * items.back().warps;
   }
   // Heavy rows: split into two RHS-column halves when one item would take more than a quarter of
-  // the ideal per-SM time (the makespan bound a static schedule can reach).
+  // the ideal per-team time (the makespan bound a static schedule can reach).
   int split_rows = 0;
   if (!(p->flags & VBSR_PLAN_NO_SPLIT) && rhs >= 16) {
     const double ideal_team = total / (double(num_sm) * kConsumerWarps);
     std::vector<Cand> out;
     out.reserve(items.size() + 64);
     for (const Cand& c : items) {
-      if (c.cost > 0.25 * ideal_team * kConsumerWarps / c.warps && c.item.nblk > 0) {
-        const int i = int(&c - items.data());
-        out.push_back(make(i, 0, rhs / 2));
-        out.push_back(make(i, rhs / 2, rhs / 2));
+      if (c.cost > 0.25 * ideal_team * kConsumerWarps / c.warps && c.chunks > 0) {
+        out.push_back(make(c.row, 0, rhs / 2));
+        out.push_back(make(c.row, rhs / 2, rhs / 2));
         ++split_rows;
       } else {
         out.push_back(c);
@@ -418,30 +427,28 @@ vbsr_status build_schedule(vbsr_plan* p) {
     class_items[cls].push_back(int(k));
     class_work[cls] += items[k].cost * items[k].warps;
   }
-  double work_sum = class_work[0] + class_work[1] + class_work[2];
+  const double work_sum = class_work[0] + class_work[1] + class_work[2];
   int ctas[3] = {0, 0, 0};
   int nonempty = 0;
   for (int c = 0; c < 3; ++c) nonempty += class_items[c].empty() ? 0 : 1;
   const int sm_budget = std::max(num_sm, nonempty);
   int assigned = 0;
   double rem[3] = {0, 0, 0};
+  auto cap_of = [&](int c) {
+    const int nt = kConsumerWarps / class_warps[c];
+    return int((class_items[c].size() + nt - 1) / nt);
+  };
   for (int c = 0; c < 3; ++c) {
     if (class_items[c].empty()) continue;
     const double share = work_sum > 0 ? sm_budget * class_work[c] / work_sum : 1.0;
-    const int nt = kConsumerWarps / class_warps[c];
-    // never more CTAs than the class has items to give one per team
-    const int cap = int((class_items[c].size() + nt - 1) / nt);
-    ctas[c] = std::max(1, std::min(cap, int(share)));
-    rem[c] = share - int(share);
+    ctas[c] = std::max(1, std::min(cap_of(c), int(share)));
+    rem[c] = share - ctas[c];
     assigned += ctas[c];
   }
   while (assigned < sm_budget) {
     int best = -1;
     for (int c = 0; c < 3; ++c) {
-      if (class_items[c].empty()) continue;
-      const int nt = kConsumerWarps / class_warps[c];
-      const int cap = int((class_items[c].size() + nt - 1) / nt);
-      if (ctas[c] >= cap) continue;
+      if (class_items[c].empty() || ctas[c] >= cap_of(c)) continue;
       if (best < 0 || rem[c] > rem[best]) best = c;
     }
     if (best < 0) break;
@@ -449,7 +456,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
     rem[best] -= 1.0;
     ++assigned;
   }
-  while (assigned > sm_budget) {  // only when rounding up the minimum of 1 overshot
+  while (assigned > sm_budget) {  // only when the minimum of one CTA per class overshot
     int best = -1;
     for (int c = 0; c < 3; ++c)
       if (ctas[c] > 1 && (best < 0 || rem[c] < rem[best])) best = c;
@@ -459,9 +466,10 @@ vbsr_status build_schedule(vbsr_plan* p) {
     --assigned;
   }
 
-  std::vector<Item> h_items;
+  // Per-row first block's value offset and block list; emit each team's stream.
+  std::vector<unsigned long long> stream;
+  stream.reserve(items.size() + size_t(d.nnzb) * 2);
   std::vector<Task> h_tasks;
-  h_items.reserve(items.size());
   int max_smem = 0;
   for (int c = 0; c < 3; ++c) {
     if (class_items[c].empty()) continue;
@@ -471,7 +479,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
     std::vector<int>& idx = class_items[c];
     std::stable_sort(idx.begin(), idx.end(),
                      [&](int a, int b) { return items[a].cost > items[b].cost; });
-    // LPT: each item goes to the least-loaded worker.
+    // LPT: each item goes to the least-loaded team.
     using Load = std::pair<double, int>;
     std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
     for (int w = 0; w < workers; ++w) heap.push({0.0, w});
@@ -487,17 +495,31 @@ vbsr_status build_schedule(vbsr_plan* p) {
       Task task{};
       int sf = 32;
       for (int j = 0; j < nt; ++j) {
-        task.team_off[j] = int(h_items.size());
-        // rows in ascending order inside a team: neighbouring rows share nothing in general,
-        // but ascending order keeps C writes and descriptor reads sequential.
+        task.team_off[j] = int(stream.size());
         std::vector<int>& l = lists[t * nt + j];
-        std::sort(l.begin(), l.end());
+        std::sort(l.begin(), l.end(), [&](int a, int b) {
+          return items[a].row != items[b].row ? items[a].row < items[b].row
+                                              : items[a].n0 < items[b].n0;
+        });
         for (int k : l) {
-          h_items.push_back(items[k].item);
-          sf = std::max(sf, stage_floats(items[k].item.h, items[k].item.nw));
+          const Cand& it = items[k];
+          const int i = it.row, h = d.h_row_size[i];
+          stream.push_back(entry::header(d.h_row_off[i], h, it.n0, it.nw));
+          int64_t val = d.h_val_off_row[i];
+          for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
+            const uint32_t desc = d.h_blk_desc[b];
+            const int w = int((desc & 7u) + 1u) * 8;
+            const int64_t col = int64_t(desc & ~7u);
+            for (int k0 = 0; k0 < w; k0 += kChunk) {
+              const int kc = std::min(kChunk, w - k0);
+              stream.push_back(entry::chunk(val, col, w, k0, kc, k0 + kc == w));
+            }
+            val += int64_t(h) * w;
+          }
+          sf = std::max(sf, stage_floats(h, it.nw));
         }
       }
-      for (int j = nt; j <= kConsumerWarps; ++j) task.team_off[j] = int(h_items.size());
+      for (int j = nt; j <= kConsumerWarps; ++j) task.team_off[j] = int(stream.size());
       task.team_warps = tw;
       task.stage_floats = sf;
       const int stages = std::min(kMaxStages, kSmemBudget / (nt * sf * 4));
@@ -507,23 +529,27 @@ vbsr_status build_schedule(vbsr_plan* p) {
       h_tasks.push_back(task);
     }
   }
+  if (stream.size() >= (size_t(1) << 31))
+    return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
   // At least ~116 KB so that one CTA occupies one SM (the schedule is static per CTA).
   p->smem_bytes = std::max(max_smem, 116 * 1024);
   p->num_tasks = int(h_tasks.size());
+  p->stream_entries = int64_t(stream.size());
 
   char buf[512];
   std::snprintf(buf, sizeof buf,
-                "rhs=%d items=%zu split_rows=%d tasks=%d (tw1=%d tw2=%d tw4=%d) smem=%d sms=%d",
-                rhs, h_items.size(), split_rows, p->num_tasks, ctas[0], ctas[1], ctas[2],
-                p->smem_bytes, num_sm);
+                "rhs=%d items=%zu split_rows=%d stream_entries=%zu tasks=%d (tw1=%d tw2=%d tw4=%d) "
+                "smem=%d sms=%d",
+                rhs, items.size(), split_rows, stream.size(), p->num_tasks, ctas[0], ctas[1],
+                ctas[2], p->smem_bytes, num_sm);
   p->summary = buf;
 
   DeviceGuard guard(d.device);
-  VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, h_items.size()) * sizeof(Item)));
+  VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(uint64_t)));
   VBSR_CUDA(cudaMalloc(&p->d_tasks, std::max<size_t>(1, h_tasks.size()) * sizeof(Task)));
   VBSR_CUDA(cudaMalloc(&p->d_status, kStatusWords * sizeof(int)));
-  if (!h_items.empty())
-    VBSR_CUDA(cudaMemcpy(p->d_items, h_items.data(), h_items.size() * sizeof(Item),
+  if (!stream.empty())
+    VBSR_CUDA(cudaMemcpy(p->d_stream, stream.data(), stream.size() * sizeof(uint64_t),
                          cudaMemcpyHostToDevice));
   if (!h_tasks.empty())
     VBSR_CUDA(cudaMemcpy(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
@@ -541,9 +567,10 @@ vbsr_status build_schedule(vbsr_plan* p) {
 void free_plan(vbsr_plan* p) {
   if (p == nullptr) return;
   DeviceGuard guard(p->device);
-  cudaFree(p->d_items);
+  cudaFree(p->d_stream);
   cudaFree(p->d_tasks);
   cudaFree(p->d_status);
+  cudaFree(p->d_timing);
   delete p;
 }
 
@@ -701,9 +728,8 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   }
   if (p->num_tasks == 0) return VBSR_OK;
   KernelParams kp;
-  kp.items = p->d_items;
+  kp.stream = p->d_stream;
   kp.tasks = p->d_tasks;
-  kp.blk = d.d_blk_desc;
   kp.values = d.d_values;
   kp.B = B;
   kp.C = C;
@@ -714,6 +740,7 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   kp.status = p->d_status;
   kp.drop_stage = p->drop_stage;
   kp.wait_limit = p->wait_limit;
+  kp.timing = p->timing_on ? p->d_timing : nullptr;
   switch (p->rhs) {
     case 8: launch_spmm<8>(p, kp, s); break;
     case 16: launch_spmm<16>(p, kp, s); break;
@@ -760,6 +787,31 @@ vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit
   if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
   p->drop_stage = drop_stage < 0 ? -1 : drop_stage;
   p->wait_limit = wait_limit_cycles > 0 ? wait_limit_cycles : 4000000000ll;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int out_len,
+                                 vbsr_stream_t stream) {
+  clear_error();
+  if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
+  DeviceGuard guard(p->device);
+  if (enable && p->d_timing == nullptr)
+    VBSR_CUDA(cudaMalloc(&p->d_timing, std::max(1, 2 * p->num_tasks) * sizeof(uint64_t)));
+  if (out != nullptr && p->d_timing != nullptr) {
+    const int n = std::min(out_len, 2 * p->num_tasks);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    VBSR_CUDA(cudaMemcpyAsync(out, p->d_timing, size_t(n) * sizeof(uint64_t),
+                              cudaMemcpyDeviceToHost, s));
+    VBSR_CUDA(cudaStreamSynchronize(s));
+  }
+  p->timing_on = enable != 0;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_num_tasks(const vbsr_plan* p, int* out) {
+  clear_error();
+  if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  *out = p->num_tasks;
   return VBSR_OK;
 }
 

@@ -14,20 +14,35 @@ namespace vbsr_b200 {
 vbsr_status set_error(vbsr_status s, const std::string& msg);
 void clear_error();
 
-// ---- work schedule -----------------------------------------------------------------------------
-// One work item: an h x nw tile of C (block row, RHS columns [n0, n0+nw)).
-struct alignas(16) Item {
-  long long val_off;  // offset (floats) of the row's first block in the device value array
-  int blk_begin;      // first block (index into the block descriptor array)
-  int nblk;           // blocks in the row
-  int c_row;          // first scalar row of the tile in C (matrix-local)
-  int h;              // block-row height
-  int n0;             // first RHS column
-  int nw;             // RHS columns
-};
-static_assert(sizeof(Item) == 32, "Item layout");
+// ---- work schedule ---------------------------------------------------------------------------
+// The plan compiles the matrix into one instruction stream per team: a sequence of 64-bit entries,
+// an item header followed by that item's k-chunks (one chunk = at most kChunk block columns of one
+// block), then the next header, and so on. Producer and consumers of a team walk the same stream.
+//
+// Header (bit 63 = 1): an h x nw tile of C starting at scalar row c_row, RHS columns [n0, n0+nw)
+//   bits  0..30 c_row       bits 31..33 h/8 - 1      bits 34..36 n0/8     bits 37..38 log2(nw/8)
+// Chunk  (bit 63 = 0): block columns [k0, k0+kc) of one block of that item
+//   bits  0..27 val/64  (value offset of the block; blocks start at multiples of 64 floats)
+//   bits 28..55 (col + k0)/8   (first scalar column of the chunk in B)
+//   bits 56..58 w/8 - 1        bit 59 k0/32     bits 60..61 kc/8 - 1     bit 62 last chunk of block
+namespace entry {
+constexpr uint64_t kHeader = 1ull << 63;
+constexpr uint64_t kLastOfBlock = 1ull << 62;
+inline uint64_t header(int64_t c_row, int h, int n0, int nw) {
+  int lg = 0;
+  while ((8 << lg) < nw) ++lg;
+  return kHeader | uint64_t(c_row) | (uint64_t(h / 8 - 1) << 31) | (uint64_t(n0 / 8) << 34) |
+         (uint64_t(lg) << 37);
+}
+inline uint64_t chunk(int64_t val, int64_t col, int w, int k0, int kc, bool last) {
+  return uint64_t(val / 64) | (uint64_t((col + k0) / 8) << 28) | (uint64_t(w / 8 - 1) << 56) |
+         (uint64_t(k0 / 32) << 59) | (uint64_t(kc / 8 - 1) << 60) | (last ? kLastOfBlock : 0);
+}
+constexpr int64_t kMaxVal = (int64_t(1) << 28) * 64;  // value offsets must stay below this
+constexpr int64_t kMaxCol = (int64_t(1) << 28) * 8;
+}  // namespace entry
 
-// One CTA task: up to kConsumerWarps / team_warps teams, team t owning items
+// One CTA task: kConsumerWarps / team_warps teams; team t walks stream entries
 // [team_off[t], team_off[t+1]).
 struct alignas(16) Task {
   int team_off[9];
@@ -52,6 +67,7 @@ struct MatrixData {
   // host copies of the row structure (the planner reads these)
   std::vector<int32_t> h_row_ptr, h_row_size;
   std::vector<int64_t> h_row_off, h_val_off_row, h_sum_w;
+  std::vector<uint32_t> h_blk_desc;  // per block: col_scalar_off | (w/8 - 1)
   // device arrays in the reference layout (device_view) ...
   int32_t *d_row_ptr = nullptr, *d_block_col = nullptr, *d_row_size = nullptr,
           *d_col_size = nullptr;
