@@ -1,8 +1,11 @@
 // vbsr_device.cu — device side of the engine: the owning device format (Matrix), the planner
 // (Plan), the execute path and the C-ABI entry points that touch a GPU.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -57,8 +60,7 @@ __device__ __forceinline__ int block_row_of(const int32_t* row_ptr, int rows, in
 }
 
 // Re-lays blocks [b_begin, b_end) from the reference layout (column-major h x w, element (r,k) at
-// r + k*h) into row panels (panel r/8 is 8 x w column-major: element (r,k) at
-// (r/8)*8*w + k*8 + r%8). `src` holds values starting at value offset src_base.
+// r + k*h) into the device format (blk_pos). `src` holds values starting at value offset src_base.
 __global__ void relayout_blocks(const int32_t* row_ptr, int rows, const int32_t* row_size,
                                 const int64_t* value_off, const uint32_t* blk, int b_begin,
                                 const float* src, long long src_base, float* dst) {
@@ -70,11 +72,11 @@ __global__ void relayout_blocks(const int32_t* row_ptr, int rows, const int32_t*
   float* d = dst + vo;
   for (int i = threadIdx.x; i < h * w; i += blockDim.x) {
     const int r = i % h, k = i / h;
-    d[(r >> 3) * 8 * w + k * 8 + (r & 7)] = s[i];
+    d[blk_pos(h, w, r, k)] = s[i];
   }
 }
 
-// Fills blocks in the panel layout with the counter-based generator: the element at reference
+// Fills blocks in the device format with the counter-based generator: the element at reference
 // (packed) position global_base + value_off[b] + r + k*h gets rng_uniform(key, that position).
 __global__ void generate_blocks(const int32_t* row_ptr, int rows, const int32_t* row_size,
                                 const int64_t* value_off, const uint32_t* blk, int nnzb,
@@ -85,8 +87,7 @@ __global__ void generate_blocks(const int32_t* row_ptr, int rows, const int32_t*
     const long long vo = value_off[b];
     for (int i = threadIdx.x; i < h * w; i += blockDim.x) {
       const int r = i % h, k = i / h;
-      dst[vo + (r >> 3) * 8 * w + k * 8 + (r & 7)] =
-          rng_uniform(key, uint64_t(global_base + vo + i));
+      dst[vo + blk_pos(h, w, r, k)] = rng_uniform(key, uint64_t(global_base + vo + i));
     }
   }
 }
@@ -99,8 +100,8 @@ __global__ void fill_uniform_kernel(uint64_t key, uint64_t first, uint64_t count
 
 // ---- raw launchers (reference launch_row_owned / launch_row_owned_scalar) --------------------------
 
-__device__ __forceinline__ float panel_value(const float* blockv, int w, int r, int k) {
-  return blockv[(r >> 3) * 8 * w + k * 8 + (r & 7)];
+__device__ __forceinline__ float block_value(const float* blockv, int h, int w, int r, int k) {
+  return blockv[blk_pos(h, w, r, k)];
 }
 
 // One output element per thread; grid (block_rows, ceil(64*rhs/256)).
@@ -118,7 +119,7 @@ __global__ void rowwise_scalar_kernel(vbsr_device_matrix a, const float* __restr
       const float* av = a.values + a.value_off[b];
       const float* bv = B + a.col_scalar_off[c] + (long long)n * a.scalar_cols;
       float part = 0.0f;
-      for (int k = 0; k < w; ++k) part = fmaf(panel_value(av, w, r, k), bv[k], part);
+      for (int k = 0; k < w; ++k) part = fmaf(block_value(av, h, w, r, k), bv[k], part);
       acc += part;
     }
     C[a.row_scalar_off[row] + r + (long long)n * a.scalar_rows] = acc;
@@ -143,7 +144,7 @@ __global__ void rowwise_direct_kernel(vbsr_device_matrix a, const float* __restr
       const float* bv = B + a.col_scalar_off[c] + (long long)n0 * a.scalar_cols;
       float part[8] = {};
       for (int k = 0; k < w; ++k) {
-        const float x = panel_value(av, w, r, k);
+        const float x = block_value(av, h, w, r, k);
 #pragma unroll
         for (int j = 0; j < 8; ++j) part[j] = fmaf(x, __ldg(bv + k + (long long)j * a.scalar_cols), part[j]);
       }
@@ -154,6 +155,38 @@ __global__ void rowwise_direct_kernel(vbsr_device_matrix a, const float* __restr
     for (int j = 0; j < 8; ++j)
       C[a.row_scalar_off[row] + r + (long long)(n0 + j) * a.scalar_rows] = acc[j];
   }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// B (K x rhs, column-major, ld K) as a 2-D tensor with an 8-column x `rows`-row box.
+vbsr_status encode_b_map(CUtensorMap* map, const float* B, int64_t K, int rhs, int rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rhs)};
+  const cuuint64_t strides[1] = {cuuint64_t(K) * sizeof(float)};
+  const cuuint32_t box[2] = {8u, cuuint32_t(rows)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return VBSR_OK;
 }
 
 bool valid_rhs(int rhs) { return rhs == 8 || rhs == 16 || rhs == 32 || rhs == 64; }
@@ -343,7 +376,7 @@ struct vbsr_plan {
 
 namespace {
 
-constexpr int kSmemBudget = 220 * 1024;  // dynamic shared memory per CTA
+constexpr int kSmemBudget = 220 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
 
 // Per-team time model of one item, in warp-issue cycles: FMAs per thread plus a per-chunk and
 // per-item overhead.
@@ -355,10 +388,11 @@ double item_cost(int h, int nw, int64_t sum_w, int nchunks) {
 template <int RHS>
 cudaError_t set_kernel_attrs() {
   cudaError_t e = cudaFuncSetAttribute(spmm_kernel<RHS, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemBudget + 1024);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(spmm_kernel<RHS, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSmemBudget);
+                              kSmemBudget + 1024);
 }
 
 vbsr_status build_schedule(vbsr_plan* p) {
@@ -531,8 +565,9 @@ vbsr_status build_schedule(vbsr_plan* p) {
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
-  // At least ~116 KB so that one CTA occupies one SM (the schedule is static per CTA).
-  p->smem_bytes = std::max(max_smem, 116 * 1024);
+  // At least ~116 KB so that one CTA occupies one SM (the schedule is static per CTA); plus 1 KB
+  // so the kernel can align its stage base to 1 KB.
+  p->smem_bytes = std::max(max_smem, 116 * 1024) + 1024;
   p->num_tasks = int(h_tasks.size());
   p->stream_entries = int64_t(stream.size());
 
@@ -728,6 +763,10 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   }
   if (p->num_tasks == 0) return VBSR_OK;
   KernelParams kp;
+  vbsr_status st = encode_b_map(&kp.b_full, B, d.K, p->rhs, p->rhs);
+  if (st != VBSR_OK) return st;
+  st = encode_b_map(&kp.b_half, B, d.K, p->rhs, p->rhs > 8 ? p->rhs / 2 : p->rhs);
+  if (st != VBSR_OK) return st;
   kp.stream = p->d_stream;
   kp.tasks = p->d_tasks;
   kp.values = d.d_values;

@@ -8,10 +8,10 @@
 // next window already in flight, so no descriptor load sits on the critical path. The producer
 // warp walks every team's stream and, for each k-chunk (at most 32 block columns of one block),
 // issues 1-D TMA bulk copies (cp.async.bulk) of
-//   * the chunk's A row panels (h/8 copies of 8*kc floats; A values stream from HBM once, with an
-//     L2 evict-first hint), and
-//   * the chunk's B rows (nw copies of kc floats, with an L2 evict-last hint because every B row
-//     is re-read by every block of the same block column),
+//   * the chunk's A values (one bulk copy of h*kc floats, contiguous in the device format; A streams
+//     from HBM once, with an L2 evict-first hint), and
+//   * the chunk's B rows (kc/8 2-D tensor copies of an 8-column x nw-row box, with an L2
+//     evict-last hint because B is re-read by every block of the same block column),
 // into a free stage, and arms the stage's full barrier with the byte count. Teams compute with
 // fp32 FMA on CUDA cores from shared memory into a TM x TN register tile per thread, keep a
 // per-block partial sum (so no single fp32 chain is longer than one block width), and store
@@ -22,6 +22,8 @@
 // plan's status word, raises a CTA-wide abort flag and unwinds; before the CTA exits after an
 // abort, the producer waits (again bounded) for every copy it issued.
 #pragma once
+#include <cuda.h>
+
 #include <cstdint>
 
 #include "vbsr_internal.h"
@@ -33,6 +35,8 @@ namespace vbsr_b200 {
 typedef unsigned long long u64;
 
 struct KernelParams {
+  CUtensorMap b_full;   // B as a K x rhs tensor, box 8 columns x rhs rows
+  CUtensorMap b_half;   // same, box 8 columns x rhs/2 rows (items of split rows)
   const u64* stream;    // per-team instruction streams
   const Task* tasks;
   const float* values;  // re-laid-out values
@@ -124,12 +128,20 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
                                              uint32_t full0, uint32_t empty0, int& s, uint32_t& ph,
                                              int tt, int lane, volatile int* abort_flag) {
   constexpr TileCfg cfg = tile_cfg(H, NW);
-  constexpr int TM = cfg.tm, TN = cfg.tn, RG = H / TM;
-  constexpr int PS = a_panel_stride(TM);
+  constexpr int TM = cfg.tm, TN = cfg.tn, RG = H / TM, NG = NW / TN;
   const bool active = tt < cfg.threads;
   const int rg = tt % RG, ng = tt / RG;
-  const int a_off = ((rg * TM) / 8) * PS + (rg * TM) % 8;
-  const int b_off = stage_b_offset(H, TM) + b_row_offset(ng * TN, TN);
+  const int r0 = rg * TM, pnl = r0 >> 3, xf = panel_xor(pnl);
+  // A: offsets (floats) of the thread's 16-byte units for the 4 columns of a k-quad, relative to
+  // the quad's first unit (panel format: unit q = 2k + (row/4 & 1), stored at q ^ xf).
+  int offa[4][2];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int h2 = (TM == 8) ? hh : ((r0 >> 2) & 1);
+      offa[kk][hh] = (((2 * kk + h2) ^ xf) << 2) + ((TM == 2) ? (r0 & 3) : 0);
+    }
 
   float acc[TM][TN], part[TM][TN];
 #pragma unroll
@@ -144,30 +156,32 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
     const int kc = chk_kc(e);
     if (!wait_phase(full0 + 8u * s, ph, p, abort_flag, lane)) return false;
     if (active) {
-      const float* As = stages + s * stage_floats + a_off;
-      const float* Bs = stages + s * stage_floats + b_off;
+      const float* As = stages + s * stage_floats + pnl * 8 * kc;
+      const float* Bs = stages + s * stage_floats + stage_b_offset(H) + ng * 8;
 #pragma unroll 1
-      for (int k = 0; k < kc; k += 8) {
+      for (int k8 = 0; k8 < kc; k8 += 8) {
+        const float* Ak = As + k8 * 8;
+        const float* Bk = Bs + k8 * NW;
 #pragma unroll
         for (int kq = 0; kq < 8; kq += 4) {
           float4 bv[TN];
 #pragma unroll
           for (int j = 0; j < TN; ++j)
-            bv[j] = *reinterpret_cast<const float4*>(Bs + j * kBRow + k + kq);
+            bv[j] = *reinterpret_cast<const float4*>(Bk + j * NG * 8 + kq);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             float a[TM];
-            const float* ap = As + (k + kq + kk) * 8;
+            const float* ap = Ak + kq * 8;
             if constexpr (TM == 8) {
-              const float4 x = *reinterpret_cast<const float4*>(ap);
-              const float4 y = *reinterpret_cast<const float4*>(ap + 4);
+              const float4 x = *reinterpret_cast<const float4*>(ap + offa[kk][0]);
+              const float4 y = *reinterpret_cast<const float4*>(ap + offa[kk][1]);
               a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w;
               a[4] = y.x; a[5] = y.y; a[6] = y.z; a[7] = y.w;
             } else if constexpr (TM == 4) {
-              const float4 x = *reinterpret_cast<const float4*>(ap);
+              const float4 x = *reinterpret_cast<const float4*>(ap + offa[kk][0]);
               a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w;
             } else {
-              const float2 x = *reinterpret_cast<const float2*>(ap);
+              const float2 x = *reinterpret_cast<const float2*>(ap + offa[kk][0]);
               a[0] = x.x; a[1] = x.y;
             }
 #pragma unroll
@@ -203,10 +217,10 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
     return true;
   }
   if (active) {
-    float* cb = p.C + (long long)c_row + rg * TM;
+    float* cb = p.C + (long long)c_row + r0;
 #pragma unroll
     for (int j = 0; j < TN; ++j) {
-      float* dst = cb + (long long)(n0 + ng * TN + j) * p.M;
+      float* dst = cb + (long long)(n0 + ng + j * NG) * p.M;
       if constexpr (TM == 8) {
         reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
         reinterpret_cast<float4*>(dst)[1] = make_float4(acc[4][j], acc[5][j], acc[6][j], acc[7][j]);
@@ -335,8 +349,7 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
             const long long val = chk_val(e), colk = chk_colk(e);
             const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
             const int h = it[j].h, nw = it[j].nw, n0 = it[j].n0;
-            const int panels = h >> 3;
-            const int ps = a_panel_stride(it[j].tm);
+            (void)w;
             const bool drop = (j == 0 && issued0 == p.drop_stage);
             if (j == 0) ++issued0;
             bool in_bounds = true;
@@ -352,15 +365,16 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
               }
             } else {
               float* st = stages + (j * D + s) * sf;
-              if (lane == 0) mbar_arrive_expect_tx(full_bar, uint32_t((panels * 32 + nw * 4) * kc));
-              __syncwarp();
-              if (lane < panels)
-                bulk_g2s(smem_addr(st + lane * ps), p.values + val + (long long)lane * 8 * w + k0 * 8,
-                         uint32_t(32 * kc), full_bar, pol_a);
-              const int boff = panels * ps;
-              for (int n = lane; n < nw; n += 32)
-                bulk_g2s(smem_addr(st + boff + b_row_offset(n, it[j].tn)),
-                         p.B + colk + (long long)(n0 + n) * p.K, uint32_t(4 * kc), full_bar, pol_b);
+              if (lane == 0) {
+                mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
+                bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc),
+                         full_bar, pol_a);
+              } else if (lane <= (kc >> 3)) {
+                const int g = lane - 1;
+                const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
+                tensor2d_g2s(smem_addr(st + stage_b_offset(h) + g * nw * 8), map,
+                             int(colk) + 8 * g, n0, full_bar, pol_b);
+              }
               filled[j] |= 1u << s;
               lastpar[j] = (lastpar[j] & ~(1u << s)) | (phase[j] << s);
             }
@@ -418,8 +432,11 @@ __device__ __forceinline__ u64 global_ns() {
 // ---- kernel --------------------------------------------------------------------------------------
 
 template <int RHS, bool CHECK>
-__global__ void __launch_bounds__(kThreads, 1) spmm_kernel(const __grid_constant__ KernelParams p) {
-  extern __shared__ __align__(128) float stages[];
+__global__ void __maxnreg__(224) spmm_kernel(const __grid_constant__ KernelParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1 KB-aligned stage base (the host adds 1 KB of slack to the dynamic allocation)
+  float* stages = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bars[2][kConsumerWarps][kMaxStages];
   __shared__ int abort_flag;
   const Task task = p.tasks[blockIdx.x];

@@ -1,17 +1,22 @@
 // vbsr_tiles.h — tile geometry shared by the host planner and the sm_100a kernels.
 //
-// One work item is one block row (or one RHS-column half of a heavy block row): an h x nw tile
-// of C, h in {8,...,64}, nw in {8,16,32,64}. A "team" of 1, 2 or 4 warps owns one item at a time;
-// each thread of the team keeps a TM x TN register tile of C (TM rows, TN RHS columns).
+// One work item is one block row (or one RHS-column half of a heavy block row): an h x nw tile of C,
+// h in {8,...,64}, nw in {8,16,32,64}. A "team" of 1, 2 or 4 warps owns one item at a time; each
+// thread of the team keeps a TM x TN register tile of C (TM consecutive rows; TN RHS columns
+// strided by the number of column groups).
 //
-// The item's A and B operands are streamed through a shared-memory ring, one k-chunk of at most
-// 32 block columns per stage:
-//   A part: h/8 row panels, each 8 rows x kc columns column-major (8*kc floats, exactly the bytes
-//           of that panel's columns [k0, k0+kc) in the device value format), placed at a panel
-//           stride of 256 + pad floats so that lanes reading different panels at the same k hit
-//           different 16-byte bank groups;
-//   B part: nw rows (one per RHS column n), row n holding B[col_off+k0 .. +kc, n0+n], placed at
-//           36 floats per row plus 4 floats after every TN rows, for the same reason.
+// Device value format. Every h x w block keeps its reference position and size in the value array
+// (value_off is unchanged), but inside the block the values are re-laid-out for the kernels: the
+// block is cut into k-chunks of 32 block columns (the last one may be narrower, kc = 8..32), each
+// chunk is one contiguous run of h*kc floats, and inside a chunk the rows form h/8 panels of 8
+// rows, panel p holding its 8 x kc values column-major in 16-byte units whose index is XOR-ed
+// with f(p) = ((p&3)<<1) | ((p>>2)&1). One TMA bulk copy moves a whole chunk into shared memory,
+// and the XOR makes the consumers' 16-byte reads of different panels at the same column fall into
+// different shared-memory bank groups (for both 8-row and 4-row thread tiles).
+//
+// Pipeline stage (one k-chunk of one block of one item): the A chunk as stored (h*kc floats)
+// followed, at offset h*32 floats, by the B chunk: kc/8 boxes of 8 columns x nw rows, each row of
+// a box 8 consecutive floats of one RHS column (written by 2-D tensor TMA, no swizzle).
 #pragma once
 
 #if defined(__CUDACC__)
@@ -26,7 +31,6 @@ constexpr int kConsumerWarps = 8;                 // compute warps per CTA
 constexpr int kThreads = 32 * (kConsumerWarps + 1); // + one producer warp
 constexpr int kChunk = 32;                        // block columns per pipeline stage
 constexpr int kMaxStages = 4;
-constexpr int kBRow = 36;                         // floats per staged B row (32 + 4 pad)
 
 struct TileCfg {
   int tm, tn;    // register tile per thread
@@ -51,21 +55,22 @@ VBSR_HD TileCfg tile_cfg(int h, int nw) {
   return c;
 }
 
-// Panel stride (floats) of the staged A chunk for a thread tile of TM rows.
-VBSR_HD int a_panel_stride(int tm) { return 256 + (tm == 8 ? 4 : (tm == 4 ? 8 : 16)); }
+// 16-byte-unit XOR of panel p (see the format description above).
+VBSR_HD int panel_xor(int p) { return ((p & 3) << 1) | ((p >> 2) & 1); }
 
-// Offset (floats) of staged B row n for a thread tile of TN columns.
-VBSR_HD int b_row_offset(int n, int tn) { return n * kBRow + (tn > 1 ? (n / tn) * 4 : 0); }
-
-// Floats of one stage for an (h, nw) item: A panels followed by B rows, rounded to 32 floats.
-VBSR_HD int stage_floats(int h, int nw) {
-  const TileCfg c = tile_cfg(h, nw);
-  const int a = (h / 8) * a_panel_stride(c.tm);
-  const int b = b_row_offset(nw, c.tn);
-  return ((a + b) + 31) / 32 * 32;
+// Position of element (r, k) of an h x w block inside the block's device storage.
+VBSR_HD int blk_pos(int h, int w, int r, int k) {
+  const int k0 = k & ~31;
+  const int kc = (w - k0) < 32 ? (w - k0) : 32;
+  const int p = r >> 3;
+  const int q = ((k - k0) << 1) | ((r >> 2) & 1);
+  return h * k0 + p * 8 * kc + ((q ^ panel_xor(p)) << 2) + (r & 3);
 }
 
-// Offset (floats) of the B rows inside a stage.
-VBSR_HD int stage_b_offset(int h, int tm) { return (h / 8) * a_panel_stride(tm); }
+// Floats of one stage for an (h, nw) item, rounded to 1 KB.
+VBSR_HD int stage_floats(int h, int nw) { return (h * 32 + nw * 32 + 255) / 256 * 256; }
+
+// Offset (floats) of the B boxes inside a stage.
+VBSR_HD int stage_b_offset(int h) { return h * 32; }
 
 }  // namespace vbsr_b200
