@@ -1,12 +1,13 @@
 // vbsr_kernels.cuh — the sm_100a SpMM kernel: C = A * B for one plan's schedule.
 //
-// CTA = kConsumerWarps compute warps + 1 producer warp, one CTA per SM, each CTA executing one
-// Task of the plan. The compute warps form teams of 1, 2 or 4 warps (fixed per task); each team
+// CTA = one producer warpgroup (4 warps; setmaxnreg lowers them to kProducerRegs registers) and two
+// consumer warpgroups (8 compute warps raised to kConsumerRegs registers), one CTA per SM, each
+// CTA executing one Task of the plan. The compute warps form teams of 1, 2 or 4 warps (fixed per task); each team
 // walks its own instruction stream (item headers and k-chunks, compiled by the planner; see
 // vbsr_internal.h) and owns a private ring of shared-memory stages guarded by "full" and "empty"
 // mbarriers. Streams are read through lane-distributed register windows of 32 entries with the
-// next window already in flight, so no descriptor load sits on the critical path. The producer
-// warp walks every team's stream and, for each k-chunk (at most 32 block columns of one block),
+// next window already in flight, so no descriptor load sits on the critical path. Producer warp w
+// walks the streams of teams w, w+4, ... and, for each k-chunk (at most 32 block columns of one block),
 // issues 1-D TMA bulk copies (cp.async.bulk) of
 //   * the chunk's A values (one bulk copy of h*kc floats, contiguous in the device format; A streams
 //     from HBM once, with an L2 evict-first hint), and
@@ -296,9 +297,10 @@ struct ProdItem {
   int h, n0, nw, tm, tn;
 };
 
+// Producer warp `pw` serves teams pw, pw + kProducerWarps, ... (NT of them).
 template <int NT, bool CHECK>
 __device__ void producer(const KernelParams& p, const Task& task, float* stages, uint32_t full_base,
-                         uint32_t empty_base, int lane, volatile int* abort_flag) {
+                         uint32_t empty_base, int pw, int lane, volatile int* abort_flag) {
   const int D = task.stages;
   const int sf = task.stage_floats;
   const uint64_t pol_a = policy_evict_first();
@@ -310,7 +312,8 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
   uint32_t live = 0;
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
-    win[j].init(p.stream, task.team_off[j], task.team_off[j + 1], lane);
+    const int team = pw + j * kProducerWarps;
+    win[j].init(p.stream, task.team_off[team], task.team_off[team + 1], lane);
     it[j] = ProdItem{8, 0, 8, 2, 1};
     slot[j] = 0;
     phase[j] = filled[j] = lastpar[j] = 0;
@@ -341,8 +344,9 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
           live &= ~(1u << j);
         } else {
           const int s = slot[j];
-          const uint32_t empty_bar = empty_base + 8u * (j * kMaxStages + s);
-          const uint32_t full_bar = full_base + 8u * (j * kMaxStages + s);
+          const int team = pw + j * kProducerWarps;
+          const uint32_t empty_bar = empty_base + 8u * (team * kMaxStages + s);
+          const uint32_t full_bar = full_base + 8u * (team * kMaxStages + s);
           // every lane probes (each gets the barrier's acquire ordering); act when all agree
           if (__all_sync(0xffffffffu, mbar_test(empty_bar, phase[j] ^ 1u))) {
             progressed = true;
@@ -350,8 +354,8 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
             const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
             const int h = it[j].h, nw = it[j].nw, n0 = it[j].n0;
             (void)w;
-            const bool drop = (j == 0 && issued0 == p.drop_stage);
-            if (j == 0) ++issued0;
+            const bool drop = (team == 0 && issued0 == p.drop_stage);
+            if (team == 0) ++issued0;
             bool in_bounds = true;
             if (CHECK)
               in_bounds = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K &&
@@ -364,7 +368,7 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
                 mbar_arrive(full_bar);  // release the consumers without touching memory
               }
             } else {
-              float* st = stages + (j * D + s) * sf;
+              float* st = stages + (team * D + s) * sf;
               if (lane == 0) {
                 mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
                 bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc),
@@ -413,7 +417,7 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
     for (int j = 0; j < NT; ++j) {
       for (int s = 0; s < D; ++s) {
         if (!(filled[j] & (1u << s))) continue;
-        const uint32_t bar = full_base + 8u * (j * kMaxStages + s);
+        const uint32_t bar = full_base + 8u * ((pw + j * kProducerWarps) * kMaxStages + s);
         const uint32_t par = (lastpar[j] >> s) & 1u;
         const long long t0 = clock64();
         while (!mbar_try(bar, par) && clock64() - t0 < p.wait_limit) {
@@ -432,7 +436,7 @@ __device__ __forceinline__ u64 global_ns() {
 // ---- kernel --------------------------------------------------------------------------------------
 
 template <int RHS, bool CHECK>
-__global__ void __maxnreg__(224) spmm_kernel(const __grid_constant__ KernelParams p) {
+__global__ void __launch_bounds__(kThreads, 1) spmm_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1 KB-aligned stage base (the host adds 1 KB of slack to the dynamic allocation)
   float* stages = reinterpret_cast<float*>(
@@ -458,15 +462,18 @@ __global__ void __maxnreg__(224) spmm_kernel(const __grid_constant__ KernelParam
   __syncthreads();
   volatile int* abort_v = &abort_flag;
 
-  if (warp == kConsumerWarps) {
+  if (warp < kProducerWarps) {
+    regs_dec<kProducerRegs>();
     if (tw == 1)
-      producer<8, CHECK>(p, task, stages, full_base, empty_base, lane, abort_v);
+      producer<2, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
     else if (tw == 2)
-      producer<4, CHECK>(p, task, stages, full_base, empty_base, lane, abort_v);
-    else
-      producer<2, CHECK>(p, task, stages, full_base, empty_base, lane, abort_v);
+      producer<1, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
+    else if (warp < 2)
+      producer<1, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
   } else {
-    consumer<RHS, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
+    regs_inc<kConsumerRegs>();
+    consumer<RHS, CHECK>(p, task, stages, full_base, empty_base, warp - kProducerWarps, lane,
+                         abort_v);
   }
   __syncthreads();
   if (threadIdx.x == 0 && p.timing) p.timing[2 * blockIdx.x + 1] = global_ns();
