@@ -255,8 +255,16 @@ def cta_time_stats(plan, B, C, stream):
     t = plan.cta_timing(stream).astype(np.int64)
     plan.enable_cta_timing(False)
     dur = (t[:, 1] - t[:, 0]) / 1e3
+    tw, cost = plan.task_stats()
+    by_team = {}
+    for w in sorted(set(tw.tolist())):
+        d = dur[tw == w]
+        by_team[f"team_warps_{w}"] = {"ctas": int(d.size), "median_us": float(np.median(d)),
+                                      "max_us": float(d.max()),
+                                      "us_per_model_unit": float(np.median(d / cost[tw == w]))}
     return {"ctas": int(t.shape[0]), "min_us": float(dur.min()), "median_us": float(np.median(dur)),
-            "max_us": float(dur.max()), "span_us": float((t[:, 1].max() - t[:, 0].min()) / 1e3)}
+            "max_us": float(dur.max()), "span_us": float((t[:, 1].max() - t[:, 0].min()) / 1e3),
+            "by_team_size": by_team}
 
 
 def time_headline(vb, torch, stream, peak, steps=200, warmup=10):

@@ -187,6 +187,10 @@ vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit
  * CTA order) from the last timed execution. */
 vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int out_len,
                                  vbsr_stream_t stream);
+/* Per-task schedule facts (a tuning aid): team size in warps and the planner's cost estimate of
+ * the task's most loaded team, for the first n tasks. Either output may be NULL. */
+vbsr_status vbsr_plan_task_stats(const vbsr_plan* p, int32_t* team_warps, double* model_cost,
+                                 int n);
 /* Number of CTAs (tasks) one execution launches. */
 vbsr_status vbsr_plan_num_tasks(const vbsr_plan* p, int* out);
 

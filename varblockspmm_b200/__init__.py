@@ -140,6 +140,7 @@ _sig = {
     "vbsr_plan_set_debug": [_vp, C.c_int, C.c_int64],
     "vbsr_plan_cta_timing": [_vp, C.c_int, C.POINTER(C.c_uint64), C.c_int, _vp],
     "vbsr_plan_num_tasks": [_vp, C.POINTER(C.c_int)],
+    "vbsr_plan_task_stats": [_vp, C.POINTER(C.c_int32), C.POINTER(C.c_double), C.c_int],
     "vbsr_launch_row_owned": [C.POINTER(DeviceMatrix), _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp],
     "vbsr_launch_row_owned_scalar": [C.POINTER(DeviceMatrix), _vp, _vp, C.c_int, _vp],
     "vbsr_generate": [C.POINTER(GenOpts), C.POINTER(_vp)],
@@ -464,6 +465,15 @@ class Plan:
         n = C.c_int()
         _check(_lib.vbsr_plan_num_tasks(self._h, C.byref(n)))
         return n.value
+
+    def task_stats(self):
+        """(team_warps, model_cost) per task of the schedule."""
+        n = self.num_tasks()
+        tw = np.zeros(n, dtype=np.int32)
+        mc = np.zeros(n, dtype=np.float64)
+        _check(_lib.vbsr_plan_task_stats(self._h, tw.ctypes.data_as(C.POINTER(C.c_int32)),
+                                         mc.ctypes.data_as(C.POINTER(C.c_double)), n))
+        return tw, mc
 
     def enable_cta_timing(self, enable: bool = True):
         _check(_lib.vbsr_plan_cta_timing(self._h, int(enable), None, 0, None))

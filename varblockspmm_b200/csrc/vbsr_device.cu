@@ -372,6 +372,8 @@ struct vbsr_plan {
   int drop_stage = -1;
   long long wait_limit = 4000000000ll;  // ~2 s at 1.965 GHz
   std::string summary;
+  std::vector<int> task_warps;      // team size of every task
+  std::vector<double> task_cost;    // planner's cost model: the task's most loaded team
 };
 
 namespace {
@@ -518,11 +520,13 @@ vbsr_status build_schedule(vbsr_plan* p) {
     std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
     for (int w = 0; w < workers; ++w) heap.push({0.0, w});
     std::vector<std::vector<int>> lists(workers);
+    std::vector<double> load(workers, 0.0);
     for (int k : idx) {
       Load l = heap.top();
       heap.pop();
       lists[l.second].push_back(k);
       l.first += items[k].cost;
+      load[l.second] = l.first;
       heap.push(l);
     }
     for (int t = 0; t < ctas[c]; ++t) {
@@ -561,6 +565,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
       task.stages = stages;
       max_smem = std::max(max_smem, nt * stages * sf * 4);
       h_tasks.push_back(task);
+      p->task_warps.push_back(tw);
+      p->task_cost.push_back(*std::max_element(load.begin() + t * nt, load.begin() + (t + 1) * nt));
     }
   }
   if (stream.size() >= (size_t(1) << 31))
@@ -844,6 +850,17 @@ vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int ou
     VBSR_CUDA(cudaStreamSynchronize(s));
   }
   p->timing_on = enable != 0;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_task_stats(const vbsr_plan* p, int32_t* team_warps, double* model_cost,
+                                 int n) {
+  clear_error();
+  if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
+  for (int i = 0; i < n && i < p->num_tasks; ++i) {
+    if (team_warps) team_warps[i] = p->task_warps[i];
+    if (model_cost) model_cost[i] = p->task_cost[i];
+  }
   return VBSR_OK;
 }
 

@@ -98,13 +98,15 @@ __device__ __forceinline__ void record_status(int* status, int code, int info) {
 
 // Warp-collective wait for phase `parity` of `bar`; every lane polls the barrier itself (so each
 // lane gets the barrier's acquire ordering), and every decision is made uniformly by the warp.
-// Returns false if the CTA aborted or the wait exceeded p.wait_limit SM clocks.
+// mbarrier.try_wait suspends the warp in hardware while the phase is pending, so waiting warps do
+// not take issue slots from the warps that compute. Returns false if the CTA aborted or the wait
+// exceeded p.wait_limit SM clocks.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const KernelParams& p,
                                            volatile int* abort_flag, int lane) {
+  if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
   const long long t0 = clock64();
   while (true) {
-    const bool ok = mbar_try(bar, parity);
-    if (__all_sync(0xffffffffu, ok)) return true;
+    if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
     int stop = 0;
     if (lane == 0) {
       if (*abort_flag) {
@@ -292,9 +294,9 @@ __device__ void consumer(const KernelParams& p, const Task& task, const float* s
 
 // ---- producer ------------------------------------------------------------------------------------
 
-// Current item of a team as seen by the producer: h, n0, nw and the tile's TM / TN packed.
+// Current item of a team as seen by the producer.
 struct ProdItem {
-  int h, n0, nw, tm, tn;
+  int h, n0, nw;
 };
 
 // Producer warp `pw` serves teams pw, pw + kProducerWarps, ... (NT of them).
@@ -314,100 +316,82 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
   for (int j = 0; j < NT; ++j) {
     const int team = pw + j * kProducerWarps;
     win[j].init(p.stream, task.team_off[team], task.team_off[team + 1], lane);
-    it[j] = ProdItem{8, 0, 8, 2, 1};
+    it[j] = ProdItem{8, 0, 8};
     slot[j] = 0;
     phase[j] = filled[j] = lastpar[j] = 0;
     if (!win[j].done()) live |= 1u << j;
   }
   int issued0 = 0;  // chunks issued for team 0 (debug drop hook)
-  long long t_stall = clock64();
+  int j = 0;
   while (live) {
-    bool progressed = false;
+    // next live team, round robin
+    while (!(live & (1u << j))) j = (j + 1 == NT) ? 0 : j + 1;
+    bool stop = false;
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      if (live & (1u << j)) {
-        // Headers need no stage: take them as they come.
-        u64 e = win[j].peek();
-        while (is_header(e)) {
-          it[j].h = hdr_h(e);
-          it[j].n0 = hdr_n0(e);
-          it[j].nw = hdr_nw(e);
-          const TileCfg c = tile_cfg(it[j].h, it[j].nw);
-          it[j].tm = c.tm;
-          it[j].tn = c.tn;
-          win[j].advance(p.stream, lane);
-          progressed = true;
-          if (win[j].done()) break;
-          e = win[j].peek();
-        }
-        if (win[j].done()) {
-          live &= ~(1u << j);
-        } else {
-          const int s = slot[j];
-          const int team = pw + j * kProducerWarps;
-          const uint32_t empty_bar = empty_base + 8u * (team * kMaxStages + s);
-          const uint32_t full_bar = full_base + 8u * (team * kMaxStages + s);
-          // every lane probes (each gets the barrier's acquire ordering); act when all agree
-          if (__all_sync(0xffffffffu, mbar_test(empty_bar, phase[j] ^ 1u))) {
-            progressed = true;
-            const long long val = chk_val(e), colk = chk_colk(e);
-            const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
-            const int h = it[j].h, nw = it[j].nw, n0 = it[j].n0;
-            (void)w;
-            const bool drop = (team == 0 && issued0 == p.drop_stage);
-            if (team == 0) ++issued0;
-            bool in_bounds = true;
-            if (CHECK)
-              in_bounds = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K &&
-                          n0 + nw <= p.rhs;
-            if (drop) {
-              // withhold the stage entirely (debug): no arrival, no copies
-            } else if (!in_bounds) {
-              if (lane == 0) {
-                record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
-                mbar_arrive(full_bar);  // release the consumers without touching memory
-              }
-            } else {
-              float* st = stages + (team * D + s) * sf;
-              if (lane == 0) {
-                mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
-                bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc),
-                         full_bar, pol_a);
-              } else if (lane <= (kc >> 3)) {
-                const int g = lane - 1;
-                const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
-                tensor2d_g2s(smem_addr(st + stage_b_offset(h) + g * nw * 8), map,
-                             int(colk) + 8 * g, n0, full_bar, pol_b);
-              }
-              filled[j] |= 1u << s;
-              lastpar[j] = (lastpar[j] & ~(1u << s)) | (phase[j] << s);
-            }
-            if (++slot[j] == D) {
-              slot[j] = 0;
-              phase[j] ^= 1u;
-            }
-            win[j].advance(p.stream, lane);
-            if (win[j].done()) live &= ~(1u << j);
-          }
-        }
+    for (int jj = 0; jj < NT; ++jj) {
+      if (jj != j) continue;  // static indexing of the per-team registers
+      // Headers need no stage: take them as they come.
+      u64 e = win[jj].peek();
+      while (is_header(e)) {
+        it[jj].h = hdr_h(e);
+        it[jj].n0 = hdr_n0(e);
+        it[jj].nw = hdr_nw(e);
+        win[jj].advance(p.stream, lane);
+        if (win[jj].done()) break;
+        e = win[jj].peek();
       }
-    }
-    if (progressed) {
-      t_stall = clock64();
-    } else {
-      int stop = 0;
-      if (lane == 0) {
-        if (*abort_flag) {
-          stop = 1;
-        } else if (clock64() - t_stall > p.wait_limit) {
-          record_status(p.status, VBSR_TIMEOUT, int(blockIdx.x));
-          *abort_flag = 1;
-          stop = 1;
-        }
+      if (win[jj].done()) {
+        live &= ~(1u << jj);
+        break;
       }
-      if (__shfl_sync(0xffffffffu, stop, 0)) break;
-      __nanosleep(20);
+      const int s = slot[jj];
+      const int team = pw + jj * kProducerWarps;
+      const uint32_t empty_bar = empty_base + 8u * (team * kMaxStages + s);
+      const uint32_t full_bar = full_base + 8u * (team * kMaxStages + s);
+      if (!wait_phase(empty_bar, phase[jj] ^ 1u, p, abort_flag, lane)) {
+        stop = true;
+        break;
+      }
+      const long long val = chk_val(e), colk = chk_colk(e);
+      const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
+      const int h = it[jj].h, nw = it[jj].nw, n0 = it[jj].n0;
+      const bool drop = (team == 0 && issued0 == p.drop_stage);
+      if (team == 0) ++issued0;
+      bool in_bounds = true;
+      if (CHECK)
+        in_bounds = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K &&
+                    n0 + nw <= p.rhs;
+      if (drop) {
+        // withhold the stage entirely (debug): no arrival, no copies
+      } else if (!in_bounds) {
+        if (lane == 0) {
+          record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+          mbar_arrive(full_bar);  // release the consumers without touching memory
+        }
+      } else {
+        float* st = stages + (team * D + s) * sf;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
+          bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc),
+                   full_bar, pol_a);
+        } else if (lane <= (kc >> 3)) {
+          const int g = lane - 1;
+          const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
+          tensor2d_g2s(smem_addr(st + stage_b_offset(h) + g * nw * 8), map, int(colk) + 8 * g, n0,
+                       full_bar, pol_b);
+        }
+        filled[jj] |= 1u << s;
+        lastpar[jj] = (lastpar[jj] & ~(1u << s)) | (phase[jj] << s);
+      }
+      if (++slot[jj] == D) {
+        slot[jj] = 0;
+        phase[jj] ^= 1u;
+      }
+      win[jj].advance(p.stream, lane);
+      if (win[jj].done()) live &= ~(1u << jj);
     }
+    if (stop) break;
+    j = (j + 1 == NT) ? 0 : j + 1;
   }
   __syncwarp();
   // After an abort, wait (bounded) for the last fill of every slot so that no bulk copy is still
