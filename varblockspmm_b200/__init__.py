@@ -162,6 +162,8 @@ STREAM_VALUES = 0xA11CE
 STREAM_DENSE = 0xB0B
 PLAN_BOUNDS_CHECK = 1
 PLAN_NO_SPLIT = 2
+PLAN_DIAG_SKIP_COPIES = 1 << 8  # diagnostics only: C is wrong
+PLAN_DIAG_SKIP_MATH = 1 << 9    # diagnostics only: C is wrong
 
 
 class Distribution(enum.IntEnum):

@@ -786,6 +786,7 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   kp.drop_stage = p->drop_stage;
   kp.wait_limit = p->wait_limit;
   kp.timing = p->timing_on ? p->d_timing : nullptr;
+  kp.diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
   switch (p->rhs) {
     case 8: launch_spmm<8>(p, kp, s); break;
     case 16: launch_spmm<16>(p, kp, s); break;

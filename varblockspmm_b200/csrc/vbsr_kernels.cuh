@@ -49,6 +49,7 @@ struct KernelParams {
   int drop_stage;       // debug: chunk number (per CTA, team 0) the producer withholds; < 0 off
   long long wait_limit; // SM clocks a single wait may take before it is declared stalled
   u64* timing;          // optional: per CTA (start, end) global timer in ns
+  int diag;             // VBSR_PLAN_DIAG_* bits (performance analysis only)
 };
 
 // ---- stream entries ------------------------------------------------------------------------------
@@ -158,7 +159,7 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
     win.advance(p.stream, lane);
     const int kc = chk_kc(e);
     if (!wait_phase(full0 + 8u * s, ph, p, abort_flag, lane)) return false;
-    if (active) {
+    if (active && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
       const float* As = stages + s * stage_floats + pnl * 8 * kc;
       const float* Bs = stages + s * stage_floats + stage_b_offset(H) + ng * 8;
 #pragma unroll 1
@@ -363,6 +364,8 @@ __device__ void producer(const KernelParams& p, const Task& task, float* stages,
                     n0 + nw <= p.rhs;
       if (drop) {
         // withhold the stage entirely (debug): no arrival, no copies
+      } else if (p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) {
+        if (lane == 0) mbar_arrive(full_bar);
       } else if (!in_bounds) {
         if (lane == 0) {
           record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
