@@ -1,27 +1,32 @@
 // vbsr_kernels.cuh — the sm_100a SpMM kernel: C = A * B for one plan's schedule.
 //
-// CTA = one producer warpgroup (4 warps; setmaxnreg lowers them to kProducerRegs registers) and two
-// consumer warpgroups (8 compute warps raised to kConsumerRegs registers), one CTA per SM, each
-// CTA executing one Task of the plan. The compute warps form teams of 1, 2 or 4 warps (fixed per task); each team
-// walks its own instruction stream (item headers and k-chunks, compiled by the planner; see
-// vbsr_internal.h) and owns a private ring of shared-memory stages guarded by "full" and "empty"
-// mbarriers. Streams are read through lane-distributed register windows of 32 entries with the
-// next window already in flight, so no descriptor load sits on the critical path. Producer warp w
-// walks the streams of teams w, w+4, ... and, for each k-chunk (at most 32 block columns of one block),
-// issues 1-D TMA bulk copies (cp.async.bulk) of
-//   * the chunk's A values (one bulk copy of h*kc floats, contiguous in the device format; A streams
-//     from HBM once, with an L2 evict-first hint), and
-//   * the chunk's B rows (kc/8 2-D tensor copies of an 8-column x nw-row box, with an L2
-//     evict-last hint because B is re-read by every block of the same block column),
-// into a free stage, and arms the stage's full barrier with the byte count. Teams compute with
-// fp32 FMA on CUDA cores from shared memory into a TM x TN register tile per thread, keep a
-// per-block partial sum (so no single fp32 chain is longer than one block width), and store
-// their tile of C straight from registers with 16-byte stores. Every C element is written by
-// exactly one thread: no atomics, no workspace, and C needs no prior clearing.
+// CTA = kConsumerWarps warps, one CTA per SM, each CTA executing one Task of the plan. The warps
+// form teams of 1, 2 or 4 warps (fixed per task); each team walks its own instruction stream (item
+// headers and k-chunks, compiled by the planner; see vbsr_internal.h) and owns a private ring of
+// D shared-memory stages guarded by "full" and "empty" mbarriers. Streams are read through
+// lane-distributed register windows of 32 entries with the next window already in flight, so no
+// descriptor load sits on the critical path.
+//
+// The team's leader warp is also its producer: it keeps a second stream cursor D-1 chunks ahead
+// and, each time the team starts a chunk, waits for the stage freed by the previous chunk and
+// issues the chunk D-1 ahead as TMA copies into it:
+//   * the chunk's A values (one cp.async.bulk of h*kc floats, contiguous in the device format;
+//     A streams from HBM once, with an L2 evict-first hint), and
+//   * the chunk's B rows (kc/8 2-D tensor copies cp.async.bulk.tensor of an 8-column x nw-row
+//     box, with an L2 evict-last hint because B is re-read by every block of the same block column),
+// arming the stage's full barrier with the byte count. Issuing costs a handful of instructions
+// per chunk, so no separate producer warps are needed and every warp of the CTA computes (with up
+// to 255 registers per thread).
+//
+// Teams compute with fp32 FMA on CUDA cores from shared memory into a TM x TN register tile per
+// thread, software-pipelined over k-quads, keep a per-block partial sum (so no single fp32 chain
+// is longer than one block width), and store their tile of C straight from registers with 16-byte
+// stores. Every C element is written by exactly one thread: no atomics, no workspace, and C needs
+// no prior clearing.
 //
 // Every wait is bounded: a wait that exceeds the plan's cycle limit records VBSR_TIMEOUT in the
 // plan's status word, raises a CTA-wide abort flag and unwinds; before the CTA exits after an
-// abort, the producer waits (again bounded) for every copy it issued.
+// abort, each leader waits (again bounded) for every copy it issued.
 #pragma once
 #include <cuda.h>
 
@@ -122,17 +127,143 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
   }
 }
 
-// ---- consumer ------------------------------------------------------------------------------------
+// ---- producer side (run by each team's leader warp) ----------------------------------------------
+
+// Issue cursor of a team: walks the team's stream ahead of the consumers.
+struct Issuer {
+  StreamWin win;
+  int h, n0, nw;        // item the cursor is in
+  int slot;             // next ring slot
+  uint32_t ph;          // ring phase of that slot
+  uint32_t filled;      // bit s: slot s has been filled at least once
+  uint32_t lastpar;     // bit s: phase parity of the last fill of slot s
+  int issued;           // chunks issued so far (debug drop hook)
+};
+
+// Issues the next chunk of the team's stream into the next ring slot (waiting until every warp of
+// the team has released that slot). Warp-collective. Returns false on abort.
+template <bool CHECK>
+__device__ __forceinline__ bool issue_next(const KernelParams& p, Issuer& is, float* team_stages,
+                                           int sf, int D, uint32_t full0, uint32_t empty0,
+                                           int team, int lane, volatile int* abort_flag) {
+  while (!is.win.done()) {
+    const u64 e = is.win.peek();
+    if (!is_header(e)) break;
+    is.h = hdr_h(e);
+    is.n0 = hdr_n0(e);
+    is.nw = hdr_nw(e);
+    is.win.advance(p.stream, lane);
+  }
+  if (is.win.done()) return true;
+  const u64 e = is.win.peek();
+  const int s = is.slot;
+  const uint32_t full_bar = full0 + 8u * s;
+  if (!wait_phase(empty0 + 8u * s, is.ph ^ 1u, p, abort_flag, lane)) return false;
+  const long long val = chk_val(e), colk = chk_colk(e);
+  const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
+  const int h = is.h, nw = is.nw, n0 = is.n0;
+  const bool drop = (team == 0 && is.issued == p.drop_stage);
+  ++is.issued;
+  bool in_bounds = true;
+  if (CHECK)
+    in_bounds = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K && n0 + nw <= p.rhs;
+  if (drop) {
+    // withhold the stage entirely (debug): no arrival, no copies
+  } else if (p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) {
+    if (lane == 0) mbar_arrive(full_bar);
+  } else if (!in_bounds) {
+    if (lane == 0) {
+      record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+      mbar_arrive(full_bar);  // release the consumers without touching memory
+    }
+  } else {
+    float* st = team_stages + s * sf;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
+      bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc), full_bar,
+               policy_evict_first());
+    } else if (lane <= (kc >> 3)) {
+      const int g = lane - 1;
+      const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
+      tensor2d_g2s(smem_addr(st + stage_b_offset(h) + g * nw * 8), map, int(colk) + 8 * g, n0,
+                   full_bar, policy_evict_last());
+    }
+    is.filled |= 1u << s;
+    is.lastpar = (is.lastpar & ~(1u << s)) | (is.ph << s);
+  }
+  if (++is.slot == D) {
+    is.slot = 0;
+    is.ph ^= 1u;
+  }
+  is.win.advance(p.stream, lane);
+  return true;
+}
+
+// ---- consumer side -------------------------------------------------------------------------------
+
+// Operands of one k-quad (4 block columns) for a TM x TN thread tile.
+template <int TM, int TN>
+struct Frag {
+  float a[4][TM];
+  float4 b[TN];
+};
+
+// Loads quad q of the stage: A from the XOR-swizzled panel chunk (offa = per-thread unit offsets),
+// B from the 8-column boxes (column n of box g at g*nw*8 + n*8).
+template <int TM, int TN, int NG>
+__device__ __forceinline__ void load_frag(Frag<TM, TN>& f, const float* As, const float* Bs, int q,
+                                          const int (&offa)[4][2], int nw) {
+  const float* ap = As + q * 32;                          // 8 units of 16 B per quad
+  const float* bp = Bs + (q >> 1) * nw * 8 + (q & 1) * 4;  // box q/2, half q%2
+#pragma unroll
+  for (int j = 0; j < TN; ++j) f.b[j] = *reinterpret_cast<const float4*>(bp + j * NG * 8);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    if constexpr (TM == 8) {
+      const float4 x = *reinterpret_cast<const float4*>(ap + offa[kk][0]);
+      const float4 y = *reinterpret_cast<const float4*>(ap + offa[kk][1]);
+      f.a[kk][0] = x.x; f.a[kk][1] = x.y; f.a[kk][2] = x.z; f.a[kk][3] = x.w;
+      f.a[kk][4] = y.x; f.a[kk][5] = y.y; f.a[kk][6] = y.z; f.a[kk][7] = y.w;
+    } else if constexpr (TM == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(ap + offa[kk][0]);
+      f.a[kk][0] = x.x; f.a[kk][1] = x.y; f.a[kk][2] = x.z; f.a[kk][3] = x.w;
+    } else {
+      const float2 x = *reinterpret_cast<const float2*>(ap + offa[kk][0]);
+      f.a[kk][0] = x.x; f.a[kk][1] = x.y;
+    }
+  }
+}
+
+template <int TM, int TN>
+__device__ __forceinline__ void fma_frag(float (&part)[TM][TN], const Frag<TM, TN>& f) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const float bk = kk == 0 ? f.b[j].x : kk == 1 ? f.b[j].y : kk == 2 ? f.b[j].z : f.b[j].w;
+#pragma unroll
+      for (int i = 0; i < TM; ++i) part[i][j] = fmaf(f.a[kk][i], bk, part[i][j]);
+    }
+}
+
+// Per-team context shared by the item routines.
+struct TeamCtx {
+  float* stages;       // the team's ring
+  int sf, D;           // floats per stage, ring depth
+  uint32_t full0, empty0;
+  int team, tt, lane;
+  bool leader;         // this warp issues the team's copies
+};
 
 // Runs one item (an h x nw tile, header already consumed): every chunk up to the next header or
 // the end of the stream, then stores the tile. Returns false on abort.
 template <int H, int NW, bool CHECK>
 __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, StreamWin& win,
-                                             const float* stages, int stage_floats, int D,
-                                             uint32_t full0, uint32_t empty0, int& s, uint32_t& ph,
-                                             int tt, int lane, volatile int* abort_flag) {
+                                             Issuer& is, const TeamCtx& c, int& s, uint32_t& ph,
+                                             volatile int* abort_flag) {
   constexpr TileCfg cfg = tile_cfg(H, NW);
   constexpr int TM = cfg.tm, TN = cfg.tn, RG = H / TM, NG = NW / TN;
+  const int tt = c.tt, lane = c.lane;
   const bool active = tt < cfg.threads;
   const int rg = tt % RG, ng = tt / RG;
   const int r0 = rg * TM, pnl = r0 >> 3, xf = panel_xor(pnl);
@@ -158,49 +289,30 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
     if (is_header(e)) break;
     win.advance(p.stream, lane);
     const int kc = chk_kc(e);
-    if (!wait_phase(full0 + 8u * s, ph, p, abort_flag, lane)) return false;
+    if (!wait_phase(c.full0 + 8u * s, ph, p, abort_flag, lane)) return false;
+    // keep the ring D-1 chunks ahead: the slot freed by the previous chunk gets the next copy
+    if (c.leader &&
+        !issue_next<CHECK>(p, is, c.stages, c.sf, c.D, c.full0, c.empty0, c.team, lane, abort_flag))
+      return false;
     if (active && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-      const float* As = stages + s * stage_floats + pnl * 8 * kc;
-      const float* Bs = stages + s * stage_floats + stage_b_offset(H) + ng * 8;
+      const float* As = c.stages + s * c.sf + pnl * 8 * kc;
+      const float* Bs = c.stages + s * c.sf + stage_b_offset(H) + ng * 8;
+      // Software-pipelined over k-quads: the operands of quad q+1 are loaded from shared memory
+      // while the FMAs of quad q run (two register fragments, alternating).
+      Frag<TM, TN> f0, f1;
+      const int nq = kc >> 2;  // even: kc is a multiple of 8
+      load_frag<TM, TN, NG>(f0, As, Bs, 0, offa, NW);
 #pragma unroll 1
-      for (int k8 = 0; k8 < kc; k8 += 8) {
-        const float* Ak = As + k8 * 8;
-        const float* Bk = Bs + k8 * NW;
-#pragma unroll
-        for (int kq = 0; kq < 8; kq += 4) {
-          float4 bv[TN];
-#pragma unroll
-          for (int j = 0; j < TN; ++j)
-            bv[j] = *reinterpret_cast<const float4*>(Bk + j * NG * 8 + kq);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            float a[TM];
-            const float* ap = Ak + kq * 8;
-            if constexpr (TM == 8) {
-              const float4 x = *reinterpret_cast<const float4*>(ap + offa[kk][0]);
-              const float4 y = *reinterpret_cast<const float4*>(ap + offa[kk][1]);
-              a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w;
-              a[4] = y.x; a[5] = y.y; a[6] = y.z; a[7] = y.w;
-            } else if constexpr (TM == 4) {
-              const float4 x = *reinterpret_cast<const float4*>(ap + offa[kk][0]);
-              a[0] = x.x; a[1] = x.y; a[2] = x.z; a[3] = x.w;
-            } else {
-              const float2 x = *reinterpret_cast<const float2*>(ap + offa[kk][0]);
-              a[0] = x.x; a[1] = x.y;
-            }
-#pragma unroll
-            for (int j = 0; j < TN; ++j) {
-              const float bk = kk == 0 ? bv[j].x : kk == 1 ? bv[j].y : kk == 2 ? bv[j].z : bv[j].w;
-#pragma unroll
-              for (int i = 0; i < TM; ++i) part[i][j] = fmaf(a[i], bk, part[i][j]);
-            }
-          }
-        }
+      for (int q = 0; q < nq; q += 2) {
+        load_frag<TM, TN, NG>(f1, As, Bs, q + 1, offa, NW);
+        fma_frag<TM, TN>(part, f0);
+        if (q + 2 < nq) load_frag<TM, TN, NG>(f0, As, Bs, q + 2, offa, NW);
+        fma_frag<TM, TN>(part, f1);
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8u * s);
-    if (++s == D) {
+    if (lane == 0) mbar_arrive(c.empty0 + 8u * s);
+    if (++s == c.D) {
       s = 0;
       ph ^= 1u;
     }
@@ -240,44 +352,58 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
 
 template <int RHS, int H, bool CHECK>
 __device__ __forceinline__ bool consume_h(const KernelParams& p, u64 hdr, StreamWin& win,
-                                          const float* stages, int sf, int D, uint32_t full0,
-                                          uint32_t empty0, int& s, uint32_t& ph, int tt, int lane,
+                                          Issuer& is, const TeamCtx& c, int& s, uint32_t& ph,
                                           volatile int* abort_flag) {
   constexpr int HALF = RHS > 8 ? RHS / 2 : RHS;
-  if (hdr_nw(hdr) == RHS)
-    return consume_item<H, RHS, CHECK>(p, hdr, win, stages, sf, D, full0, empty0, s, ph, tt, lane,
-                                       abort_flag);
-  return consume_item<H, HALF, CHECK>(p, hdr, win, stages, sf, D, full0, empty0, s, ph, tt, lane,
-                                      abort_flag);
+  if (hdr_nw(hdr) == RHS) return consume_item<H, RHS, CHECK>(p, hdr, win, is, c, s, ph, abort_flag);
+  return consume_item<H, HALF, CHECK>(p, hdr, win, is, c, s, ph, abort_flag);
 }
 
 template <int RHS, bool CHECK>
-__device__ void consumer(const KernelParams& p, const Task& task, const float* stages,
-                         uint32_t full_base, uint32_t empty_base, int warp, int lane,
-                         volatile int* abort_flag) {
+__device__ void run_team(const KernelParams& p, const Task& task, float* stages, uint32_t full_base,
+                         uint32_t empty_base, int warp, int lane, volatile int* abort_flag) {
   const int tw = task.team_warps;
-  const int team = warp / tw;
-  const int tt = (warp % tw) * 32 + lane;
-  const uint32_t full0 = full_base + 8u * (team * kMaxStages);
-  const uint32_t empty0 = empty_base + 8u * (team * kMaxStages);
-  const float* my_stages = stages + team * task.stages * task.stage_floats;
+  TeamCtx c;
+  c.team = warp / tw;
+  c.tt = (warp % tw) * 32 + lane;
+  c.lane = lane;
+  c.leader = (warp % tw) == 0;
+  c.D = task.stages;
+  c.sf = task.stage_floats;
+  c.full0 = full_base + 8u * (c.team * kMaxStages);
+  c.empty0 = empty_base + 8u * (c.team * kMaxStages);
+  c.stages = stages + c.team * c.D * c.sf;
+  const int b = task.team_off[c.team], e = task.team_off[c.team + 1];
   StreamWin win;
-  win.init(p.stream, task.team_off[team], task.team_off[team + 1], lane);
+  win.init(p.stream, b, e, lane);
+  Issuer is;
+  is.h = 8;
+  is.n0 = 0;
+  is.nw = 8;
+  is.slot = 0;
+  is.ph = 0;
+  is.filled = is.lastpar = 0;
+  is.issued = 0;
+  bool ok = true;
+  if (c.leader) {
+    is.win.init(p.stream, b, e, lane);
+    for (int i = 0; i < c.D - 1 && ok; ++i)
+      ok = issue_next<CHECK>(p, is, c.stages, c.sf, c.D, c.full0, c.empty0, c.team, lane,
+                             abort_flag);
+  }
   int s = 0;
   uint32_t ph = 0;
-  while (!win.done()) {
+  while (ok && !win.done()) {
     const u64 hdr = win.peek();
     win.advance(p.stream, lane);
     if (!is_header(hdr)) {  // malformed stream: a chunk without a header
       if (lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, win.pos);
       break;
     }
-    bool ok = true;
     switch (hdr_h(hdr)) {
-#define VBSR_CASE_H(HH)                                                                          \
-  case HH:                                                                                       \
-    ok = consume_h<RHS, HH, CHECK>(p, hdr, win, my_stages, task.stage_floats, task.stages, full0, \
-                                   empty0, s, ph, tt, lane, abort_flag);                         \
+#define VBSR_CASE_H(HH)                                                \
+  case HH:                                                             \
+    ok = consume_h<RHS, HH, CHECK>(p, hdr, win, is, c, s, ph, abort_flag); \
     break;
       VBSR_CASE_H(8)
       VBSR_CASE_H(16)
@@ -289,126 +415,16 @@ __device__ void consumer(const KernelParams& p, const Task& task, const float* s
       VBSR_CASE_H(64)
 #undef VBSR_CASE_H
     }
-    if (!ok) break;
   }
-}
-
-// ---- producer ------------------------------------------------------------------------------------
-
-// Current item of a team as seen by the producer.
-struct ProdItem {
-  int h, n0, nw;
-};
-
-// Producer warp `pw` serves teams pw, pw + kProducerWarps, ... (NT of them).
-template <int NT, bool CHECK>
-__device__ void producer(const KernelParams& p, const Task& task, float* stages, uint32_t full_base,
-                         uint32_t empty_base, int pw, int lane, volatile int* abort_flag) {
-  const int D = task.stages;
-  const int sf = task.stage_floats;
-  const uint64_t pol_a = policy_evict_first();
-  const uint64_t pol_b = policy_evict_last();
-  StreamWin win[NT];
-  ProdItem it[NT];
-  int slot[NT];
-  uint32_t phase[NT], filled[NT], lastpar[NT];
-  uint32_t live = 0;
-#pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    const int team = pw + j * kProducerWarps;
-    win[j].init(p.stream, task.team_off[team], task.team_off[team + 1], lane);
-    it[j] = ProdItem{8, 0, 8};
-    slot[j] = 0;
-    phase[j] = filled[j] = lastpar[j] = 0;
-    if (!win[j].done()) live |= 1u << j;
-  }
-  int issued0 = 0;  // chunks issued for team 0 (debug drop hook)
-  int j = 0;
-  while (live) {
-    // next live team, round robin
-    while (!(live & (1u << j))) j = (j + 1 == NT) ? 0 : j + 1;
-    bool stop = false;
-#pragma unroll
-    for (int jj = 0; jj < NT; ++jj) {
-      if (jj != j) continue;  // static indexing of the per-team registers
-      // Headers need no stage: take them as they come.
-      u64 e = win[jj].peek();
-      while (is_header(e)) {
-        it[jj].h = hdr_h(e);
-        it[jj].n0 = hdr_n0(e);
-        it[jj].nw = hdr_nw(e);
-        win[jj].advance(p.stream, lane);
-        if (win[jj].done()) break;
-        e = win[jj].peek();
-      }
-      if (win[jj].done()) {
-        live &= ~(1u << jj);
-        break;
-      }
-      const int s = slot[jj];
-      const int team = pw + jj * kProducerWarps;
-      const uint32_t empty_bar = empty_base + 8u * (team * kMaxStages + s);
-      const uint32_t full_bar = full_base + 8u * (team * kMaxStages + s);
-      if (!wait_phase(empty_bar, phase[jj] ^ 1u, p, abort_flag, lane)) {
-        stop = true;
-        break;
-      }
-      const long long val = chk_val(e), colk = chk_colk(e);
-      const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
-      const int h = it[jj].h, nw = it[jj].nw, n0 = it[jj].n0;
-      const bool drop = (team == 0 && issued0 == p.drop_stage);
-      if (team == 0) ++issued0;
-      bool in_bounds = true;
-      if (CHECK)
-        in_bounds = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K &&
-                    n0 + nw <= p.rhs;
-      if (drop) {
-        // withhold the stage entirely (debug): no arrival, no copies
-      } else if (p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) {
-        if (lane == 0) mbar_arrive(full_bar);
-      } else if (!in_bounds) {
-        if (lane == 0) {
-          record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
-          mbar_arrive(full_bar);  // release the consumers without touching memory
-        }
-      } else {
-        float* st = stages + (team * D + s) * sf;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
-          bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc),
-                   full_bar, pol_a);
-        } else if (lane <= (kc >> 3)) {
-          const int g = lane - 1;
-          const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
-          tensor2d_g2s(smem_addr(st + stage_b_offset(h) + g * nw * 8), map, int(colk) + 8 * g, n0,
-                       full_bar, pol_b);
-        }
-        filled[jj] |= 1u << s;
-        lastpar[jj] = (lastpar[jj] & ~(1u << s)) | (phase[jj] << s);
-      }
-      if (++slot[jj] == D) {
-        slot[jj] = 0;
-        phase[jj] ^= 1u;
-      }
-      win[jj].advance(p.stream, lane);
-      if (win[jj].done()) live &= ~(1u << jj);
-    }
-    if (stop) break;
-    j = (j + 1 == NT) ? 0 : j + 1;
-  }
-  __syncwarp();
-  // After an abort, wait (bounded) for the last fill of every slot so that no bulk copy is still
-  // writing this CTA's shared memory when it exits.
-  if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      for (int s = 0; s < D; ++s) {
-        if (!(filled[j] & (1u << s))) continue;
-        const uint32_t bar = full_base + 8u * ((pw + j * kProducerWarps) * kMaxStages + s);
-        const uint32_t par = (lastpar[j] >> s) & 1u;
-        const long long t0 = clock64();
-        while (!mbar_try(bar, par) && clock64() - t0 < p.wait_limit) {
-        }
+  // After an abort, wait (bounded) for the last fill of every slot this leader issued so that no
+  // bulk copy is still writing the CTA's shared memory when it exits.
+  if (c.leader && __shfl_sync(0xffffffffu, *abort_flag, 0)) {
+    for (int sl = 0; sl < c.D; ++sl) {
+      if (!(is.filled & (1u << sl))) continue;
+      const uint32_t bar = c.full0 + 8u * sl;
+      const uint32_t par = (is.lastpar >> sl) & 1u;
+      const long long t0 = clock64();
+      while (!mbar_try(bar, par) && clock64() - t0 < p.wait_limit) {
       }
     }
   }
@@ -447,21 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) spmm_kernel(const __grid_constant
     mbar_fence_init();
   }
   __syncthreads();
-  volatile int* abort_v = &abort_flag;
-
-  if (warp < kProducerWarps) {
-    regs_dec<kProducerRegs>();
-    if (tw == 1)
-      producer<2, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
-    else if (tw == 2)
-      producer<1, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
-    else if (warp < 2)
-      producer<1, CHECK>(p, task, stages, full_base, empty_base, warp, lane, abort_v);
-  } else {
-    regs_inc<kConsumerRegs>();
-    consumer<RHS, CHECK>(p, task, stages, full_base, empty_base, warp - kProducerWarps, lane,
-                         abort_v);
-  }
+  run_team<RHS, CHECK>(p, task, stages, full_base, empty_base, warp, lane, &abort_flag);
   __syncthreads();
   if (threadIdx.x == 0 && p.timing) p.timing[2 * blockIdx.x + 1] = global_ns();
 }

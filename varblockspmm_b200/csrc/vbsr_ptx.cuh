@@ -73,16 +73,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
-// Warpgroup register reallocation (all threads of the warpgroup execute it).
-template <int N>
-__device__ __forceinline__ void regs_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
-}
-template <int N>
-__device__ __forceinline__ void regs_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
-}
-
 // 2-D tensor TMA load (box from a tensor map) into shared memory, completion on `bar`.
 // x must be a multiple of 4 for 32-bit elements (16-byte aligned start).
 __device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const void* tmap, int x, int y,

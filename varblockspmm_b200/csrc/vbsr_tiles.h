@@ -27,11 +27,8 @@
 
 namespace vbsr_b200 {
 
-constexpr int kConsumerWarps = 8;                 // compute warps per CTA (two warpgroups)
-constexpr int kProducerWarps = 4;                 // one warpgroup of TMA producers
-constexpr int kThreads = 32 * (kConsumerWarps + kProducerWarps);
-constexpr int kProducerRegs = 56;                 // setmaxnreg split of the 168 registers per
-constexpr int kConsumerRegs = 224;                // thread the CTA launches with (12 warps)
+constexpr int kConsumerWarps = 8;                 // warps per CTA (all compute; team leaders
+constexpr int kThreads = 32 * kConsumerWarps;     // also issue their team's TMA copies)
 constexpr int kChunk = 32;                        // block columns per pipeline stage
 constexpr int kMaxStages = 4;
 
