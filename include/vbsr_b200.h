@@ -147,6 +147,7 @@ enum { VBSR_KERNEL_AUTO = 0, VBSR_KERNEL_ROW_OWNED = 1, VBSR_KERNEL_SPLIT_ROW = 
 enum {
   VBSR_PLAN_BOUNDS_CHECK = 1u << 0, /* use the bounds-checked kernel build                  */
   VBSR_PLAN_NO_SPLIT = 1u << 1,     /* never split heavy block rows into column halves      */
+  VBSR_PLAN_NARROW_STAGES = 1u << 2, /* pipeline stages of 32 block columns (default: up to 64) */
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
   VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9    /* consumers wait for the data but compute nothing     */

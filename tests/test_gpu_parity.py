@@ -99,8 +99,10 @@ def test_bounds_checked_build_and_no_split(cuda, rhs):
     a = run_plan(cuda, host, B, rhs)
     b = run_plan(cuda, host, B, rhs, flags=vb.PLAN_BOUNDS_CHECK)
     c = run_plan(cuda, host, B, rhs, flags=vb.PLAN_NO_SPLIT)
+    d = run_plan(cuda, host, B, rhs, flags=vb.PLAN_NARROW_STAGES)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     assert_within_bound(host, B, rhs, c)
+    assert_within_bound(host, B, rhs, d)
 
 
 def _handmade(heights, widths, rows_cols, seed=0):

@@ -22,7 +22,8 @@ from dataclasses import dataclass
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libvbsr_b200.so")
+# VBSR_B200_LIB overrides the library path (for A/B comparisons of alternative builds).
+LIB_PATH = os.environ.get("VBSR_B200_LIB") or os.path.join(_HERE, "libvbsr_b200.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(
@@ -162,6 +163,7 @@ STREAM_VALUES = 0xA11CE
 STREAM_DENSE = 0xB0B
 PLAN_BOUNDS_CHECK = 1
 PLAN_NO_SPLIT = 2
+PLAN_NARROW_STAGES = 4
 PLAN_DIAG_SKIP_COPIES = 1 << 8  # diagnostics only: C is wrong
 PLAN_DIAG_SKIP_MATH = 1 << 9    # diagnostics only: C is wrong
 

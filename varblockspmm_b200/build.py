@@ -20,7 +20,8 @@ CXXLIB = os.path.join(HERE, "libvbsr_b200_cxx.so")
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
+COMMON = [*os.environ.get("VBSR_EXTRA_FLAGS", "").split(),
+          "-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
           "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 
 SOURCES = ["vbsr_host.cpp", "vbsr_device.cu"]

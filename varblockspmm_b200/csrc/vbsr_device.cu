@@ -531,7 +531,18 @@ vbsr_status build_schedule(vbsr_plan* p) {
     }
     for (int t = 0; t < ctas[c]; ++t) {
       Task task{};
-      int sf = 32;
+      // Stage width: 64 block columns when two such stages per team fit, else 32.
+      int sf64 = 256, sf32 = 256;
+      for (int j = 0; j < nt; ++j)
+        for (int k : lists[t * nt + j]) {
+          const int h = d.h_row_size[items[k].row];
+          sf64 = std::max(sf64, stage_floats(h, items[k].nw, 64));
+          sf32 = std::max(sf32, stage_floats(h, items[k].nw, 32));
+        }
+      const bool wide = (p->flags & VBSR_PLAN_NARROW_STAGES) == 0 &&
+                        2 * nt * sf64 * 4 <= kSmemBudget;
+      const int cols = wide ? 64 : 32;
+      const int sf = wide ? sf64 : sf32;
       for (int j = 0; j < nt; ++j) {
         task.team_off[j] = int(stream.size());
         std::vector<int>& l = lists[t * nt + j];
@@ -543,23 +554,31 @@ vbsr_status build_schedule(vbsr_plan* p) {
           const Cand& it = items[k];
           const int i = it.row, h = d.h_row_size[i];
           stream.push_back(entry::header(d.h_row_off[i], h, it.n0, it.nw));
+          // Chunks packed greedily into stages of `cols` columns; a chunk never straddles two.
           int64_t val = d.h_val_off_row[i];
+          int used = 0;
           for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
             const uint32_t desc = d.h_blk_desc[b];
             const int w = int((desc & 7u) + 1u) * 8;
             const int64_t col = int64_t(desc & ~7u);
             for (int k0 = 0; k0 < w; k0 += kChunk) {
               const int kc = std::min(kChunk, w - k0);
-              stream.push_back(entry::chunk(val, col, w, k0, kc, k0 + kc == w));
+              if (used + kc > cols) {
+                stream.back() |= entry::kLastOfStage;
+                used = 0;
+              }
+              stream.push_back(entry::chunk(val, col, w, k0, kc, false));
+              used += kc;
             }
             val += int64_t(h) * w;
           }
-          sf = std::max(sf, stage_floats(h, it.nw));
+          if (used > 0) stream.back() |= entry::kLastOfStage;
         }
       }
       for (int j = nt; j <= kConsumerWarps; ++j) task.team_off[j] = int(stream.size());
       task.team_warps = tw;
       task.stage_floats = sf;
+      task.stage_cols = cols;
       const int stages = std::min(kMaxStages, kSmemBudget / (nt * sf * 4));
       if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
       task.stages = stages;

@@ -21,13 +21,15 @@ void clear_error();
 //
 // Header (bit 63 = 1): an h x nw tile of C starting at scalar row c_row, RHS columns [n0, n0+nw)
 //   bits  0..30 c_row       bits 31..33 h/8 - 1      bits 34..36 n0/8     bits 37..38 log2(nw/8)
-// Chunk  (bit 63 = 0): block columns [k0, k0+kc) of one block of that item
+// Chunk  (bit 63 = 0): block columns [k0, k0+kc) of one block of that item (one contiguous k-chunk
+// of the device value format, kc <= 32). Consecutive chunks of an item are packed into one
+// pipeline stage of up to Task::stage_cols columns; bit 62 marks the last chunk of a stage.
 //   bits  0..27 val/64  (value offset of the block; blocks start at multiples of 64 floats)
 //   bits 28..55 (col + k0)/8   (first scalar column of the chunk in B)
-//   bits 56..58 w/8 - 1        bit 59 k0/32     bits 60..61 kc/8 - 1     bit 62 last chunk of block
+//   bits 56..58 w/8 - 1        bit 59 k0/32     bits 60..61 kc/8 - 1     bit 62 last chunk of stage
 namespace entry {
 constexpr uint64_t kHeader = 1ull << 63;
-constexpr uint64_t kLastOfBlock = 1ull << 62;
+constexpr uint64_t kLastOfStage = 1ull << 62;
 inline uint64_t header(int64_t c_row, int h, int n0, int nw) {
   int lg = 0;
   while ((8 << lg) < nw) ++lg;
@@ -36,7 +38,7 @@ inline uint64_t header(int64_t c_row, int h, int n0, int nw) {
 }
 inline uint64_t chunk(int64_t val, int64_t col, int w, int k0, int kc, bool last) {
   return uint64_t(val / 64) | (uint64_t((col + k0) / 8) << 28) | (uint64_t(w / 8 - 1) << 56) |
-         (uint64_t(k0 / 32) << 59) | (uint64_t(kc / 8 - 1) << 60) | (last ? kLastOfBlock : 0);
+         (uint64_t(k0 / 32) << 59) | (uint64_t(kc / 8 - 1) << 60) | (last ? kLastOfStage : 0);
 }
 constexpr int64_t kMaxVal = (int64_t(1) << 28) * 64;  // value offsets must stay below this
 constexpr int64_t kMaxCol = (int64_t(1) << 28) * 8;
@@ -49,8 +51,10 @@ struct alignas(16) Task {
   int team_warps;     // 1, 2 or 4
   int stages;         // ring depth per team
   int stage_floats;   // floats per stage
+  int stage_cols;     // block columns one stage holds (32 or 64)
+  int pad[3];
 };
-static_assert(sizeof(Task) == 48, "Task layout");
+static_assert(sizeof(Task) == 64, "Task layout");
 
 // Per-block descriptor: col_scalar_off | (w/8 - 1); col_scalar_off is a multiple of 8 so its low
 // three bits are free.

@@ -69,7 +69,7 @@ __device__ __forceinline__ long long chk_colk(u64 e) { return (long long)((e >> 
 __device__ __forceinline__ int chk_w(u64 e) { return int(((e >> 56) & 7u) + 1u) * 8; }
 __device__ __forceinline__ int chk_k0(u64 e) { return int((e >> 59) & 1u) * 32; }
 __device__ __forceinline__ int chk_kc(u64 e) { return int(((e >> 60) & 3u) + 1u) * 8; }
-__device__ __forceinline__ bool chk_last(u64 e) { return ((e >> 62) & 1u) != 0; }
+__device__ __forceinline__ bool chk_stage_end(u64 e) { return ((e >> 62) & 1u) != 0; }
 
 // A team stream [pos, end) seen through a window of 32 entries (lane i holds entry wbase + i) and
 // the following window, loaded one window ahead. All lanes keep identical pos/wbase/end.
@@ -109,6 +109,16 @@ __device__ __forceinline__ void record_status(int* status, int code, int info) {
 // exceeded p.wait_limit SM clocks.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const KernelParams& p,
                                            volatile int* abort_flag, int lane) {
+#ifdef VBSR_WAIT_LANE0
+  {
+    int ok = 0;
+    if (lane == 0) ok = mbar_try(bar, parity);
+    if (__shfl_sync(0xffffffffu, ok, 0)) {
+      __syncwarp();
+      return true;
+    }
+  }
+#endif
   if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
   const long long t0 = clock64();
   while (true) {
@@ -144,8 +154,9 @@ struct Issuer {
 // the team has released that slot). Warp-collective. Returns false on abort.
 template <bool CHECK>
 __device__ __forceinline__ bool issue_next(const KernelParams& p, Issuer& is, float* team_stages,
-                                           int sf, int D, uint32_t full0, uint32_t empty0,
-                                           int team, int lane, volatile int* abort_flag) {
+                                           int sf, int D, int cols, uint32_t full0,
+                                           uint32_t empty0, int team, int lane,
+                                           volatile int* abort_flag) {
   while (!is.win.done()) {
     const u64 e = is.win.peek();
     if (!is_header(e)) break;
@@ -155,47 +166,55 @@ __device__ __forceinline__ bool issue_next(const KernelParams& p, Issuer& is, fl
     is.win.advance(p.stream, lane);
   }
   if (is.win.done()) return true;
-  const u64 e = is.win.peek();
   const int s = is.slot;
   const uint32_t full_bar = full0 + 8u * s;
   if (!wait_phase(empty0 + 8u * s, is.ph ^ 1u, p, abort_flag, lane)) return false;
-  const long long val = chk_val(e), colk = chk_colk(e);
-  const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
   const int h = is.h, nw = is.nw, n0 = is.n0;
   const bool drop = (team == 0 && is.issued == p.drop_stage);
   ++is.issued;
+  float* st = team_stages + s * sf;
+  const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
+  const bool copy = !drop && !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES);
   bool in_bounds = true;
-  if (CHECK)
-    in_bounds = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K && n0 + nw <= p.rhs;
-  if (drop) {
-    // withhold the stage entirely (debug): no arrival, no copies
-  } else if (p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) {
-    if (lane == 0) mbar_arrive(full_bar);
-  } else if (!in_bounds) {
-    if (lane == 0) {
-      record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
-      mbar_arrive(full_bar);  // release the consumers without touching memory
+  int c0 = 0;
+  while (!is.win.done()) {  // the stage's chunks (ends at a stage-end mark)
+    const u64 e = is.win.peek();
+    is.win.advance(p.stream, lane);
+    const long long val = chk_val(e), colk = chk_colk(e);
+    const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
+    bool ok = true;
+    if (CHECK)
+      ok = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K && n0 + nw <= p.rhs &&
+           c0 + kc <= cols;
+    in_bounds = in_bounds && ok;
+    if (copy && ok) {
+      if (lane == 0) {
+        mbar_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
+        bulk_g2s(smem_addr(st + h * c0), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc),
+                 full_bar, policy_evict_first());
+      } else if (lane <= (kc >> 3)) {
+        const int g = lane - 1;
+        tensor2d_g2s(smem_addr(st + stage_b_offset(h, cols) + ((c0 >> 3) + g) * nw * 8), map,
+                     int(colk) + 8 * g, n0, full_bar, policy_evict_last());
+      }
     }
-  } else {
-    float* st = team_stages + s * sf;
+    c0 += kc;
+    if (chk_stage_end(e)) break;
+  }
+  if (!drop) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
-      bulk_g2s(smem_addr(st), p.values + val + (long long)h * k0, uint32_t(h * 4 * kc), full_bar,
-               policy_evict_first());
-    } else if (lane <= (kc >> 3)) {
-      const int g = lane - 1;
-      const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
-      tensor2d_g2s(smem_addr(st + stage_b_offset(h) + g * nw * 8), map, int(colk) + 8 * g, n0,
-                   full_bar, policy_evict_last());
+      if (!in_bounds) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+      mbar_arrive(full_bar);  // the stage's bytes were announced chunk by chunk
     }
-    is.filled |= 1u << s;
-    is.lastpar = (is.lastpar & ~(1u << s)) | (is.ph << s);
+    if (copy) {
+      is.filled |= 1u << s;
+      is.lastpar = (is.lastpar & ~(1u << s)) | (is.ph << s);
+    }
   }
   if (++is.slot == D) {
     is.slot = 0;
     is.ph ^= 1u;
   }
-  is.win.advance(p.stream, lane);
   return true;
 }
 
@@ -249,7 +268,7 @@ __device__ __forceinline__ void fma_frag(float (&part)[TM][TN], const Frag<TM, T
 // Per-team context shared by the item routines.
 struct TeamCtx {
   float* stages;       // the team's ring
-  int sf, D;           // floats per stage, ring depth
+  int sf, D, cols;     // floats per stage, ring depth, block columns per stage
   uint32_t full0, empty0;
   int team, tt, lane;
   bool leader;         // this warp issues the team's copies
@@ -285,45 +304,51 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
     for (int j = 0; j < TN; ++j) acc[i][j] = part[i][j] = 0.0f;
 
   while (!win.done()) {
-    const u64 e = win.peek();
-    if (is_header(e)) break;
-    win.advance(p.stream, lane);
-    const int kc = chk_kc(e);
+    if (is_header(win.peek())) break;
     if (!wait_phase(c.full0 + 8u * s, ph, p, abort_flag, lane)) return false;
-    // keep the ring D-1 chunks ahead: the slot freed by the previous chunk gets the next copy
-    if (c.leader &&
-        !issue_next<CHECK>(p, is, c.stages, c.sf, c.D, c.full0, c.empty0, c.team, lane, abort_flag))
+    // keep the ring D-1 stages ahead: the slot freed by the previous stage gets the next copies
+    if (c.leader && !issue_next<CHECK>(p, is, c.stages, c.sf, c.D, c.cols, c.full0, c.empty0,
+                                       c.team, lane, abort_flag))
       return false;
-    if (active && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-      const float* As = c.stages + s * c.sf + pnl * 8 * kc;
-      const float* Bs = c.stages + s * c.sf + stage_b_offset(H) + ng * 8;
-      // Software-pipelined over k-quads: the operands of quad q+1 are loaded from shared memory
-      // while the FMAs of quad q run (two register fragments, alternating).
-      Frag<TM, TN> f0, f1;
-      const int nq = kc >> 2;  // even: kc is a multiple of 8
-      load_frag<TM, TN, NG>(f0, As, Bs, 0, offa, NW);
+    const float* stage = c.stages + s * c.sf;
+    int c0 = 0;
+    while (!win.done()) {  // the stage's chunks
+      const u64 e = win.peek();
+      win.advance(p.stream, lane);
+      const int kc = chk_kc(e);
+      if (active && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+        const float* As = stage + H * c0 + pnl * 8 * kc;
+        const float* Bs = stage + stage_b_offset(H, c.cols) + (c0 >> 3) * NW * 8 + ng * 8;
+        // Software-pipelined over k-quads: the operands of quad q+1 are loaded from shared
+        // memory while the FMAs of quad q run (two register fragments, alternating).
+        Frag<TM, TN> f0, f1;
+        const int nq = kc >> 2;  // even: kc is a multiple of 8
+        load_frag<TM, TN, NG>(f0, As, Bs, 0, offa, NW);
 #pragma unroll 1
-      for (int q = 0; q < nq; q += 2) {
-        load_frag<TM, TN, NG>(f1, As, Bs, q + 1, offa, NW);
-        fma_frag<TM, TN>(part, f0);
-        if (q + 2 < nq) load_frag<TM, TN, NG>(f0, As, Bs, q + 2, offa, NW);
-        fma_frag<TM, TN>(part, f1);
+        for (int q = 0; q < nq; q += 2) {
+          load_frag<TM, TN, NG>(f1, As, Bs, q + 1, offa, NW);
+          fma_frag<TM, TN>(part, f0);
+          if (q + 2 < nq) load_frag<TM, TN, NG>(f0, As, Bs, q + 2, offa, NW);
+          fma_frag<TM, TN>(part, f1);
+        }
       }
+      c0 += kc;
+      if (chk_k0(e) + kc == chk_w(e)) {  // block done: fold its partial sums in
+#pragma unroll
+        for (int i = 0; i < TM; ++i)
+#pragma unroll
+          for (int j = 0; j < TN; ++j) {
+            acc[i][j] += part[i][j];
+            part[i][j] = 0.0f;
+          }
+      }
+      if (chk_stage_end(e)) break;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(c.empty0 + 8u * s);
     if (++s == c.D) {
       s = 0;
       ph ^= 1u;
-    }
-    if (chk_last(e)) {
-#pragma unroll
-      for (int i = 0; i < TM; ++i)
-#pragma unroll
-        for (int j = 0; j < TN; ++j) {
-          acc[i][j] += part[i][j];
-          part[i][j] = 0.0f;
-        }
     }
   }
 
@@ -370,6 +395,7 @@ __device__ void run_team(const KernelParams& p, const Task& task, float* stages,
   c.leader = (warp % tw) == 0;
   c.D = task.stages;
   c.sf = task.stage_floats;
+  c.cols = task.stage_cols;
   c.full0 = full_base + 8u * (c.team * kMaxStages);
   c.empty0 = empty_base + 8u * (c.team * kMaxStages);
   c.stages = stages + c.team * c.D * c.sf;
@@ -388,7 +414,7 @@ __device__ void run_team(const KernelParams& p, const Task& task, float* stages,
   if (c.leader) {
     is.win.init(p.stream, b, e, lane);
     for (int i = 0; i < c.D - 1 && ok; ++i)
-      ok = issue_next<CHECK>(p, is, c.stages, c.sf, c.D, c.full0, c.empty0, c.team, lane,
+      ok = issue_next<CHECK>(p, is, c.stages, c.sf, c.D, c.cols, c.full0, c.empty0, c.team, lane,
                              abort_flag);
   }
   int s = 0;

@@ -14,9 +14,10 @@
 // and the XOR makes the consumers' 16-byte reads of different panels at the same column fall into
 // different shared-memory bank groups (for both 8-row and 4-row thread tiles).
 //
-// Pipeline stage (one k-chunk of one block of one item): the A chunk as stored (h*kc floats)
-// followed, at offset h*32 floats, by the B chunk: kc/8 boxes of 8 columns x nw rows, each row of
-// a box 8 consecutive floats of one RHS column (written by 2-D tensor TMA, no swizzle).
+// Pipeline stage: consecutive k-chunks of one item, packed up to `cols` (32 or 64) block columns.
+// A chunk starting at stage column c0 keeps its stored layout at offset h*c0 floats; the B part
+// starts at h*cols floats and holds one box per 8 stage columns (box c0/8 + g at (c0/8+g)*nw*8),
+// each box nw rows of 8 consecutive floats of one RHS column (2-D tensor TMA, no swizzle).
 #pragma once
 
 #if defined(__CUDACC__)
@@ -29,7 +30,8 @@ namespace vbsr_b200 {
 
 constexpr int kConsumerWarps = 8;                 // warps per CTA (all compute; team leaders
 constexpr int kThreads = 32 * kConsumerWarps;     // also issue their team's TMA copies)
-constexpr int kChunk = 32;                        // block columns per pipeline stage
+constexpr int kChunk = 32;                        // block columns per device k-chunk
+constexpr int kMaxStageCols = 64;                 // block columns per pipeline stage (max)
 constexpr int kMaxStages = 4;
 
 struct TileCfg {
@@ -67,10 +69,10 @@ VBSR_HD int blk_pos(int h, int w, int r, int k) {
   return h * k0 + p * 8 * kc + ((q ^ panel_xor(p)) << 2) + (r & 3);
 }
 
-// Floats of one stage for an (h, nw) item, rounded to 1 KB.
-VBSR_HD int stage_floats(int h, int nw) { return (h * 32 + nw * 32 + 255) / 256 * 256; }
+// Floats of one stage of `cols` block columns for an (h, nw) item, rounded to 1 KB.
+VBSR_HD int stage_floats(int h, int nw, int cols) { return ((h + nw) * cols + 255) / 256 * 256; }
 
-// Offset (floats) of the B boxes inside a stage.
-VBSR_HD int stage_b_offset(int h) { return h * 32; }
+// Offset (floats) of the B boxes inside a stage of `cols` columns.
+VBSR_HD int stage_b_offset(int h, int cols) { return h * cols; }
 
 }  // namespace vbsr_b200
