@@ -168,6 +168,23 @@ vbsr_status vbsr_plan_destroy(vbsr_plan* p);
  * differ. Launch failures return VBSR_CUDA_ERROR (cudaGetLastError right after the launch). */
 vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr_stream_t stream);
 
+/* Same computation as vbsr_plan_execute, for callers that must not have device memory allocated
+ * on their behalf (hosts that own every device allocation, or paths where the implicit device
+ * synchronisation of cudaMalloc/cudaFree is not allowed). No reference counterpart: the reference
+ * has no such entry point. It calls no cudaMalloc, cudaFree or other allocating routine; the
+ * kernel's status words and per-CTA timestamps live instead in one fixed array compiled into the
+ * library (16 KB per GPU, kept until the process exits), and plans of more than 1024 CTAs are
+ * rejected with VBSR_INVALID_ARGUMENT. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream capture. Each call clears
+ * the array's used part first, and all calls share it, so calls that overlap on the GPU race on it
+ * (their C results are unaffected, only the reported status/timestamps). With cta_times == NULL the
+ * call is asynchronous like vbsr_plan_execute; otherwise it synchronises `stream`, copies up to
+ * cta_times_len timestamps ((start, end) pairs in ns, per CTA) and returns VBSR_TIMEOUT or
+ * VBSR_BOUNDS_VIOLATION if the kernel recorded one. */
+vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float* C,
+                                      vbsr_stream_t stream, uint64_t* cta_times,
+                                      int cta_times_len);
+
 /* Plan::launch_count (plan.cpp:23-31): kernel launches per execute (always 1 here). */
 vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out);
 

@@ -136,6 +136,7 @@ _sig = {
     "vbsr_plan_destroy": [_vp],
     "vbsr_plan_execute": [_vp, _vp, _vp, _vp],
     "vbsr_plan_launch_count": [_vp, C.POINTER(C.c_int)],
+    "vbsr_plan_execute_noalloc": [_vp, _vp, _vp, _vp, C.POINTER(C.c_uint64), C.c_int],
     "vbsr_plan_check_status": [_vp, _vp],
     "vbsr_plan_describe": [_vp, C.c_char_p, C.c_size_t],
     "vbsr_plan_set_debug": [_vp, C.c_int, C.c_int64],
@@ -447,6 +448,22 @@ class Plan:
     def execute(self, B, C_out, stream=None):
         """Enqueues C = A * B on `stream` (asynchronous, allocation-free)."""
         _check(_lib.vbsr_plan_execute(self._h, _dev_ptr(B), _dev_ptr(C_out), _stream_ptr(stream)))
+
+    def execute_noalloc(self, B, C_out, stream=None, report: bool = False):
+        """Like execute, but allocates nothing: status words and CTA timestamps live in a fixed
+        array inside the library (see vbsr_plan_execute_noalloc). With report=True, waits for the
+        launch, raises on a recorded timeout or bounds violation, and returns the (start, end)
+        timestamps per CTA."""
+        if not report:
+            _check(_lib.vbsr_plan_execute_noalloc(self._h, _dev_ptr(B), _dev_ptr(C_out),
+                                                  _stream_ptr(stream), None, 0))
+            return None
+        n = self.num_tasks()
+        out = np.zeros(2 * n, dtype=np.uint64)
+        _check(_lib.vbsr_plan_execute_noalloc(self._h, _dev_ptr(B), _dev_ptr(C_out),
+                                              _stream_ptr(stream),
+                                              out.ctypes.data_as(C.POINTER(C.c_uint64)), 2 * n))
+        return out.reshape(n, 2)
 
     def launch_count(self) -> int:
         n = C.c_int()

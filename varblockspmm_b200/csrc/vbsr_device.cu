@@ -816,6 +816,113 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   return VBSR_OK;
 }
 
+// ---- execute without allocating ---------------------------------------------------------------------
+//
+// vbsr_plan_execute keeps the kernel's status word (and, when timing is switched on, its per-CTA
+// timestamps) in device memory that the plan allocated with cudaMalloc. Some callers are not
+// allowed to have device memory allocated on their behalf at all: code running inside a host
+// framework that owns every device allocation (serving runtimes with their own pool, plugins whose
+// host forbids cudaMalloc/cudaFree because they synchronise the device), or code paths that must
+// never trigger an implicit device synchronisation. For them, vbsr_plan_execute_noalloc below keeps
+// that scratch in one fixed array compiled into this library instead.
+//
+// Layout of the array: words 0..1 hold the kernel's status words (four 32-bit values), followed by
+// one (start, end) pair of 64-bit timestamps per CTA, for at most kNoAllocMaxCtas CTAs (16 KB in
+// total). Every GPU that loads this library holds the array until the process exits.
+constexpr int kNoAllocMaxCtas = 1024;
+static __device__ __align__(256) unsigned long long g_noalloc_scratch[2 + 2 * kNoAllocMaxCtas];
+
+namespace {
+// Device address of g_noalloc_scratch, looked up once per device. In host code the symbol's name
+// is only a host-side stand-in, so the address must come from cudaGetSymbolAddress with that
+// device current.
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+unsigned long long* g_noalloc_ptr[kMaxDevices] = {};
+
+vbsr_status noalloc_scratch(int device, unsigned long long** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return set_error(VBSR_INVALID_ARGUMENT, "device ordinal out of range for the static scratch");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e));
+    g_noalloc_ptr[device] = static_cast<unsigned long long*>(ptr);
+  }
+  *out = g_noalloc_ptr[device];
+  return VBSR_OK;
+}
+}  // namespace
+
+vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float* C,
+                                      vbsr_stream_t stream, uint64_t* cta_times,
+                                      int cta_times_len) {
+  clear_error();
+  if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
+  if (B == nullptr || C == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null B or C");
+  if (p->num_tasks > kNoAllocMaxCtas)
+    return set_error(VBSR_INVALID_ARGUMENT,
+                     "plan launches " + std::to_string(p->num_tasks) +
+                         " CTAs; vbsr_plan_execute_noalloc supports at most " +
+                         std::to_string(kNoAllocMaxCtas));
+  const MatrixData& d = p->m->d;
+  DeviceGuard guard(p->device);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if ((reinterpret_cast<uintptr_t>(B) & 15u) || (reinterpret_cast<uintptr_t>(C) & 15u)) {
+    vbsr_device_matrix view;  // unaligned buffers: the plain-load row kernel (no scratch)
+    vbsr_matrix_device_view(p->m, &view);
+    return launch_view_kernel(&view, B, C, p->rhs, s, false);
+  }
+  if (p->num_tasks == 0) return VBSR_OK;
+  unsigned long long* scratch = nullptr;
+  vbsr_status st = noalloc_scratch(p->device, &scratch);
+  if (st != VBSR_OK) return st;
+  // the array keeps the previous call's contents: clear the status words and the timestamps
+  const size_t used = (2 + 2 * size_t(p->num_tasks)) * sizeof(unsigned long long);
+  VBSR_CUDA(cudaMemsetAsync(scratch, 0, used, s));
+  KernelParams kp;
+  st = encode_b_map(&kp.b_full, B, d.K, p->rhs, p->rhs);
+  if (st != VBSR_OK) return st;
+  st = encode_b_map(&kp.b_half, B, d.K, p->rhs, p->rhs > 8 ? p->rhs / 2 : p->rhs);
+  if (st != VBSR_OK) return st;
+  kp.stream = p->d_stream;
+  kp.tasks = p->d_tasks;
+  kp.values = d.d_values;
+  kp.B = B;
+  kp.C = C;
+  kp.M = d.M;
+  kp.K = d.K;
+  kp.nvalues = d.nvalues;
+  kp.rhs = p->rhs;
+  kp.status = reinterpret_cast<int*>(scratch);
+  kp.drop_stage = p->drop_stage;
+  kp.wait_limit = p->wait_limit;
+  kp.timing = scratch + 2;
+  kp.diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
+  switch (p->rhs) {
+    case 8: launch_spmm<8>(p, kp, s); break;
+    case 16: launch_spmm<16>(p, kp, s); break;
+    case 32: launch_spmm<32>(p, kp, s); break;
+    case 64: launch_spmm<64>(p, kp, s); break;
+  }
+  VBSR_CUDA(cudaGetLastError());
+  if (cta_times == nullptr) return VBSR_OK;
+  // Reporting mode: wait for this launch, then return its status and CTA timestamps.
+  int words[kStatusWords] = {0, 0, 0, 0};
+  VBSR_CUDA(cudaMemcpyAsync(words, scratch, sizeof words, cudaMemcpyDeviceToHost, s));
+  const int n = std::max(0, std::min(cta_times_len, 2 * p->num_tasks));
+  if (n > 0)
+    VBSR_CUDA(cudaMemcpyAsync(cta_times, scratch + 2, size_t(n) * sizeof(uint64_t),
+                              cudaMemcpyDeviceToHost, s));
+  VBSR_CUDA(cudaStreamSynchronize(s));
+  if (words[kStatusCode] == VBSR_TIMEOUT)
+    return set_error(VBSR_TIMEOUT, "pipeline wait timed out in CTA " + std::to_string(words[kStatusInfo]));
+  if (words[kStatusCode] == VBSR_BOUNDS_VIOLATION)
+    return set_error(VBSR_BOUNDS_VIOLATION, "index out of bounds (info " + std::to_string(words[kStatusInfo]) + ")");
+  return VBSR_OK;
+}
+
 vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out) {
   clear_error();
   if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
