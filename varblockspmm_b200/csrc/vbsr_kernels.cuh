@@ -19,7 +19,7 @@
 // to 255 registers per thread).
 //
 // Teams compute with fp32 FMA on CUDA cores from shared memory into a TM x TN register tile per
-// thread (the k loop fully unrolled per chunk width), keep a per-block partial sum (so no single fp32 chain
+// thread, software-pipelined over k-quads, keep a per-block partial sum (so no single fp32 chain
 // is longer than one block width), and store their tile of C straight from registers with 16-byte
 // stores. Every C element is written by exactly one thread: no atomics, no workspace, and C needs
 // no prior clearing.
@@ -31,7 +31,6 @@
 #include <cuda.h>
 
 #include <cstdint>
-#include <type_traits>
 
 #include "vbsr_internal.h"
 #include "vbsr_ptx.cuh"
@@ -110,6 +109,16 @@ __device__ __forceinline__ void record_status(int* status, int code, int info) {
 // exceeded p.wait_limit SM clocks.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const KernelParams& p,
                                            volatile int* abort_flag, int lane) {
+#ifdef VBSR_WAIT_LANE0
+  {
+    int ok = 0;
+    if (lane == 0) ok = mbar_try(bar, parity);
+    if (__shfl_sync(0xffffffffu, ok, 0)) {
+      __syncwarp();
+      return true;
+    }
+  }
+#endif
   if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
   const long long t0 = clock64();
   while (true) {
@@ -310,22 +319,18 @@ __device__ __forceinline__ bool consume_item(const KernelParams& p, u64 hdr, Str
       if (active && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
         const float* As = stage + H * c0 + pnl * 8 * kc;
         const float* Bs = stage + stage_b_offset(H, c.cols) + (c0 >> 3) * NW * 8 + ng * 8;
+        // Software-pipelined over k-quads: the operands of quad q+1 are loaded from shared
+        // memory while the FMAs of quad q run (two register fragments, alternating).
+        Frag<TM, TN> f0, f1;
         const int nq = kc >> 2;  // even: kc is a multiple of 8
-        // Fully unrolled per chunk width (nq quads of 4 columns): the compiler schedules the
-        // shared-memory loads of later quads under the FMAs of earlier ones.
-        auto run = [&](auto NQ) {
-          constexpr int N = decltype(NQ)::value;
-#pragma unroll
-          for (int q = 0; q < N; ++q) {
-            Frag<TM, TN> f;
-            load_frag<TM, TN, NG>(f, As, Bs, q, offa, NW);
-            fma_frag<TM, TN>(part, f);
-          }
-        };
-        if (nq == 8) run(std::integral_constant<int, 8>());
-        else if (nq == 6) run(std::integral_constant<int, 6>());
-        else if (nq == 4) run(std::integral_constant<int, 4>());
-        else run(std::integral_constant<int, 2>());
+        load_frag<TM, TN, NG>(f0, As, Bs, 0, offa, NW);
+#pragma unroll 1
+        for (int q = 0; q < nq; q += 2) {
+          load_frag<TM, TN, NG>(f1, As, Bs, q + 1, offa, NW);
+          fma_frag<TM, TN>(part, f0);
+          if (q + 2 < nq) load_frag<TM, TN, NG>(f0, As, Bs, q + 2, offa, NW);
+          fma_frag<TM, TN>(part, f1);
+        }
       }
       c0 += kc;
       if (chk_k0(e) + kc == chk_w(e)) {  // block done: fold its partial sums in
