@@ -15,7 +15,8 @@
 #include <vector>
 
 #include "vbsr_internal.h"
-#include "vbsr_kernels.cuh"
+#include "vbsr_kernels_common.cuh"
+#include "vbsr_tc.cuh"
 #include "vbsr_rng.h"
 #include "vbsr_tiles.h"
 
@@ -172,7 +173,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// B (K x rhs, column-major, ld K) as a 2-D tensor with an 8-column x `rows`-row box.
+// B (K x rhs, column-major, ld K) as a 2-D tensor with an 8-column x `rows`-row box, written to
+// shared memory with the 32-byte swizzle (the K-major operand layout of tcgen05.mma).
 vbsr_status encode_b_map(CUtensorMap* map, const float* B, int64_t K, int rhs, int rows) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
@@ -182,7 +184,7 @@ vbsr_status encode_b_map(CUtensorMap* map, const float* B, int64_t K, int rhs, i
   const cuuint32_t estr[2] = {1u, 1u};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
@@ -380,23 +382,24 @@ namespace {
 
 constexpr int kSmemBudget = 220 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
 
-// Per-team time model of one item, in warp-issue cycles: FMAs per thread plus a per-chunk and
-// per-item overhead.
-double item_cost(int h, int nw, int64_t sum_w, int nchunks) {
-  const TileCfg c = tile_cfg(h, nw);
-  return double(c.tm) * c.tn * double(sum_w) + 160.0 * nchunks + 400.0;
+// Per-team time model of one item: the bytes its stages move (A and B) plus a fixed cost per stage
+// and per item, in bytes-equivalent units.
+double item_cost(int h, int nw, int64_t sum_w, int nstages) {
+  return 4.0 * double(h + nw) * double(sum_w) + 4096.0 * nstages + 8192.0;
 }
 
-template <int RHS>
 cudaError_t set_kernel_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(spmm_kernel<RHS, false>,
+  cudaError_t e = cudaFuncSetAttribute(spmm_tc_kernel<false>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kSmemBudget + 1024);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(spmm_kernel<RHS, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute(spmm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               kSmemBudget + 1024);
 }
 
+// Schedule for spmm_tc_kernel: one item per block row, kTcTeams teams of four warps per CTA, one
+// CTA per SM; items assigned to teams by longest-processing-time-first on the cost model; each
+// team's stream packs the item's k-chunks into stages of kTcCols block columns.
 vbsr_status build_schedule(vbsr_plan* p) {
   const MatrixData& d = p->m->d;
   const int rhs = p->rhs;
@@ -405,203 +408,99 @@ vbsr_status build_schedule(vbsr_plan* p) {
   if (d.nvalues >= entry::kMaxVal || d.K >= entry::kMaxCol || d.M >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "matrix exceeds the schedule's index range");
 
-  struct Cand {
-    int row, n0, nw, warps, chunks;
-    double cost;
-  };
-  std::vector<int> row_chunks(d.block_rows);
-  for (int i = 0; i < d.block_rows; ++i) {
-    int c = 0;
+  const int R = d.block_rows;
+  std::vector<int> row_stages(R);
+  std::vector<double> cost(R);
+  for (int i = 0; i < R; ++i) {
+    int st = 0, used = 0;
     for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
       const int w = int((d.h_blk_desc[b] & 7u) + 1u) * 8;
-      c += (w + kChunk - 1) / kChunk;
-    }
-    row_chunks[i] = c;
-  }
-  std::vector<Cand> items;
-  items.reserve(size_t(d.block_rows) * 2);
-  auto make = [&](int i, int n0, int nw) {
-    Cand c;
-    c.row = i;
-    c.n0 = n0;
-    c.nw = nw;
-    c.warps = tile_cfg(d.h_row_size[i], nw).warps;
-    c.chunks = row_chunks[i];
-    c.cost = item_cost(d.h_row_size[i], nw, d.h_sum_w[i], c.chunks);
-    return c;
-  };
-  double total = 0.0;
-  for (int i = 0; i < d.block_rows; ++i) {
-    items.push_back(make(i, 0, rhs));
-    total += items.back().cost * items.back().warps;
-  }
-  // Heavy rows: split into two RHS-column halves when one item would take more than a quarter of
-  // the ideal per-team time (the makespan bound a static schedule can reach).
-  int split_rows = 0;
-  if (!(p->flags & VBSR_PLAN_NO_SPLIT) && rhs >= 16) {
-    const double ideal_team = total / (double(num_sm) * kConsumerWarps);
-    std::vector<Cand> out;
-    out.reserve(items.size() + 64);
-    for (const Cand& c : items) {
-      if (c.cost > 0.25 * ideal_team * kConsumerWarps / c.warps && c.chunks > 0) {
-        out.push_back(make(c.row, 0, rhs / 2));
-        out.push_back(make(c.row, rhs / 2, rhs / 2));
-        ++split_rows;
-      } else {
-        out.push_back(c);
+      for (int k0 = 0; k0 < w; k0 += kChunk) {
+        const int kc = std::min(kChunk, w - k0);
+        if (used == 0 || used + kc > kTcCols) {
+          ++st;
+          used = 0;
+        }
+        used += kc;
       }
     }
-    items.swap(out);
+    row_stages[i] = st;
+    cost[i] = item_cost(d.h_row_size[i], rhs, d.h_sum_w[i], st);
+  }
+  const int ctas = std::max(1, std::min(num_sm, (R + kTcTeams - 1) / kTcTeams));
+  const int teams = ctas * kTcTeams;
+  std::vector<int> order(R);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+  using Load = std::pair<double, int>;
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int t = 0; t < teams; ++t) heap.push({0.0, t});
+  std::vector<std::vector<int>> lists(teams);
+  std::vector<double> load(teams, 0.0);
+  for (int i : order) {
+    Load l = heap.top();
+    heap.pop();
+    lists[l.second].push_back(i);
+    l.first += cost[i];
+    load[l.second] = l.first;
+    heap.push(l);
   }
 
-  // Classes by team size; SMs shared out in proportion to each class's warp-time.
-  const int class_warps[3] = {1, 2, 4};
-  double class_work[3] = {0, 0, 0};
-  std::vector<int> class_items[3];
-  for (size_t k = 0; k < items.size(); ++k) {
-    const int cls = items[k].warps == 1 ? 0 : items[k].warps == 2 ? 1 : 2;
-    class_items[cls].push_back(int(k));
-    class_work[cls] += items[k].cost * items[k].warps;
-  }
-  const double work_sum = class_work[0] + class_work[1] + class_work[2];
-  int ctas[3] = {0, 0, 0};
-  int nonempty = 0;
-  for (int c = 0; c < 3; ++c) nonempty += class_items[c].empty() ? 0 : 1;
-  const int sm_budget = std::max(num_sm, nonempty);
-  int assigned = 0;
-  double rem[3] = {0, 0, 0};
-  auto cap_of = [&](int c) {
-    const int nt = kConsumerWarps / class_warps[c];
-    return int((class_items[c].size() + nt - 1) / nt);
-  };
-  for (int c = 0; c < 3; ++c) {
-    if (class_items[c].empty()) continue;
-    const double share = work_sum > 0 ? sm_budget * class_work[c] / work_sum : 1.0;
-    ctas[c] = std::max(1, std::min(cap_of(c), int(share)));
-    rem[c] = share - ctas[c];
-    assigned += ctas[c];
-  }
-  while (assigned < sm_budget) {
-    int best = -1;
-    for (int c = 0; c < 3; ++c) {
-      if (class_items[c].empty() || ctas[c] >= cap_of(c)) continue;
-      if (best < 0 || rem[c] > rem[best]) best = c;
-    }
-    if (best < 0) break;
-    ++ctas[best];
-    rem[best] -= 1.0;
-    ++assigned;
-  }
-  while (assigned > sm_budget) {  // only when the minimum of one CTA per class overshot
-    int best = -1;
-    for (int c = 0; c < 3; ++c)
-      if (ctas[c] > 1 && (best < 0 || rem[c] < rem[best])) best = c;
-    if (best < 0) break;
-    --ctas[best];
-    rem[best] += 1.0;
-    --assigned;
-  }
-
-  // Per-row first block's value offset and block list; emit each team's stream.
   std::vector<unsigned long long> stream;
-  stream.reserve(items.size() + size_t(d.nnzb) * 2);
+  stream.reserve(size_t(R) + size_t(d.nnzb) * 2);
   std::vector<Task> h_tasks;
-  int max_smem = 0;
-  for (int c = 0; c < 3; ++c) {
-    if (class_items[c].empty()) continue;
-    const int tw = class_warps[c];
-    const int nt = kConsumerWarps / tw;
-    const int workers = ctas[c] * nt;
-    std::vector<int>& idx = class_items[c];
-    std::stable_sort(idx.begin(), idx.end(),
-                     [&](int a, int b) { return items[a].cost > items[b].cost; });
-    // LPT: each item goes to the least-loaded team.
-    using Load = std::pair<double, int>;
-    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-    for (int w = 0; w < workers; ++w) heap.push({0.0, w});
-    std::vector<std::vector<int>> lists(workers);
-    std::vector<double> load(workers, 0.0);
-    for (int k : idx) {
-      Load l = heap.top();
-      heap.pop();
-      lists[l.second].push_back(k);
-      l.first += items[k].cost;
-      load[l.second] = l.first;
-      heap.push(l);
-    }
-    for (int t = 0; t < ctas[c]; ++t) {
-      Task task{};
-      // Stage width: 64 block columns when two such stages per team fit, else 32.
-      int sf64 = 256, sf32 = 256;
-      for (int j = 0; j < nt; ++j)
-        for (int k : lists[t * nt + j]) {
-          const int h = d.h_row_size[items[k].row];
-          sf64 = std::max(sf64, stage_floats(h, items[k].nw, 64));
-          sf32 = std::max(sf32, stage_floats(h, items[k].nw, 32));
-        }
-      const bool wide = (p->flags & VBSR_PLAN_NARROW_STAGES) == 0 &&
-                        2 * nt * sf64 * 4 <= kSmemBudget;
-      const int cols = wide ? 64 : 32;
-      const int sf = wide ? sf64 : sf32;
-      for (int j = 0; j < nt; ++j) {
-        task.team_off[j] = int(stream.size());
-        std::vector<int>& l = lists[t * nt + j];
-        std::sort(l.begin(), l.end(), [&](int a, int b) {
-          return items[a].row != items[b].row ? items[a].row < items[b].row
-                                              : items[a].n0 < items[b].n0;
-        });
-        for (int k : l) {
-          const Cand& it = items[k];
-          const int i = it.row, h = d.h_row_size[i];
-          stream.push_back(entry::header(d.h_row_off[i], h, it.n0, it.nw));
-          // Chunks packed greedily into stages of `cols` columns; a chunk never straddles two.
-          int64_t val = d.h_val_off_row[i];
-          int used = 0;
-          for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
-            const uint32_t desc = d.h_blk_desc[b];
-            const int w = int((desc & 7u) + 1u) * 8;
-            const int64_t col = int64_t(desc & ~7u);
-            for (int k0 = 0; k0 < w; k0 += kChunk) {
-              const int kc = std::min(kChunk, w - k0);
-              if (used + kc > cols) {
-                stream.back() |= entry::kLastOfStage;
-                used = 0;
-              }
-              stream.push_back(entry::chunk(val, col, w, k0, kc, false));
-              used += kc;
+  const int stages = std::min(kMaxStages, kSmemBudget / (kTcTeams * kTcStageFloats * 4));
+  if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
+  for (int t = 0; t < ctas; ++t) {
+    Task task{};
+    for (int j = 0; j < kTcTeams; ++j) {
+      task.team_off[j] = int(stream.size());
+      std::vector<int>& l = lists[t * kTcTeams + j];
+      std::sort(l.begin(), l.end());
+      for (int i : l) {
+        const int h = d.h_row_size[i];
+        stream.push_back(entry::header(d.h_row_off[i], h, 0, rhs));
+        // k-chunks packed greedily into stages of kTcCols columns; a chunk never straddles two
+        int64_t val = d.h_val_off_row[i];
+        int used = 0;
+        for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
+          const uint32_t desc = d.h_blk_desc[b];
+          const int w = int((desc & 7u) + 1u) * 8;
+          const int64_t col = int64_t(desc & ~7u);
+          for (int k0 = 0; k0 < w; k0 += kChunk) {
+            const int kc = std::min(kChunk, w - k0);
+            if (used > 0 && used + kc > kTcCols) {
+              stream.back() |= entry::kLastOfStage;
+              used = 0;
             }
-            val += int64_t(h) * w;
+            stream.push_back(entry::chunk(val, col, w, k0, kc, false));
+            used += kc;
           }
-          if (used > 0) stream.back() |= entry::kLastOfStage;
+          val += int64_t(h) * w;
         }
+        if (used > 0) stream.back() |= entry::kLastOfStage;
       }
-      for (int j = nt; j <= kConsumerWarps; ++j) task.team_off[j] = int(stream.size());
-      task.team_warps = tw;
-      task.stage_floats = sf;
-      task.stage_cols = cols;
-      const int stages = std::min(kMaxStages, kSmemBudget / (nt * sf * 4));
-      if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
-      task.stages = stages;
-      max_smem = std::max(max_smem, nt * stages * sf * 4);
-      h_tasks.push_back(task);
-      p->task_warps.push_back(tw);
-      p->task_cost.push_back(*std::max_element(load.begin() + t * nt, load.begin() + (t + 1) * nt));
     }
+    for (int j = kTcTeams; j <= 8; ++j) task.team_off[j] = int(stream.size());
+    task.team_warps = 4;
+    task.stage_floats = kTcStageFloats;
+    task.stage_cols = kTcCols;
+    task.stages = stages;
+    h_tasks.push_back(task);
+    p->task_warps.push_back(4);
+    p->task_cost.push_back(std::max(load[t * kTcTeams], load[t * kTcTeams + 1]));
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
-  // At least ~116 KB so that one CTA occupies one SM (the schedule is static per CTA); plus 1 KB
-  // so the kernel can align its stage base to 1 KB.
-  p->smem_bytes = std::max(max_smem, 116 * 1024) + 1024;
+  p->smem_bytes = kTcTeams * stages * kTcStageFloats * 4 + 1024;
   p->num_tasks = int(h_tasks.size());
   p->stream_entries = int64_t(stream.size());
 
   char buf[512];
   std::snprintf(buf, sizeof buf,
-                "rhs=%d items=%zu split_rows=%d stream_entries=%zu tasks=%d (tw1=%d tw2=%d tw4=%d) "
-                "smem=%d sms=%d",
-                rhs, items.size(), split_rows, stream.size(), p->num_tasks, ctas[0], ctas[1],
-                ctas[2], p->smem_bytes, num_sm);
+                "rhs=%d items=%d stream_entries=%zu tasks=%d teams=%d stages=%d smem=%d sms=%d "
+                "kernel=tcgen05-3xtf32",
+                rhs, R, stream.size(), p->num_tasks, teams, stages, p->smem_bytes, num_sm);
   p->summary = buf;
 
   DeviceGuard guard(d.device);
@@ -615,12 +514,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
     VBSR_CUDA(cudaMemcpy(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
                          cudaMemcpyHostToDevice));
   VBSR_CUDA(cudaMemset(p->d_status, 0, kStatusWords * sizeof(int)));
-  switch (rhs) {
-    case 8: VBSR_CUDA(set_kernel_attrs<8>()); break;
-    case 16: VBSR_CUDA(set_kernel_attrs<16>()); break;
-    case 32: VBSR_CUDA(set_kernel_attrs<32>()); break;
-    case 64: VBSR_CUDA(set_kernel_attrs<64>()); break;
-  }
+  VBSR_CUDA(set_kernel_attrs());
   return VBSR_OK;
 }
 
@@ -634,12 +528,11 @@ void free_plan(vbsr_plan* p) {
   delete p;
 }
 
-template <int RHS>
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
   if (p->flags & VBSR_PLAN_BOUNDS_CHECK)
-    spmm_kernel<RHS, true><<<p->num_tasks, kThreads, p->smem_bytes, stream>>>(kp);
+    spmm_tc_kernel<true><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
   else
-    spmm_kernel<RHS, false><<<p->num_tasks, kThreads, p->smem_bytes, stream>>>(kp);
+    spmm_tc_kernel<false><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
 }
 
 vbsr_status launch_view_kernel(const vbsr_device_matrix* a, const float* B, float* C, int rhs,
@@ -806,12 +699,7 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   kp.wait_limit = p->wait_limit;
   kp.timing = p->timing_on ? p->d_timing : nullptr;
   kp.diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
-  switch (p->rhs) {
-    case 8: launch_spmm<8>(p, kp, s); break;
-    case 16: launch_spmm<16>(p, kp, s); break;
-    case 32: launch_spmm<32>(p, kp, s); break;
-    case 64: launch_spmm<64>(p, kp, s); break;
-  }
+  launch_spmm(p, kp, s);
   VBSR_CUDA(cudaGetLastError());
   return VBSR_OK;
 }
@@ -900,12 +788,7 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
   kp.wait_limit = p->wait_limit;
   kp.timing = scratch + 2;
   kp.diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
-  switch (p->rhs) {
-    case 8: launch_spmm<8>(p, kp, s); break;
-    case 16: launch_spmm<16>(p, kp, s); break;
-    case 32: launch_spmm<32>(p, kp, s); break;
-    case 64: launch_spmm<64>(p, kp, s); break;
-  }
+  launch_spmm(p, kp, s);
   VBSR_CUDA(cudaGetLastError());
   if (cta_times == nullptr) return VBSR_OK;
   // Reporting mode: wait for this launch, then return its status and CTA timestamps.

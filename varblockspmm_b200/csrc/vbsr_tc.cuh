@@ -1,0 +1,426 @@
+// vbsr_tc.cuh — the sm_100a SpMM kernel on 5th-generation tensor cores (tcgen05, TMEM).
+//
+// Per work item (one block row i: an h x nw tile of C) the kernel computes the transposed product
+//     D (64 x h) = sum over the row's blocks b of  B_b^T (64 x w) * A_b^T (w x h)
+// with tcgen05.mma kind::tf32 (M = 64: the item's nw RHS columns, padded; N = h; K = 8 per MMA) and
+// an fp32 accumulator in tensor memory. FP32 accuracy comes from the 3xTF32 split: every staged
+// operand x is split into hi = x with its low 13 mantissa bits cleared (exactly representable in
+// tf32) and lo = x - hi (exact in fp32), and three MMAs accumulate hi*hi + hi*lo + lo*hi. The
+// dropped lo*lo term and the tf32 conversion of lo are below 2^-19 relative per product.
+//
+// CTA = two teams of four warps (warp w of a team sits in TMEM sub-partition w, so together the
+// four read all 64 accumulator rows), one CTA per SM. Each team walks its instruction stream (item
+// headers and k-chunks, compiled by the planner; vbsr_internal.h) and owns a ring of D stages of
+// 32 block columns:
+//   * the team's leader warp issues the TMA copies D-1 stages ahead: A chunks with cp.async.bulk
+//     (the device format already holds each chunk as the K-major 32-byte-swizzled operand tile the
+//     MMA reads), B with 2-D cp.async.bulk.tensor boxes of 8 columns x nw rows, SWIZZLE_32B;
+//   * when a stage lands, the team's 128 threads split A and B into hi (in place) and lo (a second
+//     buffer), fence the generic-proxy writes for the async proxy and arrive on the stage's
+//     "split" mbarrier (one arrival per warp; no named barriers, so every wait stays bounded);
+//   * one thread issues the stage's MMAs and tcgen05.commit, whose mbarrier arrival frees the
+//     stage for the next copies;
+//   * at the end of an item the thread commits to the team's accumulator barrier, and the four
+//     warps load D with tcgen05.ld and store C (each thread: one RHS column, h consecutive rows).
+// Every wait is bounded (see wait_phase); after an abort each leader drains its copies and MMAs
+// before the CTA releases its tensor memory.
+#pragma once
+#include <cuda.h>
+
+#include <cstdint>
+
+#include "vbsr_internal.h"
+#include "vbsr_kernels_common.cuh"
+#include "vbsr_ptx.cuh"
+#include "vbsr_tiles.h"
+
+namespace vbsr_b200 {
+
+constexpr int kTcTeams = 2;                 // teams per CTA (4 warps each)
+constexpr int kTcThreads = 32 * 4 * kTcTeams;
+constexpr int kTcCols = 32;                 // block columns per stage
+constexpr int kTcM = 64;                    // MMA M (RHS columns, padded)
+// Stage layout (floats): A hi | A lo | B hi | B lo, fixed offsets.
+constexpr int kStA = 0;
+constexpr int kStALo = 64 * kTcCols;                    // A: up to 64 rows x 32 columns
+constexpr int kStB = 2 * 64 * kTcCols;
+constexpr int kBoxFloats = kTcM * 8;                    // one 8-column B box, padded to 64 rows
+constexpr int kStBLo = kStB + (kTcCols / 8) * kBoxFloats;
+constexpr int kTcStageFloats = kStBLo + (kTcCols / 8) * kBoxFloats;  // 8192 floats = 32 KB
+constexpr int kTmemCols = 64 * kTcTeams;                // one 64-column accumulator per team
+constexpr int kTmemAlloc = 128;                         // power of two >= kTmemCols
+
+// ---- tcgen05 wrappers ------------------------------------------------------------------------------
+
+__device__ __forceinline__ void tc_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// K-major, 32-byte-swizzled operand: rows of 8 tf32 (32 bytes), 8-row atoms 256 bytes apart.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t smem_byte_addr) {
+  return uint64_t((smem_byte_addr >> 4) & 0x3FFFu) | (uint64_t(16 >> 4) << 16) |
+         (uint64_t(256 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(6) << 61);
+}
+
+// kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major, M x N.
+__device__ __forceinline__ uint32_t tf32_idesc(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// ---- producer side (team leader warp) ----------------------------------------------------------
+
+template <bool CHECK>
+__device__ __forceinline__ bool tc_issue_next(const KernelParams& p, Issuer& is, float* team_stages,
+                                              int D, uint32_t full0, uint32_t empty0, int team,
+                                              int lane, volatile int* abort_flag) {
+  while (!is.win.done()) {
+    const u64 e = is.win.peek();
+    if (!is_header(e)) break;
+    is.h = hdr_h(e);
+    is.n0 = hdr_n0(e);
+    is.nw = hdr_nw(e);
+    is.win.advance(p.stream, lane);
+  }
+  if (is.win.done()) return true;
+  const int s = is.slot;
+  const uint32_t full_bar = full0 + 8u * s;
+  if (!wait_phase(empty0 + 8u * s, is.ph ^ 1u, p, abort_flag, lane)) return false;
+  const int h = is.h, nw = is.nw, n0 = is.n0;
+  const bool drop = (team == 0 && is.issued == p.drop_stage);
+  ++is.issued;
+  float* st = team_stages + s * kTcStageFloats;
+  const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
+  const bool copy = !drop && !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES);
+  bool in_bounds = true;
+  int c0 = 0;
+  while (!is.win.done()) {  // the stage's chunks (ends at a stage-end mark)
+    const u64 e = is.win.peek();
+    is.win.advance(p.stream, lane);
+    const long long val = chk_val(e), colk = chk_colk(e);
+    const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
+    bool ok = true;
+    if (CHECK)
+      ok = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K && n0 + nw <= p.rhs &&
+           c0 + kc <= kTcCols && h <= 64 && nw <= kTcM;
+    in_bounds = in_bounds && ok;
+    if (copy && ok) {
+      if (lane == 0) {
+        mbar_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
+        bulk_g2s(smem_addr(st + kStA + h * c0), p.values + val + (long long)h * k0,
+                 uint32_t(h * 4 * kc), full_bar, policy_evict_first());
+      } else if (lane <= (kc >> 3)) {
+        const int g = lane - 1;
+        tensor2d_g2s(smem_addr(st + kStB + ((c0 >> 3) + g) * kBoxFloats), map, int(colk) + 8 * g,
+                     n0, full_bar, policy_evict_last());
+      }
+    }
+    c0 += kc;
+    if (chk_stage_end(e)) break;
+  }
+  if (!drop) {
+    if (lane == 0) {
+      if (!in_bounds) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+      mbar_arrive(full_bar);  // the stage's bytes were announced chunk by chunk
+    }
+    if (copy) {
+      is.filled |= 1u << s;
+      is.lastpar = (is.lastpar & ~(1u << s)) | (is.ph << s);
+    }
+  }
+  if (++is.slot == D) {
+    is.slot = 0;
+    is.ph ^= 1u;
+  }
+  return true;
+}
+
+// ---- team ----------------------------------------------------------------------------------------
+
+// hi = x with the low 13 mantissa bits cleared, lo = x - hi, over n4 float4s at p (hi in place).
+__device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int tid) {
+  for (int i = tid; i < n4; i += 128) {
+    float4* ph = reinterpret_cast<float4*>(base) + i;
+    float4 x = *ph;
+    float4 hi, lo;
+    hi.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    hi.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    hi.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    hi.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    lo.x = x.x - hi.x;
+    lo.y = x.y - hi.y;
+    lo.z = x.z - hi.z;
+    lo.w = x.w - hi.w;
+    *ph = hi;
+    *reinterpret_cast<float4*>(base + lo_off + 4 * i) = lo;
+  }
+}
+
+template <bool CHECK>
+__device__ void tc_run_team(const KernelParams& p, const Task& task, float* stages,
+                            uint32_t full_base, uint32_t empty_base, uint32_t split_base,
+                            uint32_t acc_base, uint32_t accfree_base, uint32_t tmem_base, int warp,
+                            int lane, volatile int* abort_flag) {
+  const int team = warp >> 2, wq = warp & 3;  // wq: this warp's TMEM sub-partition
+  const int tid = wq * 32 + lane;             // thread index within the team
+  const bool leader = wq == 0;
+  const bool issuer = leader && lane == 0;
+  const int D = task.stages;
+  const uint32_t full0 = full_base + 8u * (team * kMaxStages);
+  const uint32_t empty0 = empty_base + 8u * (team * kMaxStages);
+  const uint32_t split0 = split_base + 8u * (team * kMaxStages);
+  const uint32_t accbar = acc_base + 8u * team;
+  const uint32_t accfree = accfree_base + 8u * team;
+  const uint32_t tmem_d = tmem_base + uint32_t(team * 64);  // lane 0, columns team*64..
+  float* my = stages + team * D * kTcStageFloats;
+  const int b = task.team_off[team], e = task.team_off[team + 1];
+
+  StreamWin win;
+  win.init(p.stream, b, e, lane);
+  Issuer is;
+  is.h = 8;
+  is.n0 = 0;
+  is.nw = 8;
+  is.slot = 0;
+  is.ph = 0;
+  is.filled = is.lastpar = 0;
+  is.issued = 0;
+  bool ok = true;
+  if (leader) {
+    is.win.init(p.stream, b, e, lane);
+    for (int i = 0; i < D - 1 && ok; ++i)
+      ok = tc_issue_next<CHECK>(p, is, my, D, full0, empty0, team, lane, abort_flag);
+  }
+  int s = 0;
+  uint32_t ph = 0, accph = 0;
+  int items_done = 0;  // items whose accumulator the four warps have read
+  bool mma_issued = false;
+  while (ok && !win.done()) {
+    const u64 hdr = win.peek();
+    win.advance(p.stream, lane);
+    if (!is_header(hdr)) {
+      if (lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, win.pos);
+      ok = false;
+      break;
+    }
+    const int h = hdr_h(hdr), nw = hdr_nw(hdr), n0 = hdr_n0(hdr), c_row = hdr_crow(hdr);
+    const uint32_t idesc = tf32_idesc(kTcM, h);
+    uint32_t accumulate = 0;  // the item's first MMA overwrites the accumulator
+    bool any = false;
+    while (!win.done()) {
+      if (is_header(win.peek())) break;
+      if (!wait_phase(full0 + 8u * s, ph, p, abort_flag, lane)) {
+        ok = false;
+        break;
+      }
+      if (leader && !tc_issue_next<CHECK>(p, is, my, D, full0, empty0, team, lane, abort_flag)) {
+        ok = false;
+        break;
+      }
+      float* st = my + s * kTcStageFloats;
+      // the stage's chunk list: widths and total
+      int cols = 0;
+      uint32_t kcs = 0;  // 2 bits per chunk: kc/8 - 1
+      int nchunks = 0;
+      while (!win.done()) {
+        const u64 ce = win.peek();
+        win.advance(p.stream, lane);
+        const int kc = chk_kc(ce);
+        kcs |= uint32_t(kc / 8 - 1) << (2 * nchunks);
+        ++nchunks;
+        cols += kc;
+        if (chk_stage_end(ce)) break;
+      }
+      if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+        // split A (h rows x cols) and the used B boxes (nw rows each) into hi / lo
+        split_hi_lo(st + kStA, kStALo - kStA, (h * cols) / 4, tid);
+        for (int g = 0; g < cols / 8; ++g)
+          split_hi_lo(st + kStB + g * kBoxFloats, kStBLo - kStB, nw * 2, tid);
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(split0 + 8u * s);
+      if (leader) {
+        bool go = wait_phase(split0 + 8u * s, ph, p, abort_flag, lane);
+        // the item's first MMA overwrites the accumulator: the four warps must have finished
+        // reading the previous item's
+        if (go && !any && items_done > 0)
+          go = wait_phase(accfree, uint32_t((items_done - 1) & 1), p, abort_flag, lane);
+        if (!go) {
+          ok = false;
+          break;
+        }
+      }
+      if (issuer) {
+        tc_fence_after();
+        if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+          const uint32_t sa = smem_addr(st);
+          int c0 = 0;
+          for (int c = 0; c < nchunks; ++c) {
+            const int kc = int(((kcs >> (2 * c)) & 3u) + 1u) * 8;
+            for (int g = 0; g < kc / 8; ++g) {
+              const int col = c0 + 8 * g;  // stage column of this 8-column group
+              const uint32_t a_hi = sa + 4u * uint32_t(kStB + (col >> 3) * kBoxFloats);
+              const uint32_t a_lo = a_hi + 4u * uint32_t(kStBLo - kStB);
+              const uint32_t b_hi = sa + 4u * uint32_t(kStA + h * c0 + g * h * 8);
+              const uint32_t b_lo = b_hi + 4u * uint32_t(kStALo - kStA);
+              tc_mma_tf32(tmem_d, sw32_desc(a_hi), sw32_desc(b_hi), idesc, accumulate);
+              tc_mma_tf32(tmem_d, sw32_desc(a_hi), sw32_desc(b_lo), idesc, 1u);
+              tc_mma_tf32(tmem_d, sw32_desc(a_lo), sw32_desc(b_hi), idesc, 1u);
+              accumulate = 1u;
+            }
+            c0 += kc;
+          }
+          mma_issued = true;
+        }
+        tc_commit(empty0 + 8u * s);  // frees the stage once these MMAs have read it
+      }
+      __syncwarp();
+      any = true;
+      if (++s == D) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    if (!ok) break;
+    // epilogue: D -> C (a block row with no blocks is stored as zeros)
+    if (issuer) tc_commit(accbar);
+    if (!wait_phase(accbar, accph, p, abort_flag, lane)) {
+      ok = false;
+      break;
+    }
+    accph ^= 1u;
+    tc_fence_after();
+    const int m = 16 * wq + lane;  // accumulator row = RHS column of this thread
+    const uint32_t taddr = tmem_d + (uint32_t(32 * wq) << 16);
+    const bool valid = lane < 16 && m < nw;
+    const bool store = !(CHECK && ((long long)c_row + h > p.M || n0 + nw > p.rhs));
+    if (CHECK && !store && tid == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, c_row);
+    float* dst = p.C + (long long)(n0 + m) * p.M + c_row;
+    for (int c = 0; c < h; c += 8) {
+      float v[8];
+      tc_ld8(taddr + uint32_t(c), v);
+      if (!any || (p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+      }
+      if (valid && store) {
+        reinterpret_cast<float4*>(dst + c)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(dst + c)[1] = make_float4(v[4], v[5], v[6], v[7]);
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(accfree);  // this warp is done with the accumulator
+    ++items_done;
+  }
+  (void)mma_issued;
+  // After an abort: wait (bounded) for the leader's copies and for every MMA issued so far.
+  if (leader && __shfl_sync(0xffffffffu, *abort_flag, 0)) {
+    if (issuer) tc_commit(accbar);
+    const long long t0 = clock64();
+    while (!mbar_try(accbar, accph) && clock64() - t0 < p.wait_limit) {
+    }
+    for (int sl = 0; sl < D; ++sl) {
+      if (!(is.filled & (1u << sl))) continue;
+      const uint32_t bar = full0 + 8u * sl;
+      const uint32_t par = (is.lastpar >> sl) & 1u;
+      const long long t1 = clock64();
+      while (!mbar_try(bar, par) && clock64() - t1 < p.wait_limit) {
+      }
+    }
+  }
+}
+
+template <bool CHECK>
+__global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  float* stages = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bars[2][kTcTeams][kMaxStages];
+  __shared__ __align__(8) uint64_t splitbars[kTcTeams][kMaxStages];
+  __shared__ __align__(8) uint64_t accbars[kTcTeams];
+  __shared__ __align__(8) uint64_t accfree[kTcTeams];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const Task task = p.tasks[blockIdx.x];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t full_base = smem_addr(&bars[0][0][0]);
+  const uint32_t empty_base = smem_addr(&bars[1][0][0]);
+  const uint32_t split_base = smem_addr(&splitbars[0][0]);
+  const uint32_t acc_base = smem_addr(&accbars[0]);
+  const uint32_t accfree_base = smem_addr(&accfree[0]);
+  if (warp == 0) {
+    tc_alloc(smem_addr(&tmem_slot), kTmemAlloc);
+    tc_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    if (p.timing) p.timing[2 * blockIdx.x] = global_ns();
+    for (int j = 0; j < kTcTeams; ++j) {
+      for (int s = 0; s < task.stages; ++s) {
+        mbar_init(full_base + 8u * (j * kMaxStages + s), 1u);
+        mbar_init(empty_base + 8u * (j * kMaxStages + s), 1u);  // tcgen05.commit arrival
+        mbar_init(split_base + 8u * (j * kMaxStages + s), 4u);  // one arrival per team warp
+      }
+      mbar_init(acc_base + 8u * j, 1u);
+      mbar_init(accfree_base + 8u * j, 4u);
+    }
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  tc_run_team<CHECK>(p, task, stages, full_base, empty_base, split_base, acc_base, accfree_base,
+                     tmem_base, warp, lane, &abort_flag);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tc_dealloc(tmem_base, kTmemAlloc);
+  }
+  if (threadIdx.x == 0 && p.timing) p.timing[2 * blockIdx.x + 1] = global_ns();
+}
+
+}  // namespace vbsr_b200
