@@ -36,8 +36,9 @@
 
 namespace vbsr_b200 {
 
-constexpr int kTcTeams = 2;                 // teams per CTA (4 warps each)
-constexpr int kTcThreads = 32 * 4 * kTcTeams;
+constexpr int kTcTeams = 2;                 // teams per CTA
+constexpr int kTcWarps = 5 * kTcTeams;      // per team: 4 worker warps + 1 issuer warp
+constexpr int kTcThreads = 32 * kTcWarps;
 constexpr int kTcCols = 32;                 // block columns per stage
 constexpr int kTcM = 64;                    // MMA M (RHS columns, padded)
 // Stage layout (floats): A hi | A lo | B hi | B lo, fixed offsets.
@@ -47,8 +48,8 @@ constexpr int kStB = 2 * 64 * kTcCols;
 constexpr int kBoxFloats = kTcM * 8;                    // one 8-column B box, padded to 64 rows
 constexpr int kStBLo = kStB + (kTcCols / 8) * kBoxFloats;
 constexpr int kTcStageFloats = kStBLo + (kTcCols / 8) * kBoxFloats;  // 8192 floats = 32 KB
-constexpr int kTmemCols = 64 * kTcTeams;                // one 64-column accumulator per team
-constexpr int kTmemAlloc = 128;                         // power of two >= kTmemCols
+constexpr int kTmemCols = 2 * 64 * kTcTeams;            // two 64-column accumulators per team
+constexpr int kTmemAlloc = 256;                         // power of two >= kTmemCols
 
 // ---- tcgen05 wrappers ------------------------------------------------------------------------------
 
@@ -92,6 +93,20 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+// tcgen05.ld of 8 consecutive accumulator columns without waiting (see tc_wait_ld).
+__device__ __forceinline__ void tc_ld8_nowait(uint32_t taddr, float* v) {
+  uint32_t r0, r1, r2, r3, r4, r5, r6, r7;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3), "=r"(r4), "=r"(r5), "=r"(r6), "=r"(r7)
+               : "r"(taddr)
+               : "memory");
+  v[0] = __uint_as_float(r0); v[1] = __uint_as_float(r1); v[2] = __uint_as_float(r2);
+  v[3] = __uint_as_float(r3); v[4] = __uint_as_float(r4); v[5] = __uint_as_float(r5);
+  v[6] = __uint_as_float(r6); v[7] = __uint_as_float(r7);
+}
+__device__ __forceinline__ void tc_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -196,25 +211,128 @@ __device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int
   }
 }
 
-template <bool CHECK>
-__device__ void tc_run_team(const KernelParams& p, const Task& task, float* stages,
-                            uint32_t full_base, uint32_t empty_base, uint32_t split_base,
-                            uint32_t acc_base, uint32_t accfree_base, uint32_t tmem_base, int warp,
-                            int lane, volatile int* abort_flag) {
-  const int team = warp >> 2, wq = warp & 3;  // wq: this warp's TMEM sub-partition
-  const int tid = wq * 32 + lane;             // thread index within the team
-  const bool leader = wq == 0;
-  const bool issuer = leader && lane == 0;
-  const int D = task.stages;
-  const uint32_t full0 = full_base + 8u * (team * kMaxStages);
-  const uint32_t empty0 = empty_base + 8u * (team * kMaxStages);
-  const uint32_t split0 = split_base + 8u * (team * kMaxStages);
-  const uint32_t accbar = acc_base + 8u * team;
-  const uint32_t accfree = accfree_base + 8u * team;
-  const uint32_t tmem_d = tmem_base + uint32_t(team * 64);  // lane 0, columns team*64..
-  float* my = stages + team * D * kTcStageFloats;
-  const int b = task.team_off[team], e = task.team_off[team + 1];
+// Barriers of one team (shared-memory addresses).
+struct TeamBars {
+  uint32_t full0, empty0, split0;  // per ring slot: TMA landed / MMAs done / hi-lo split done
+  uint32_t acc0, accfree0;         // per accumulator buffer: MMAs of the item done / D read
+  uint32_t drain;                  // abort drain
+};
 
+// Epilogue of one item: D (accumulator buffer) -> C. Each worker warp reads its TMEM sub-partition;
+// thread `lane` < 16 of warp wq holds accumulator row m = 16*wq + lane = RHS column n0 + m, i.e.
+// C[c_row .. c_row+h-1, n0+m], stored as h consecutive floats.
+template <bool CHECK>
+__device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const TeamBars& tb, int buf,
+                                            uint32_t parity, uint32_t tmem_acc, int wq, int lane,
+                                            u64 hdr, bool any, volatile int* abort_flag) {
+  if (!wait_phase(tb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
+  tc_fence_after();
+  const int h = hdr_h(hdr), nw = hdr_nw(hdr), n0 = hdr_n0(hdr), c_row = hdr_crow(hdr);
+  const uint32_t taddr = tmem_acc + (uint32_t(32 * wq) << 16);
+  float v[64];
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    if (c * 8 < h) tc_ld8_nowait(taddr + uint32_t(8 * c), v + 8 * c);
+  tc_wait_ld();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tb.accfree0 + 8u * buf);  // this warp is done with the buffer
+  const int m = 16 * wq + lane;
+  const bool store = !(CHECK && ((long long)c_row + h > p.M || n0 + nw > p.rhs));
+  if (CHECK && !store && wq == 0 && lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, c_row);
+  if (lane < 16 && m < nw && store) {
+    const bool zero = !any || (p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+    float4* dst = reinterpret_cast<float4*>(p.C + (long long)(n0 + m) * p.M + c_row);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (c * 8 < h) {
+        dst[2 * c] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                          : make_float4(v[8 * c], v[8 * c + 1], v[8 * c + 2], v[8 * c + 3]);
+        dst[2 * c + 1] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                              : make_float4(v[8 * c + 4], v[8 * c + 5], v[8 * c + 6], v[8 * c + 7]);
+      }
+  }
+  return true;
+}
+
+// Worker warp wq (0..3) of a team: split every stage into hi / lo as it lands, and store each
+// item's result one item later (so the tensor cores work on item j while item j-1 is stored).
+template <bool CHECK>
+__device__ void tc_worker(const KernelParams& p, const Task& task, float* my, const TeamBars& tb,
+                          uint32_t tmem_team, int team, int wq, int lane, volatile int* abort_flag) {
+  const int D = task.stages;
+  const int tid = wq * 32 + lane;
+  StreamWin win;
+  win.init(p.stream, task.team_off[team], task.team_off[team + 1], lane);
+  int s = 0;
+  uint32_t ph = 0;
+  int j = 0;
+  u64 prev_hdr = 0;
+  bool prev_any = false, ok = true;
+  while (ok && !win.done()) {
+    const u64 hdr = win.peek();
+    win.advance(p.stream, lane);
+    if (!is_header(hdr)) {
+      if (lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, win.pos);
+      break;
+    }
+    const int h = hdr_h(hdr), nw = hdr_nw(hdr);
+    bool any = false;
+    while (!win.done() && !is_header(win.peek())) {
+      if (!wait_phase(tb.full0 + 8u * s, ph, p, abort_flag, lane)) {
+        ok = false;
+        break;
+      }
+      int cols = 0;
+      while (!win.done()) {
+        const u64 ce = win.peek();
+        win.advance(p.stream, lane);
+        cols += chk_kc(ce);
+        if (chk_stage_end(ce)) break;
+      }
+      float* st = my + s * kTcStageFloats;
+      if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+        split_hi_lo(st + kStA, kStALo - kStA, (h * cols) / 4, tid);
+        for (int g = 0; g < cols / 8; ++g)
+          split_hi_lo(st + kStB + g * kBoxFloats, kStBLo - kStB, nw * 2, tid);
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tb.split0 + 8u * s);
+      any = true;
+      if (++s == D) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    if (!ok) break;
+    if (j > 0) {
+      const int pj = j - 1;
+      if (!tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1),
+                              tmem_team + uint32_t(64 * (pj & 1)), wq, lane, prev_hdr, prev_any,
+                              abort_flag)) {
+        ok = false;
+        break;
+      }
+    }
+    prev_hdr = hdr;
+    prev_any = any;
+    ++j;
+  }
+  if (ok && j > 0) {
+    const int pj = j - 1;
+    tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1), tmem_team + uint32_t(64 * (pj & 1)),
+                       wq, lane, prev_hdr, prev_any, abort_flag);
+  }
+}
+
+// Issuer warp of a team: lane 0 issues each stage's MMAs once the workers have split it, the warp
+// keeps the TMA ring D-1 stages ahead.
+template <bool CHECK>
+__device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, const TeamBars& tb,
+                          uint32_t tmem_team, int team, int lane, volatile int* abort_flag) {
+  const int D = task.stages;
+  const int b = task.team_off[team], e = task.team_off[team + 1];
   StreamWin win;
   win.init(p.stream, b, e, lane);
   Issuer is;
@@ -225,145 +343,91 @@ __device__ void tc_run_team(const KernelParams& p, const Task& task, float* stag
   is.ph = 0;
   is.filled = is.lastpar = 0;
   is.issued = 0;
+  is.win.init(p.stream, b, e, lane);
   bool ok = true;
-  if (leader) {
-    is.win.init(p.stream, b, e, lane);
-    for (int i = 0; i < D - 1 && ok; ++i)
-      ok = tc_issue_next<CHECK>(p, is, my, D, full0, empty0, team, lane, abort_flag);
-  }
+  for (int i = 0; i < D - 1 && ok; ++i)
+    ok = tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag);
   int s = 0;
-  uint32_t ph = 0, accph = 0;
-  int items_done = 0;  // items whose accumulator the four warps have read
-  bool mma_issued = false;
+  uint32_t ph = 0;
+  int j = 0;
+  const uint32_t sbase = smem_addr(my);
   while (ok && !win.done()) {
     const u64 hdr = win.peek();
     win.advance(p.stream, lane);
-    if (!is_header(hdr)) {
-      if (lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, win.pos);
+    if (!is_header(hdr)) break;
+    const int h = hdr_h(hdr);
+    const int buf = j & 1;
+    const uint32_t tmem_d = tmem_team + uint32_t(64 * buf);
+    if (j >= 2 && !wait_phase(tb.accfree0 + 8u * buf, uint32_t(((j - 2) >> 1) & 1), p, abort_flag,
+                              lane)) {
       ok = false;
       break;
     }
-    const int h = hdr_h(hdr), nw = hdr_nw(hdr), n0 = hdr_n0(hdr), c_row = hdr_crow(hdr);
+    tc_fence_after();
     const uint32_t idesc = tf32_idesc(kTcM, h);
-    uint32_t accumulate = 0;  // the item's first MMA overwrites the accumulator
-    bool any = false;
-    while (!win.done()) {
-      if (is_header(win.peek())) break;
-      if (!wait_phase(full0 + 8u * s, ph, p, abort_flag, lane)) {
+    uint32_t accumulate = 0;
+    while (!win.done() && !is_header(win.peek())) {
+      if (!wait_phase(tb.split0 + 8u * s, ph, p, abort_flag, lane)) {
         ok = false;
         break;
       }
-      if (leader && !tc_issue_next<CHECK>(p, is, my, D, full0, empty0, team, lane, abort_flag)) {
-        ok = false;
-        break;
-      }
-      float* st = my + s * kTcStageFloats;
-      // the stage's chunk list: widths and total
-      int cols = 0;
-      uint32_t kcs = 0;  // 2 bits per chunk: kc/8 - 1
-      int nchunks = 0;
+      tc_fence_after();
+      // descriptors of the stage's first 8-column group; advance by fixed strides
+      const uint32_t st = sbase + 4u * uint32_t(s * kTcStageFloats);
+      uint64_t a_hi = sw32_desc(st + 4u * kStB);
+      const uint64_t lo_delta_a = uint64_t((4u * (kStBLo - kStB)) >> 4);
+      int c0 = 0;
       while (!win.done()) {
         const u64 ce = win.peek();
         win.advance(p.stream, lane);
         const int kc = chk_kc(ce);
-        kcs |= uint32_t(kc / 8 - 1) << (2 * nchunks);
-        ++nchunks;
-        cols += kc;
+        uint64_t b_hi = sw32_desc(st + 4u * uint32_t(kStA + h * c0));
+        const uint64_t lo_delta_b = uint64_t((4u * (kStALo - kStA)) >> 4);
+        if (lane == 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+          for (int g = 0; g < kc / 8; ++g) {
+            tc_mma_tf32(tmem_d, a_hi, b_hi, idesc, accumulate);
+            tc_mma_tf32(tmem_d, a_hi, b_hi + lo_delta_b, idesc, 1u);
+            tc_mma_tf32(tmem_d, a_hi + lo_delta_a, b_hi, idesc, 1u);
+            accumulate = 1u;
+            a_hi += uint64_t((4u * kBoxFloats) >> 4);
+            b_hi += uint64_t((4u * 8u * uint32_t(h)) >> 4);
+          }
+        } else {
+          a_hi += uint64_t((kc / 8) * ((4u * kBoxFloats) >> 4));
+        }
+        accumulate = 1u;
+        c0 += kc;
         if (chk_stage_end(ce)) break;
       }
-      if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-        // split A (h rows x cols) and the used B boxes (nw rows each) into hi / lo
-        split_hi_lo(st + kStA, kStALo - kStA, (h * cols) / 4, tid);
-        for (int g = 0; g < cols / 8; ++g)
-          split_hi_lo(st + kStB + g * kBoxFloats, kStBLo - kStB, nw * 2, tid);
-        fence_proxy_async_smem();
-      }
+      if (lane == 0) tc_commit(tb.empty0 + 8u * s);  // frees the slot once these MMAs read it
       __syncwarp();
-      if (lane == 0) mbar_arrive(split0 + 8u * s);
-      if (leader) {
-        bool go = wait_phase(split0 + 8u * s, ph, p, abort_flag, lane);
-        // the item's first MMA overwrites the accumulator: the four warps must have finished
-        // reading the previous item's
-        if (go && !any && items_done > 0)
-          go = wait_phase(accfree, uint32_t((items_done - 1) & 1), p, abort_flag, lane);
-        if (!go) {
-          ok = false;
-          break;
-        }
+      if (!tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag)) {
+        ok = false;
+        break;
       }
-      if (issuer) {
-        tc_fence_after();
-        if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-          const uint32_t sa = smem_addr(st);
-          int c0 = 0;
-          for (int c = 0; c < nchunks; ++c) {
-            const int kc = int(((kcs >> (2 * c)) & 3u) + 1u) * 8;
-            for (int g = 0; g < kc / 8; ++g) {
-              const int col = c0 + 8 * g;  // stage column of this 8-column group
-              const uint32_t a_hi = sa + 4u * uint32_t(kStB + (col >> 3) * kBoxFloats);
-              const uint32_t a_lo = a_hi + 4u * uint32_t(kStBLo - kStB);
-              const uint32_t b_hi = sa + 4u * uint32_t(kStA + h * c0 + g * h * 8);
-              const uint32_t b_lo = b_hi + 4u * uint32_t(kStALo - kStA);
-              tc_mma_tf32(tmem_d, sw32_desc(a_hi), sw32_desc(b_hi), idesc, accumulate);
-              tc_mma_tf32(tmem_d, sw32_desc(a_hi), sw32_desc(b_lo), idesc, 1u);
-              tc_mma_tf32(tmem_d, sw32_desc(a_lo), sw32_desc(b_hi), idesc, 1u);
-              accumulate = 1u;
-            }
-            c0 += kc;
-          }
-          mma_issued = true;
-        }
-        tc_commit(empty0 + 8u * s);  // frees the stage once these MMAs have read it
-      }
-      __syncwarp();
-      any = true;
       if (++s == D) {
         s = 0;
         ph ^= 1u;
       }
     }
     if (!ok) break;
-    // epilogue: D -> C (a block row with no blocks is stored as zeros)
-    if (issuer) tc_commit(accbar);
-    if (!wait_phase(accbar, accph, p, abort_flag, lane)) {
-      ok = false;
-      break;
-    }
-    accph ^= 1u;
-    tc_fence_after();
-    const int m = 16 * wq + lane;  // accumulator row = RHS column of this thread
-    const uint32_t taddr = tmem_d + (uint32_t(32 * wq) << 16);
-    const bool valid = lane < 16 && m < nw;
-    const bool store = !(CHECK && ((long long)c_row + h > p.M || n0 + nw > p.rhs));
-    if (CHECK && !store && tid == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, c_row);
-    float* dst = p.C + (long long)(n0 + m) * p.M + c_row;
-    for (int c = 0; c < h; c += 8) {
-      float v[8];
-      tc_ld8(taddr + uint32_t(c), v);
-      if (!any || (p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
-      }
-      if (valid && store) {
-        reinterpret_cast<float4*>(dst + c)[0] = make_float4(v[0], v[1], v[2], v[3]);
-        reinterpret_cast<float4*>(dst + c)[1] = make_float4(v[4], v[5], v[6], v[7]);
-      }
-    }
-    tc_fence_before();
+    if (lane == 0) tc_commit(tb.acc0 + 8u * buf);  // the item's accumulator is complete
     __syncwarp();
-    if (lane == 0) mbar_arrive(accfree);  // this warp is done with the accumulator
-    ++items_done;
+    ++j;
   }
-  (void)mma_issued;
-  // After an abort: wait (bounded) for the leader's copies and for every MMA issued so far.
-  if (leader && __shfl_sync(0xffffffffu, *abort_flag, 0)) {
-    if (issuer) tc_commit(accbar);
+  // Every MMA this warp issued has completed before the CTA releases its tensor memory (bounded).
+  if (lane == 0) tc_commit(tb.drain);
+  __syncwarp();
+  {
     const long long t0 = clock64();
-    while (!mbar_try(accbar, accph) && clock64() - t0 < p.wait_limit) {
+    while (!mbar_try(tb.drain, 0) && clock64() - t0 < p.wait_limit) {
     }
+  }
+  // After an abort also wait (bounded) for every copy still in flight.
+  if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
     for (int sl = 0; sl < D; ++sl) {
       if (!(is.filled & (1u << sl))) continue;
-      const uint32_t bar = full0 + 8u * sl;
+      const uint32_t bar = tb.full0 + 8u * sl;
       const uint32_t par = (is.lastpar >> sl) & 1u;
       const long long t1 = clock64();
       while (!mbar_try(bar, par) && clock64() - t1 < p.wait_limit) {
@@ -377,19 +441,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   float* stages = reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bars[2][kTcTeams][kMaxStages];
-  __shared__ __align__(8) uint64_t splitbars[kTcTeams][kMaxStages];
-  __shared__ __align__(8) uint64_t accbars[kTcTeams];
-  __shared__ __align__(8) uint64_t accfree[kTcTeams];
+  __shared__ __align__(8) uint64_t bars[3][kTcTeams][kMaxStages];  // full, empty, split
+  __shared__ __align__(8) uint64_t accbars[2][kTcTeams][2];        // acc done, acc free
+  __shared__ __align__(8) uint64_t drainbars[kTcTeams];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   const Task task = p.tasks[blockIdx.x];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t full_base = smem_addr(&bars[0][0][0]);
-  const uint32_t empty_base = smem_addr(&bars[1][0][0]);
-  const uint32_t split_base = smem_addr(&splitbars[0][0]);
-  const uint32_t acc_base = smem_addr(&accbars[0]);
-  const uint32_t accfree_base = smem_addr(&accfree[0]);
   if (warp == 0) {
     tc_alloc(smem_addr(&tmem_slot), kTmemAlloc);
     tc_relinquish();
@@ -398,12 +456,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     if (p.timing) p.timing[2 * blockIdx.x] = global_ns();
     for (int j = 0; j < kTcTeams; ++j) {
       for (int s = 0; s < task.stages; ++s) {
-        mbar_init(full_base + 8u * (j * kMaxStages + s), 1u);
-        mbar_init(empty_base + 8u * (j * kMaxStages + s), 1u);  // tcgen05.commit arrival
-        mbar_init(split_base + 8u * (j * kMaxStages + s), 4u);  // one arrival per team warp
+        mbar_init(smem_addr(&bars[0][j][s]), 1u);  // TMA: one arrival + transaction bytes
+        mbar_init(smem_addr(&bars[1][j][s]), 1u);  // tcgen05.commit
+        mbar_init(smem_addr(&bars[2][j][s]), 4u);  // one arrival per worker warp
       }
-      mbar_init(acc_base + 8u * j, 1u);
-      mbar_init(accfree_base + 8u * j, 4u);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(smem_addr(&accbars[0][j][b]), 1u);
+        mbar_init(smem_addr(&accbars[1][j][b]), 4u);
+      }
+      mbar_init(smem_addr(&drainbars[j]), 1u);
     }
     abort_flag = 0;
     mbar_fence_init();
@@ -412,8 +473,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
-  tc_run_team<CHECK>(p, task, stages, full_base, empty_base, split_base, acc_base, accfree_base,
-                     tmem_base, warp, lane, &abort_flag);
+  // warps 0..4*kTcTeams-1 are workers (team = warp/4, sub-partition = warp%4); the last kTcTeams
+  // warps are the teams' issuers
+  const bool worker = warp < 4 * kTcTeams;
+  const int team = worker ? (warp >> 2) : (warp - 4 * kTcTeams);
+  TeamBars tb;
+  tb.full0 = smem_addr(&bars[0][team][0]);
+  tb.empty0 = smem_addr(&bars[1][team][0]);
+  tb.split0 = smem_addr(&bars[2][team][0]);
+  tb.acc0 = smem_addr(&accbars[0][team][0]);
+  tb.accfree0 = smem_addr(&accbars[1][team][0]);
+  tb.drain = smem_addr(&drainbars[team]);
+  float* my = stages + team * task.stages * kTcStageFloats;
+  const uint32_t tmem_team = tmem_base + uint32_t(128 * team);
+  if (worker)
+    tc_worker<CHECK>(p, task, my, tb, tmem_team, team, warp & 3, lane, &abort_flag);
+  else
+    tc_issuer<CHECK>(p, task, my, tb, tmem_team, team, lane, &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
