@@ -205,7 +205,8 @@ vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit
 /* Per-CTA timing (no reference counterpart; a tuning aid): enable != 0 makes the following
  * executions record, for every CTA, its start and end on the GPU's global nanosecond timer.
  * If `out` is not NULL, synchronises `stream` and copies up to out_len values (start, end pairs in
- * CTA order) from the last timed execution. */
+ * CTA order) from the last timed execution; values past the first 2 * tasks are 16 per-CTA cycle
+ * counters that only an instrumented build (VBSR_PROF) fills, zero otherwise. */
 vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int out_len,
                                  vbsr_stream_t stream);
 /* Per-task schedule facts (a tuning aid): team size in warps and the planner's cost estimate of

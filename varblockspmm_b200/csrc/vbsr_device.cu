@@ -488,7 +488,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
     task.stages = stages;
     h_tasks.push_back(task);
     p->task_warps.push_back(4);
-    p->task_cost.push_back(std::max(load[t * kTcTeams], load[t * kTcTeams + 1]));
+    p->task_cost.push_back(*std::max_element(load.begin() + t * kTcTeams,
+                                             load.begin() + (t + 1) * kTcTeams));
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
@@ -851,9 +852,11 @@ vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int ou
   if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
   DeviceGuard guard(p->device);
   if (enable && p->d_timing == nullptr)
-    VBSR_CUDA(cudaMalloc(&p->d_timing, std::max(1, 2 * p->num_tasks) * sizeof(uint64_t)));
+    VBSR_CUDA(cudaMalloc(&p->d_timing, std::max(1, 18 * p->num_tasks) * sizeof(uint64_t)));
+  if (enable && out == nullptr)  // switching on: start from zeroed counters
+    VBSR_CUDA(cudaMemset(p->d_timing, 0, std::max(1, 18 * p->num_tasks) * sizeof(uint64_t)));
   if (out != nullptr && p->d_timing != nullptr) {
-    const int n = std::min(out_len, 2 * p->num_tasks);
+    const int n = std::min(out_len, 18 * p->num_tasks);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     VBSR_CUDA(cudaMemcpyAsync(out, p->d_timing, size_t(n) * sizeof(uint64_t),
                               cudaMemcpyDeviceToHost, s));

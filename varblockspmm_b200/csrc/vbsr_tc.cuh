@@ -8,8 +8,11 @@
 // tf32) and lo = x - hi (exact in fp32), and three MMAs accumulate hi*hi + hi*lo + lo*hi. The
 // dropped lo*lo term and the tf32 conversion of lo are below 2^-19 relative per product.
 //
-// CTA = two teams of four warps (warp w of a team sits in TMEM sub-partition w, so together the
-// four read all 64 accumulator rows), one CTA per SM. Each team walks its instruction stream (item
+// CTA = two teams, one CTA per SM. A team has four worker warps (warp w sits in TMEM sub-partition
+// w, so together they read all 64 accumulator rows) and two issuer warps. A single thread can issue
+// a tcgen05.mma only every ~55 cycles, while the tensor core overlaps MMAs from several issuers, so
+// the two issuers of a team take alternate 8-column groups, each into its own partial accumulator,
+// and the epilogue adds the two partials. Each team walks its instruction stream (item
 // headers and k-chunks, compiled by the planner; vbsr_internal.h) and owns a ring of D stages of
 // 32 block columns:
 //   * the team's leader warp issues the TMA copies D-1 stages ahead: A chunks with cp.async.bulk
@@ -36,8 +39,12 @@
 
 namespace vbsr_b200 {
 
-constexpr int kTcTeams = 2;                 // teams per CTA
-constexpr int kTcWarps = 5 * kTcTeams;      // per team: 4 worker warps + 1 issuer warp
+#ifndef VBSR_TC_TEAMS
+#define VBSR_TC_TEAMS 2
+#endif
+constexpr int kTcTeams = VBSR_TC_TEAMS;     // teams per CTA
+constexpr int kTcIssuers = 2;               // MMA-issuing warps per team
+constexpr int kTcWarps = (4 + kTcIssuers) * kTcTeams;  // per team: 4 worker warps + issuers
 constexpr int kTcThreads = 32 * kTcWarps;
 constexpr int kTcCols = 32;                 // block columns per stage
 constexpr int kTcM = 64;                    // MMA M (RHS columns, padded)
@@ -48,8 +55,11 @@ constexpr int kStB = 2 * 64 * kTcCols;
 constexpr int kBoxFloats = kTcM * 8;                    // one 8-column B box, padded to 64 rows
 constexpr int kStBLo = kStB + (kTcCols / 8) * kBoxFloats;
 constexpr int kTcStageFloats = kStBLo + (kTcCols / 8) * kBoxFloats;  // 8192 floats = 32 KB
-constexpr int kTmemCols = 2 * 64 * kTcTeams;            // two 64-column accumulators per team
-constexpr int kTmemAlloc = 256;                         // power of two >= kTmemCols
+// per team: 2 buffers (items alternate) x kTcIssuers partial accumulators x 64 columns
+constexpr int kTmemCols = 2 * kTcIssuers * 64 * kTcTeams;
+constexpr int kTmemAlloc = kTmemCols <= 128 ? 128 : (kTmemCols <= 256 ? 256 : 512);
+static_assert(kTmemCols <= 512, "tensor memory holds 512 columns");
+constexpr int kTeamTmem = 2 * kTcIssuers * 64;          // columns per team
 
 // ---- tcgen05 wrappers ------------------------------------------------------------------------------
 
@@ -211,6 +221,21 @@ __device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int
   }
 }
 
+// Optional cycle counters (instrumented builds only): per CTA 16 slots after the 2 * tasks
+// start/end timestamps of the timing buffer.
+#ifdef VBSR_PROF
+#define VBSR_PROF_T0(v) const long long v = clock64()
+#define VBSR_PROF_ADD(p, slot, t0)                                                          \
+  do {                                                                                     \
+    if ((p).timing && (threadIdx.x & 31) == 0)                                             \
+      atomicAdd((p).timing + 2 * gridDim.x + 16 * blockIdx.x + (slot),                     \
+                (unsigned long long)(clock64() - (t0)));                                   \
+  } while (0)
+#else
+#define VBSR_PROF_T0(v)
+#define VBSR_PROF_ADD(p, slot, t0) do { } while (0)
+#endif
+
 // Barriers of one team (shared-memory addresses).
 struct TeamBars {
   uint32_t full0, empty0, split0;  // per ring slot: TMA landed / MMAs done / hi-lo split done
@@ -224,15 +249,18 @@ struct TeamBars {
 template <bool CHECK>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const TeamBars& tb, int buf,
                                             uint32_t parity, uint32_t tmem_acc, int wq, int lane,
-                                            u64 hdr, bool any, volatile int* abort_flag) {
+                                            u64 hdr, int groups, volatile int* abort_flag) {
   if (!wait_phase(tb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
   tc_fence_after();
   const int h = hdr_h(hdr), nw = hdr_nw(hdr), n0 = hdr_n0(hdr), c_row = hdr_crow(hdr);
   const uint32_t taddr = tmem_acc + (uint32_t(32 * wq) << 16);
-  float v[64];
+  float v[64], u[64];
 #pragma unroll
   for (int c = 0; c < 8; ++c)
-    if (c * 8 < h) tc_ld8_nowait(taddr + uint32_t(8 * c), v + 8 * c);
+    if (c * 8 < h) {
+      tc_ld8_nowait(taddr + uint32_t(8 * c), v + 8 * c);
+      tc_ld8_nowait(taddr + 64u + uint32_t(8 * c), u + 8 * c);
+    }
   tc_wait_ld();
   tc_fence_before();
   __syncwarp();
@@ -241,15 +269,22 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const TeamBar
   const bool store = !(CHECK && ((long long)c_row + h > p.M || n0 + nw > p.rhs));
   if (CHECK && !store && wq == 0 && lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, c_row);
   if (lane < 16 && m < nw && store) {
-    const bool zero = !any || (p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+    // partial 0 holds the even 8-column groups, partial 1 the odd ones (if the item has any)
+    const float s0 = (groups > 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) ? 1.0f : 0.0f;
+    const float s1 = (groups > 1 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) ? 1.0f : 0.0f;
     float4* dst = reinterpret_cast<float4*>(p.C + (long long)(n0 + m) * p.M + c_row);
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       if (c * 8 < h) {
-        dst[2 * c] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
-                          : make_float4(v[8 * c], v[8 * c + 1], v[8 * c + 2], v[8 * c + 3]);
-        dst[2 * c + 1] = zero ? make_float4(0.f, 0.f, 0.f, 0.f)
-                              : make_float4(v[8 * c + 4], v[8 * c + 5], v[8 * c + 6], v[8 * c + 7]);
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = s0 != 0.0f ? v[8 * c + i] : 0.0f;
+          const float b = s1 != 0.0f ? u[8 * c + i] : 0.0f;
+          r[i] = a + b;
+        }
+        dst[2 * c] = make_float4(r[0], r[1], r[2], r[3]);
+        dst[2 * c + 1] = make_float4(r[4], r[5], r[6], r[7]);
       }
   }
   return true;
@@ -268,7 +303,9 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
   uint32_t ph = 0;
   int j = 0;
   u64 prev_hdr = 0;
-  bool prev_any = false, ok = true;
+  int prev_groups = 0;
+  bool ok = true;
+  VBSR_PROF_T0(t_all);
   while (ok && !win.done()) {
     const u64 hdr = win.peek();
     win.advance(p.stream, lane);
@@ -277,12 +314,15 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
       break;
     }
     const int h = hdr_h(hdr), nw = hdr_nw(hdr);
-    bool any = false;
+    int groups = 0;  // 8-column groups of the item (the issuers alternate over them)
     while (!win.done() && !is_header(win.peek())) {
+      VBSR_PROF_T0(t_w);
       if (!wait_phase(tb.full0 + 8u * s, ph, p, abort_flag, lane)) {
         ok = false;
         break;
       }
+      VBSR_PROF_ADD(p, 6, t_w);
+      VBSR_PROF_T0(t_s);
       int cols = 0;
       while (!win.done()) {
         const u64 ce = win.peek();
@@ -299,7 +339,8 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(tb.split0 + 8u * s);
-      any = true;
+      VBSR_PROF_ADD(p, 7, t_s);
+      groups += cols / 8;
       if (++s == D) {
         s = 0;
         ph ^= 1u;
@@ -308,29 +349,37 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
     if (!ok) break;
     if (j > 0) {
       const int pj = j - 1;
+      VBSR_PROF_T0(t_e);
+      const bool eok = true;
+      (void)eok;
       if (!tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1),
-                              tmem_team + uint32_t(64 * (pj & 1)), wq, lane, prev_hdr, prev_any,
-                              abort_flag)) {
+                              tmem_team + uint32_t(128 * (pj & 1)), wq, lane, prev_hdr,
+                              prev_groups, abort_flag)) {
         ok = false;
         break;
       }
+      VBSR_PROF_ADD(p, 9, t_e);
     }
     prev_hdr = hdr;
-    prev_any = any;
+    prev_groups = groups;
     ++j;
   }
   if (ok && j > 0) {
     const int pj = j - 1;
-    tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1), tmem_team + uint32_t(64 * (pj & 1)),
-                       wq, lane, prev_hdr, prev_any, abort_flag);
+    tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1), tmem_team + uint32_t(128 * (pj & 1)),
+                       wq, lane, prev_hdr, prev_groups, abort_flag);
   }
+  VBSR_PROF_ADD(p, 5, t_all);
 }
 
-// Issuer warp of a team: lane 0 issues each stage's MMAs once the workers have split it, the warp
-// keeps the TMA ring D-1 stages ahead.
+// Issuer warp `half` (0 or 1) of a team: lane 0 issues the MMAs of every other 8-column group
+// (those with group index % 2 == half, counted from the item's start) into its partial
+// accumulator once the workers have split the stage; issuer 0 also keeps the TMA ring D-1 stages
+// ahead.
 template <bool CHECK>
 __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, const TeamBars& tb,
-                          uint32_t tmem_team, int team, int lane, volatile int* abort_flag) {
+                          uint32_t tmem_team, int team, int half, int lane,
+                          volatile int* abort_flag) {
   const int D = task.stages;
   const int b = task.team_off[team], e = task.team_off[team + 1];
   StreamWin win;
@@ -345,32 +394,40 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
   is.issued = 0;
   is.win.init(p.stream, b, e, lane);
   bool ok = true;
-  for (int i = 0; i < D - 1 && ok; ++i)
+  const bool feeder = half == 0;  // issues the TMA copies
+  for (int i = 0; feeder && i < D - 1 && ok; ++i)
     ok = tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag);
   int s = 0;
   uint32_t ph = 0;
   int j = 0;
   const uint32_t sbase = smem_addr(my);
+  VBSR_PROF_T0(t_all);
   while (ok && !win.done()) {
     const u64 hdr = win.peek();
     win.advance(p.stream, lane);
     if (!is_header(hdr)) break;
     const int h = hdr_h(hdr);
     const int buf = j & 1;
-    const uint32_t tmem_d = tmem_team + uint32_t(64 * buf);
+    const uint32_t tmem_d = tmem_team + uint32_t(128 * buf + 64 * half);
+    VBSR_PROF_T0(t_f);
     if (j >= 2 && !wait_phase(tb.accfree0 + 8u * buf, uint32_t(((j - 2) >> 1) & 1), p, abort_flag,
                               lane)) {
       ok = false;
       break;
     }
+    VBSR_PROF_ADD(p, 3, t_f);
     tc_fence_after();
     const uint32_t idesc = tf32_idesc(kTcM, h);
     uint32_t accumulate = 0;
+    int gi = 0;  // group index within the item
     while (!win.done() && !is_header(win.peek())) {
+      VBSR_PROF_T0(t_sp);
       if (!wait_phase(tb.split0 + 8u * s, ph, p, abort_flag, lane)) {
         ok = false;
         break;
       }
+      VBSR_PROF_ADD(p, 1, t_sp);
+      VBSR_PROF_T0(t_m);
       tc_fence_after();
       // descriptors of the stage's first 8-column group; advance by fixed strides
       const uint32_t st = sbase + 4u * uint32_t(s * kTcStageFloats);
@@ -383,28 +440,28 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
         const int kc = chk_kc(ce);
         uint64_t b_hi = sw32_desc(st + 4u * uint32_t(kStA + h * c0));
         const uint64_t lo_delta_b = uint64_t((4u * (kStALo - kStA)) >> 4);
-        if (lane == 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-          for (int g = 0; g < kc / 8; ++g) {
+        for (int g = 0; g < kc / 8; ++g, ++gi) {
+          if (lane == 0 && (gi & 1) == half && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
             tc_mma_tf32(tmem_d, a_hi, b_hi, idesc, accumulate);
             tc_mma_tf32(tmem_d, a_hi, b_hi + lo_delta_b, idesc, 1u);
             tc_mma_tf32(tmem_d, a_hi + lo_delta_a, b_hi, idesc, 1u);
             accumulate = 1u;
-            a_hi += uint64_t((4u * kBoxFloats) >> 4);
-            b_hi += uint64_t((4u * 8u * uint32_t(h)) >> 4);
           }
-        } else {
-          a_hi += uint64_t((kc / 8) * ((4u * kBoxFloats) >> 4));
+          a_hi += uint64_t((4u * kBoxFloats) >> 4);
+          b_hi += uint64_t((4u * 8u * uint32_t(h)) >> 4);
         }
-        accumulate = 1u;
         c0 += kc;
         if (chk_stage_end(ce)) break;
       }
       if (lane == 0) tc_commit(tb.empty0 + 8u * s);  // frees the slot once these MMAs read it
       __syncwarp();
-      if (!tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag)) {
+      VBSR_PROF_ADD(p, 4, t_m);
+      VBSR_PROF_T0(t_i);
+      if (feeder && !tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag)) {
         ok = false;
         break;
       }
+      VBSR_PROF_ADD(p, 2, t_i);
       if (++s == D) {
         s = 0;
         ph ^= 1u;
@@ -415,6 +472,7 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
     __syncwarp();
     ++j;
   }
+  VBSR_PROF_ADD(p, 0, t_all);
   // Every MMA this warp issued has completed before the CTA releases its tensor memory (bounded).
   if (lane == 0) tc_commit(tb.drain);
   __syncwarp();
@@ -457,14 +515,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     for (int j = 0; j < kTcTeams; ++j) {
       for (int s = 0; s < task.stages; ++s) {
         mbar_init(smem_addr(&bars[0][j][s]), 1u);  // TMA: one arrival + transaction bytes
-        mbar_init(smem_addr(&bars[1][j][s]), 1u);  // tcgen05.commit
+        mbar_init(smem_addr(&bars[1][j][s]), uint32_t(kTcIssuers));  // tcgen05.commit per issuer
         mbar_init(smem_addr(&bars[2][j][s]), 4u);  // one arrival per worker warp
       }
       for (int b = 0; b < 2; ++b) {
-        mbar_init(smem_addr(&accbars[0][j][b]), 1u);
+        mbar_init(smem_addr(&accbars[0][j][b]), uint32_t(kTcIssuers));
         mbar_init(smem_addr(&accbars[1][j][b]), 4u);
       }
-      mbar_init(smem_addr(&drainbars[j]), 1u);
+      mbar_init(smem_addr(&drainbars[j]), uint32_t(kTcIssuers));
     }
     abort_flag = 0;
     mbar_fence_init();
@@ -473,10 +531,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
-  // warps 0..4*kTcTeams-1 are workers (team = warp/4, sub-partition = warp%4); the last kTcTeams
-  // warps are the teams' issuers
+  // warps 0..4*kTcTeams-1 are workers (team = warp/4, sub-partition = warp%4); the remaining
+  // warps are the teams' issuers (kTcIssuers consecutive warps per team)
   const bool worker = warp < 4 * kTcTeams;
-  const int team = worker ? (warp >> 2) : (warp - 4 * kTcTeams);
+  const int iw = warp - 4 * kTcTeams;
+  const int team = worker ? (warp >> 2) : (iw / kTcIssuers);
   TeamBars tb;
   tb.full0 = smem_addr(&bars[0][team][0]);
   tb.empty0 = smem_addr(&bars[1][team][0]);
@@ -485,11 +544,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   tb.accfree0 = smem_addr(&accbars[1][team][0]);
   tb.drain = smem_addr(&drainbars[team]);
   float* my = stages + team * task.stages * kTcStageFloats;
-  const uint32_t tmem_team = tmem_base + uint32_t(128 * team);
+  const uint32_t tmem_team = tmem_base + uint32_t(kTeamTmem * team);
   if (worker)
     tc_worker<CHECK>(p, task, my, tb, tmem_team, team, warp & 3, lane, &abort_flag);
   else
-    tc_issuer<CHECK>(p, task, my, tb, tmem_team, team, lane, &abort_flag);
+    tc_issuer<CHECK>(p, task, my, tb, tmem_team, team, iw % kTcIssuers, lane, &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
