@@ -366,7 +366,7 @@ struct vbsr_plan {
   int num_tasks = 0;
   int smem_bytes = 0;
   int64_t stream_entries = 0;
-  unsigned long long* d_stream = nullptr;
+  StageDesc* d_stream = nullptr;
   Task* d_tasks = nullptr;
   int* d_status = nullptr;
   unsigned long long* d_timing = nullptr;  // allocated on first request
@@ -405,7 +405,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   const int rhs = p->rhs;
   int num_sm = 148;
   VBSR_CUDA(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, d.device));
-  if (d.nvalues >= entry::kMaxVal || d.K >= entry::kMaxCol || d.M >= (int64_t(1) << 31))
+  if (d.nvalues >= stage::kMaxVal || d.K >= stage::kMaxCol || d.M >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "matrix exceeds the schedule's index range");
 
   const int R = d.block_rows;
@@ -446,11 +446,12 @@ vbsr_status build_schedule(vbsr_plan* p) {
     heap.push(l);
   }
 
-  std::vector<unsigned long long> stream;
+  std::vector<StageDesc> stream;
   stream.reserve(size_t(R) + size_t(d.nnzb) * 2);
   std::vector<Task> h_tasks;
   const int stages = std::min(kMaxStages, kSmemBudget / (kTcTeams * kTcStageFloats * 4));
   if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
+  const uint64_t nwc = uint64_t(stage::nw_code(rhs));
   for (int t = 0; t < ctas; ++t) {
     Task task{};
     for (int j = 0; j < kTcTeams; ++j) {
@@ -459,10 +460,14 @@ vbsr_status build_schedule(vbsr_plan* p) {
       std::sort(l.begin(), l.end());
       for (int i : l) {
         const int h = d.h_row_size[i];
-        stream.push_back(entry::header(d.h_row_off[i], h, 0, rhs));
-        // k-chunks packed greedily into stages of kTcCols columns; a chunk never straddles two
+        const uint64_t base0 = (uint64_t(h / 8 - 1) << 32) | (nwc << 39);
+        const uint64_t w1 = uint64_t(d.h_row_off[i]);
+        const size_t item_first = stream.size();
+        // k-chunks packed greedily into stages of kTcCols columns; a chunk never straddles two.
+        // A stage's chunks are consecutive in the value array, so its A is one contiguous range.
         int64_t val = d.h_val_off_row[i];
         int used = 0;
+        StageDesc cur{};
         for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
           const uint32_t desc = d.h_blk_desc[b];
           const int w = int((desc & 7u) + 1u) * 8;
@@ -470,24 +475,44 @@ vbsr_status build_schedule(vbsr_plan* p) {
           for (int k0 = 0; k0 < w; k0 += kChunk) {
             const int kc = std::min(kChunk, w - k0);
             if (used > 0 && used + kc > kTcCols) {
-              stream.back() |= entry::kLastOfStage;
+              cur.w[0] |= uint64_t(used / 8 - 1) << 28;
+              stream.push_back(cur);
               used = 0;
             }
-            stream.push_back(entry::chunk(val, col, w, k0, kc, false));
+            if (used == 0) {
+              cur = StageDesc{};
+              cur.w[0] = base0 | uint64_t((val + int64_t(h) * k0) / 64);
+              cur.w[1] = w1;
+            }
+            for (int g = 0; g < kc / 8; ++g) {
+              const int gg = used / 8 + g;
+              const uint64_t c8 = uint64_t((col + k0 + 8 * g) / 8);
+              cur.w[2 + gg / 2] |= c8 << (32 * (gg & 1));
+            }
             used += kc;
           }
           val += int64_t(h) * w;
         }
-        if (used > 0) stream.back() |= entry::kLastOfStage;
+        if (used > 0) {
+          cur.w[0] |= uint64_t(used / 8 - 1) << 28;
+          stream.push_back(cur);
+        } else {  // a block row without blocks: one empty stage, its C rows become zeros
+          StageDesc e{};
+          e.w[0] = base0 | stage::kEmpty;
+          e.w[1] = w1;
+          stream.push_back(e);
+        }
+        stream[item_first].w[0] |= stage::kFirst;
+        stream.back().w[0] |= stage::kLast;
       }
     }
     for (int j = kTcTeams; j <= 8; ++j) task.team_off[j] = int(stream.size());
-    task.team_warps = 4;
+    task.team_warps = 4 + kTcIssuers;
     task.stage_floats = kTcStageFloats;
     task.stage_cols = kTcCols;
     task.stages = stages;
     h_tasks.push_back(task);
-    p->task_warps.push_back(4);
+    p->task_warps.push_back(4 + kTcIssuers);
     p->task_cost.push_back(*std::max_element(load.begin() + t * kTcTeams,
                                              load.begin() + (t + 1) * kTcTeams));
   }
@@ -499,17 +524,17 @@ vbsr_status build_schedule(vbsr_plan* p) {
 
   char buf[512];
   std::snprintf(buf, sizeof buf,
-                "rhs=%d items=%d stream_entries=%zu tasks=%d teams=%d stages=%d smem=%d sms=%d "
+                "rhs=%d items=%d pipeline_stages=%zu tasks=%d teams=%d ring=%d smem=%d sms=%d "
                 "kernel=tcgen05-3xtf32",
                 rhs, R, stream.size(), p->num_tasks, teams, stages, p->smem_bytes, num_sm);
   p->summary = buf;
 
   DeviceGuard guard(d.device);
-  VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(uint64_t)));
+  VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
   VBSR_CUDA(cudaMalloc(&p->d_tasks, std::max<size_t>(1, h_tasks.size()) * sizeof(Task)));
   VBSR_CUDA(cudaMalloc(&p->d_status, kStatusWords * sizeof(int)));
   if (!stream.empty())
-    VBSR_CUDA(cudaMemcpy(p->d_stream, stream.data(), stream.size() * sizeof(uint64_t),
+    VBSR_CUDA(cudaMemcpy(p->d_stream, stream.data(), stream.size() * sizeof(StageDesc),
                          cudaMemcpyHostToDevice));
   if (!h_tasks.empty())
     VBSR_CUDA(cudaMemcpy(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
@@ -686,7 +711,7 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   if (st != VBSR_OK) return st;
   st = encode_b_map(&kp.b_half, B, d.K, p->rhs, p->rhs > 8 ? p->rhs / 2 : p->rhs);
   if (st != VBSR_OK) return st;
-  kp.stream = p->d_stream;
+  kp.stages = p->d_stream;
   kp.tasks = p->d_tasks;
   kp.values = d.d_values;
   kp.B = B;
@@ -775,7 +800,7 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
   if (st != VBSR_OK) return st;
   st = encode_b_map(&kp.b_half, B, d.K, p->rhs, p->rhs > 8 ? p->rhs / 2 : p->rhs);
   if (st != VBSR_OK) return st;
-  kp.stream = p->d_stream;
+  kp.stages = p->d_stream;
   kp.tasks = p->d_tasks;
   kp.values = d.d_values;
   kp.B = B;

@@ -15,43 +15,40 @@ vbsr_status set_error(vbsr_status s, const std::string& msg);
 void clear_error();
 
 // ---- work schedule ---------------------------------------------------------------------------
-// The plan compiles the matrix into one instruction stream per team: a sequence of 64-bit entries,
-// an item header followed by that item's k-chunks (one chunk = at most kChunk block columns of one
-// block), then the next header, and so on. Producer and consumers of a team walk the same stream.
-//
-// Header (bit 63 = 1): an h x nw tile of C starting at scalar row c_row, RHS columns [n0, n0+nw)
-//   bits  0..30 c_row       bits 31..33 h/8 - 1      bits 34..36 n0/8     bits 37..38 log2(nw/8)
-// Chunk  (bit 63 = 0): block columns [k0, k0+kc) of one block of that item (one contiguous k-chunk
-// of the device value format, kc <= 32). Consecutive chunks of an item are packed into one
-// pipeline stage of up to Task::stage_cols columns; bit 62 marks the last chunk of a stage.
-//   bits  0..27 val/64  (value offset of the block; blocks start at multiples of 64 floats)
-//   bits 28..55 (col + k0)/8   (first scalar column of the chunk in B)
-//   bits 56..58 w/8 - 1        bit 59 k0/32     bits 60..61 kc/8 - 1     bit 62 last chunk of stage
-namespace entry {
-constexpr uint64_t kHeader = 1ull << 63;
-constexpr uint64_t kLastOfStage = 1ull << 62;
-inline uint64_t header(int64_t c_row, int h, int n0, int nw) {
+// The plan compiles the matrix into one list of pipeline stages per team. A stage covers up to
+// kTcCols (32) consecutive block columns of one work item (one block row: an h x nw tile of C).
+// Because a block row's blocks are contiguous in the value array and each block's k-chunks are
+// stored in order, the A values of a stage are one contiguous range; B is one 8-column box per
+// 8-column group. A block row with no blocks is one "empty" stage (C rows stored as zeros).
+// Descriptor, 4 x 64 bits:
+//   w0: bits  0..27 A start / 64 (value offsets of blocks and chunks are multiples of 64 floats)
+//       bits 28..29 columns/8 - 1   bit 30 first stage of the item   bit 31 last stage of the item
+//       bits 32..34 h/8 - 1         bit 35 empty item   bits 36..38 n0/8   bits 39..40 log2(nw/8)
+//   w1: bits  0..30 c_row (first scalar row of the tile in C)
+//   w2: group 0 column / 8 (bits 0..27), group 1 column / 8 (bits 32..59)
+//   w3: group 2 column / 8, group 3 column / 8
+struct alignas(32) StageDesc {
+  uint64_t w[4];
+};
+static_assert(sizeof(StageDesc) == 32, "StageDesc layout");
+namespace stage {
+constexpr uint64_t kFirst = 1ull << 30, kLast = 1ull << 31, kEmpty = 1ull << 35;
+constexpr int64_t kMaxVal = (int64_t(1) << 28) * 64;  // value offsets must stay below this
+constexpr int64_t kMaxCol = (int64_t(1) << 28) * 8;   // scalar columns must stay below this
+inline int nw_code(int nw) {
   int lg = 0;
   while ((8 << lg) < nw) ++lg;
-  return kHeader | uint64_t(c_row) | (uint64_t(h / 8 - 1) << 31) | (uint64_t(n0 / 8) << 34) |
-         (uint64_t(lg) << 37);
+  return lg;
 }
-inline uint64_t chunk(int64_t val, int64_t col, int w, int k0, int kc, bool last) {
-  return uint64_t(val / 64) | (uint64_t((col + k0) / 8) << 28) | (uint64_t(w / 8 - 1) << 56) |
-         (uint64_t(k0 / 32) << 59) | (uint64_t(kc / 8 - 1) << 60) | (last ? kLastOfStage : 0);
-}
-constexpr int64_t kMaxVal = (int64_t(1) << 28) * 64;  // value offsets must stay below this
-constexpr int64_t kMaxCol = (int64_t(1) << 28) * 8;
-}  // namespace entry
+}  // namespace stage
 
-// One CTA task: kConsumerWarps / team_warps teams; team t walks stream entries
-// [team_off[t], team_off[t+1]).
+// One CTA task: team t walks stage descriptors [team_off[t], team_off[t+1]).
 struct alignas(16) Task {
   int team_off[9];
-  int team_warps;     // 1, 2 or 4
+  int team_warps;     // warps per team
   int stages;         // ring depth per team
   int stage_floats;   // floats per stage
-  int stage_cols;     // block columns one stage holds (32 or 64)
+  int stage_cols;     // block columns one stage holds
   int pad[3];
 };
 static_assert(sizeof(Task) == 64, "Task layout");

@@ -1,6 +1,5 @@
 // vbsr_kernels_common.cuh — pieces shared by the engine's kernels: launch parameters, the
-// per-team instruction-stream entries and their register windows, bounded mbarrier waits, the
-// status word, and the team's issue cursor.
+// per-team stage descriptors and their register windows, bounded mbarrier waits, the status word.
 #pragma once
 #include <cuda.h>
 
@@ -16,58 +15,75 @@ typedef unsigned long long u64;
 
 struct KernelParams {
   CUtensorMap b_full;   // B as a K x rhs tensor, box 8 columns x rhs rows
-  CUtensorMap b_half;   // same, box 8 columns x rhs/2 rows (items of split rows)
-  const u64* stream;    // per-team instruction streams
+  CUtensorMap b_half;   // same, box 8 columns x rhs/2 rows
+  const StageDesc* stages;  // per-team stage descriptors
   const Task* tasks;
-  const float* values;  // re-laid-out values
+  const float* values;  // device-format values
   const float* B;
   float* C;
   long long M, K, nvalues;
   int rhs;
   int* status;
-  int drop_stage;       // debug: chunk number (per CTA, team 0) the producer withholds; < 0 off
+  int drop_stage;       // debug: stage number (team 0 of each CTA) whose copies are withheld
   long long wait_limit; // SM clocks a single wait may take before it is declared stalled
   u64* timing;          // optional: per CTA (start, end) global timer in ns
   int diag;             // VBSR_PLAN_DIAG_* bits (performance analysis only)
 };
 
-// ---- stream entries ------------------------------------------------------------------------------
+// ---- stage descriptors -----------------------------------------------------------------------------
 
-__device__ __forceinline__ bool is_header(u64 e) { return (e >> 63) != 0; }
-__device__ __forceinline__ int hdr_crow(u64 e) { return int(e & 0x7fffffffull); }
-__device__ __forceinline__ int hdr_h(u64 e) { return int(((e >> 31) & 7u) + 1u) * 8; }
-__device__ __forceinline__ int hdr_n0(u64 e) { return int((e >> 34) & 7u) * 8; }
-__device__ __forceinline__ int hdr_nw(u64 e) { return 8 << int((e >> 37) & 3u); }
-__device__ __forceinline__ long long chk_val(u64 e) { return (long long)(e & 0xfffffffull) * 64; }
-__device__ __forceinline__ long long chk_colk(u64 e) { return (long long)((e >> 28) & 0xfffffffull) * 8; }
-__device__ __forceinline__ int chk_w(u64 e) { return int(((e >> 56) & 7u) + 1u) * 8; }
-__device__ __forceinline__ int chk_k0(u64 e) { return int((e >> 59) & 1u) * 32; }
-__device__ __forceinline__ int chk_kc(u64 e) { return int(((e >> 60) & 3u) + 1u) * 8; }
-__device__ __forceinline__ bool chk_stage_end(u64 e) { return ((e >> 62) & 1u) != 0; }
+struct Stage {
+  u64 w0, w1, w2, w3;
+  __device__ __forceinline__ long long a_start() const { return (long long)(w0 & 0xfffffffull) * 64; }
+  __device__ __forceinline__ int cols() const { return int(((w0 >> 28) & 3u) + 1u) * 8; }
+  __device__ __forceinline__ bool first() const { return (w0 >> 30) & 1u; }
+  __device__ __forceinline__ bool last() const { return (w0 >> 31) & 1u; }
+  __device__ __forceinline__ int h() const { return int(((w0 >> 32) & 7u) + 1u) * 8; }
+  __device__ __forceinline__ bool empty() const { return (w0 >> 35) & 1u; }
+  __device__ __forceinline__ int n0() const { return int((w0 >> 36) & 7u) * 8; }
+  __device__ __forceinline__ int nw() const { return 8 << int((w0 >> 39) & 3u); }
+  __device__ __forceinline__ int c_row() const { return int(w1 & 0x7fffffffull); }
+  __device__ __forceinline__ int group_col(int g) const {  // scalar column of 8-column group g
+    const u64 w = g < 2 ? w2 : w3;
+    return int((w >> (32 * (g & 1))) & 0xfffffffull) * 8;
+  }
+};
 
-// A team stream [pos, end) seen through a window of 32 entries (lane i holds entry wbase + i) and
-// the following window, loaded one window ahead. All lanes keep identical pos/wbase/end.
-struct StreamWin {
-  u64 cur, next;
+// A team's stage list [pos, end) seen through a window of 32 descriptors (lane i holds stage
+// wbase + i) and the following window, loaded one window ahead; reading a stage is four
+// independent shuffles. All lanes keep identical pos / wbase / end.
+struct StageWin {
+  ulonglong4 cur, next;
   int pos, wbase, end;
 
-  __device__ __forceinline__ void init(const u64* s, int b, int e, int lane) {
+  __device__ __forceinline__ static ulonglong4 load(const StageDesc* s, int i, int end) {
+    if (i >= end) return make_ulonglong4(0, 0, 0, 0);
+    const ulonglong2* q = reinterpret_cast<const ulonglong2*>(s + i);
+    const ulonglong2 a = __ldg(q), b = __ldg(q + 1);
+    return make_ulonglong4(a.x, a.y, b.x, b.y);
+  }
+  __device__ __forceinline__ void init(const StageDesc* s, int b, int e, int lane) {
     pos = b;
     wbase = b;
     end = e;
-    cur = (b + lane < e) ? __ldg(s + b + lane) : 0ull;
-    next = (b + 32 + lane < e) ? __ldg(s + b + 32 + lane) : 0ull;
+    cur = load(s, b + lane, e);
+    next = load(s, b + 32 + lane, e);
   }
   __device__ __forceinline__ bool done() const { return pos >= end; }
-  __device__ __forceinline__ u64 peek() const {
-    return __shfl_sync(0xffffffffu, cur, (pos - wbase) & 31);
+  __device__ __forceinline__ Stage peek() const {
+    const int src = (pos - wbase) & 31;
+    Stage st;
+    st.w0 = __shfl_sync(0xffffffffu, cur.x, src);
+    st.w1 = __shfl_sync(0xffffffffu, cur.y, src);
+    st.w2 = __shfl_sync(0xffffffffu, cur.z, src);
+    st.w3 = __shfl_sync(0xffffffffu, cur.w, src);
+    return st;
   }
-  __device__ __forceinline__ void advance(const u64* s, int lane) {
+  __device__ __forceinline__ void advance(const StageDesc* s, int lane) {
     if (++pos - wbase == 32) {
       wbase += 32;
       cur = next;
-      const int i = wbase + 32 + lane;
-      next = (i < end) ? __ldg(s + i) : 0ull;
+      next = load(s, wbase + 32 + lane, end);
     }
   }
 };
@@ -114,16 +130,6 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
 // ---- producer side (run by each team's leader warp) ----------------------------------------------
 
 // Issue cursor of a team: walks the team's stream ahead of the consumers.
-struct Issuer {
-  StreamWin win;
-  int h, n0, nw;        // item the cursor is in
-  int slot;             // next ring slot
-  uint32_t ph;          // ring phase of that slot
-  uint32_t filled;      // bit s: slot s has been filled at least once
-  uint32_t lastpar;     // bit s: phase parity of the last fill of slot s
-  int issued;           // chunks issued so far (debug drop hook)
-};
-
 __device__ __forceinline__ u64 global_ns() {
   u64 t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -12,12 +12,12 @@
 // w, so together they read all 64 accumulator rows) and two issuer warps. A single thread can issue
 // a tcgen05.mma only every ~55 cycles, while the tensor core overlaps MMAs from several issuers, so
 // the two issuers of a team take alternate 8-column groups, each into its own partial accumulator,
-// and the epilogue adds the two partials. Each team walks its instruction stream (item
-// headers and k-chunks, compiled by the planner; vbsr_internal.h) and owns a ring of D stages of
-// 32 block columns:
-//   * the team's leader warp issues the TMA copies D-1 stages ahead: A chunks with cp.async.bulk
-//     (the device format already holds each chunk as the K-major 32-byte-swizzled operand tile the
-//     MMA reads), B with 2-D cp.async.bulk.tensor boxes of 8 columns x nw rows, SWIZZLE_32B;
+// and the epilogue adds the two partials. Each team walks its list of stage descriptors (compiled
+// by the planner; vbsr_internal.h) and owns a ring of D stages of 32 block columns:
+//   * issuer 0 keeps the TMA ring D-1 stages ahead: the stage's A values with one cp.async.bulk
+//     (contiguous in the device format, which already holds every 8-column group as the K-major
+//     32-byte-swizzled operand tile the MMA reads), B with one 2-D cp.async.bulk.tensor box of
+//     8 columns x nw rows (SWIZZLE_32B) per group;
 //   * when a stage lands, the team's 128 threads split A and B into hi (in place) and lo (a second
 //     buffer), fence the generic-proxy writes for the async proxy and arrive on the stage's
 //     "split" mbarrier (one arrival per warp; no named barriers, so every wait stays bounded);
@@ -133,93 +133,14 @@ __device__ __forceinline__ uint32_t tf32_idesc(int m, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-// ---- producer side (team leader warp) ----------------------------------------------------------
+// ---- team pieces --------------------------------------------------------------------------------
 
-template <bool CHECK>
-__device__ __forceinline__ bool tc_issue_next(const KernelParams& p, Issuer& is, float* team_stages,
-                                              int D, uint32_t full0, uint32_t empty0, int team,
-                                              int lane, volatile int* abort_flag) {
-  while (!is.win.done()) {
-    const u64 e = is.win.peek();
-    if (!is_header(e)) break;
-    is.h = hdr_h(e);
-    is.n0 = hdr_n0(e);
-    is.nw = hdr_nw(e);
-    is.win.advance(p.stream, lane);
-  }
-  if (is.win.done()) return true;
-  const int s = is.slot;
-  const uint32_t full_bar = full0 + 8u * s;
-  if (!wait_phase(empty0 + 8u * s, is.ph ^ 1u, p, abort_flag, lane)) return false;
-  const int h = is.h, nw = is.nw, n0 = is.n0;
-  const bool drop = (team == 0 && is.issued == p.drop_stage);
-  ++is.issued;
-  float* st = team_stages + s * kTcStageFloats;
-  const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
-  const bool copy = !drop && !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES);
-  bool in_bounds = true;
-  int c0 = 0;
-  while (!is.win.done()) {  // the stage's chunks (ends at a stage-end mark)
-    const u64 e = is.win.peek();
-    is.win.advance(p.stream, lane);
-    const long long val = chk_val(e), colk = chk_colk(e);
-    const int w = chk_w(e), k0 = chk_k0(e), kc = chk_kc(e);
-    bool ok = true;
-    if (CHECK)
-      ok = val + (long long)h * w <= p.nvalues && colk - k0 + w <= p.K && n0 + nw <= p.rhs &&
-           c0 + kc <= kTcCols && h <= 64 && nw <= kTcM;
-    in_bounds = in_bounds && ok;
-    if (copy && ok) {
-      if (lane == 0) {
-        mbar_expect_tx(full_bar, uint32_t((h + nw) * 4 * kc));
-        bulk_g2s(smem_addr(st + kStA + h * c0), p.values + val + (long long)h * k0,
-                 uint32_t(h * 4 * kc), full_bar, policy_evict_first());
-      } else if (lane <= (kc >> 3)) {
-        const int g = lane - 1;
-        tensor2d_g2s(smem_addr(st + kStB + ((c0 >> 3) + g) * kBoxFloats), map, int(colk) + 8 * g,
-                     n0, full_bar, policy_evict_last());
-      }
-    }
-    c0 += kc;
-    if (chk_stage_end(e)) break;
-  }
-  if (!drop) {
-    if (lane == 0) {
-      if (!in_bounds) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
-      mbar_arrive(full_bar);  // the stage's bytes were announced chunk by chunk
-    }
-    if (copy) {
-      is.filled |= 1u << s;
-      is.lastpar = (is.lastpar & ~(1u << s)) | (is.ph << s);
-    }
-  }
-  if (++is.slot == D) {
-    is.slot = 0;
-    is.ph ^= 1u;
-  }
-  return true;
-}
-
-// ---- team ----------------------------------------------------------------------------------------
-
-// hi = x with the low 13 mantissa bits cleared, lo = x - hi, over n4 float4s at p (hi in place).
-__device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int tid) {
-  for (int i = tid; i < n4; i += 128) {
-    float4* ph = reinterpret_cast<float4*>(base) + i;
-    float4 x = *ph;
-    float4 hi, lo;
-    hi.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
-    hi.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
-    hi.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
-    hi.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
-    lo.x = x.x - hi.x;
-    lo.y = x.y - hi.y;
-    lo.z = x.z - hi.z;
-    lo.w = x.w - hi.w;
-    *ph = hi;
-    *reinterpret_cast<float4*>(base + lo_off + 4 * i) = lo;
-  }
-}
+// Barriers of one team (shared-memory addresses).
+struct TeamBars {
+  uint32_t full0, empty0, split0;  // per ring slot: TMA landed / MMAs done / hi-lo split done
+  uint32_t acc0, accfree0;         // per accumulator buffer: MMAs of the item done / D read
+  uint32_t drain;                  // end-of-kernel drain of the issuers' MMAs
+};
 
 // Optional cycle counters (instrumented builds only): per CTA 16 slots after the 2 * tasks
 // start/end timestamps of the timing buffer.
@@ -236,23 +157,103 @@ __device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int
 #define VBSR_PROF_ADD(p, slot, t0) do { } while (0)
 #endif
 
-// Barriers of one team (shared-memory addresses).
-struct TeamBars {
-  uint32_t full0, empty0, split0;  // per ring slot: TMA landed / MMAs done / hi-lo split done
-  uint32_t acc0, accfree0;         // per accumulator buffer: MMAs of the item done / D read
-  uint32_t drain;                  // abort drain
+// TMA feed cursor (issuer 0 of a team): runs D-1 non-empty stages ahead of the MMAs.
+struct Feeder {
+  StageWin win;
+  int slot;             // next ring slot
+  uint32_t ph;          // ring phase of that slot
+  uint32_t filled;      // bit s: slot s has been filled at least once
+  uint32_t lastpar;     // bit s: phase parity of the last fill of slot s
+  int issued;           // stages issued so far (debug drop hook)
 };
 
-// Epilogue of one item: D (accumulator buffer) -> C. Each worker warp reads its TMEM sub-partition;
-// thread `lane` < 16 of warp wq holds accumulator row m = 16*wq + lane = RHS column n0 + m, i.e.
-// C[c_row .. c_row+h-1, n0+m], stored as h consecutive floats.
+// Issues the copies of the next non-empty stage into the next ring slot, after the MMAs of the
+// slot's previous stage have completed. Warp-collective. Returns false on abort.
+template <bool CHECK>
+__device__ __forceinline__ bool feed_next(const KernelParams& p, Feeder& f, float* team_stages,
+                                          int D, const TeamBars& tb, int team, int lane,
+                                          volatile int* abort_flag) {
+  while (!f.win.done() && f.win.peek().empty()) f.win.advance(p.stages, lane);
+  if (f.win.done()) return true;
+  const Stage st = f.win.peek();
+  f.win.advance(p.stages, lane);
+  const int s = f.slot;
+  const uint32_t full_bar = tb.full0 + 8u * s;
+  if (!wait_phase(tb.empty0 + 8u * s, f.ph ^ 1u, p, abort_flag, lane)) return false;
+  const int h = st.h(), nw = st.nw(), n0 = st.n0(), cols = st.cols();
+  const long long a0 = st.a_start();
+  const bool drop = (team == 0 && f.issued == p.drop_stage);
+  ++f.issued;
+  bool ok = true;
+  if (CHECK) {
+    ok = a0 + (long long)h * cols <= p.nvalues && n0 + nw <= p.rhs && nw <= kTcM;
+    for (int g = 0; g < cols / 8; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
+  }
+  if (drop) {
+    // withhold the stage entirely (debug): no arrival, no copies
+  } else if ((p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) || !ok) {
+    if (lane == 0) {
+      if (!ok) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+      mbar_arrive(full_bar);  // release the workers without touching memory
+    }
+  } else {
+    float* sp = team_stages + s * kTcStageFloats;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * cols));
+      bulk_g2s(smem_addr(sp + kStA), p.values + a0, uint32_t(h * 4 * cols), full_bar,
+               policy_evict_first());
+    } else if (lane <= (cols >> 3)) {
+      const int g = lane - 1;
+      const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
+      tensor2d_g2s(smem_addr(sp + kStB + g * kBoxFloats), map, st.group_col(g), n0, full_bar,
+                   policy_evict_last());
+    }
+    f.filled |= 1u << s;
+    f.lastpar = (f.lastpar & ~(1u << s)) | (f.ph << s);
+  }
+  if (++f.slot == D) {
+    f.slot = 0;
+    f.ph ^= 1u;
+  }
+  return true;
+}
+
+// hi = x with the low 13 mantissa bits cleared, lo = x - hi, over n4 float4s at base (hi in
+// place, lo at base + lo_off), spread over the team's 128 worker threads.
+__device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int tid) {
+  for (int i = tid; i < n4; i += 128) {
+    float4* ph = reinterpret_cast<float4*>(base) + i;
+    const float4 x = *ph;
+    float4 hi, lo;
+    hi.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    hi.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    hi.z = __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    hi.w = __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    lo.x = x.x - hi.x;
+    lo.y = x.y - hi.y;
+    lo.z = x.z - hi.z;
+    lo.w = x.w - hi.w;
+    *ph = hi;
+    *reinterpret_cast<float4*>(base + lo_off + 4 * i) = lo;
+  }
+}
+
+// An item as the workers remember it for the lagged epilogue.
+struct ItemInfo {
+  int h, nw, n0, c_row, groups;
+};
+
+// Epilogue of one item: D -> C. Each worker warp reads its TMEM sub-partition; thread `lane` < 16
+// of warp wq holds accumulator row m = 16*wq + lane = RHS column n0 + m, i.e.
+// C[c_row .. c_row+h-1, n0+m], stored as h consecutive floats. Partial 0 holds the even 8-column
+// groups, partial 1 (64 columns further) the odd ones.
 template <bool CHECK>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const TeamBars& tb, int buf,
                                             uint32_t parity, uint32_t tmem_acc, int wq, int lane,
-                                            u64 hdr, int groups, volatile int* abort_flag) {
+                                            const ItemInfo& it, volatile int* abort_flag) {
   if (!wait_phase(tb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
   tc_fence_after();
-  const int h = hdr_h(hdr), nw = hdr_nw(hdr), n0 = hdr_n0(hdr), c_row = hdr_crow(hdr);
+  const int h = it.h;
   const uint32_t taddr = tmem_acc + (uint32_t(32 * wq) << 16);
   float v[64], u[64];
 #pragma unroll
@@ -266,23 +267,20 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const TeamBar
   __syncwarp();
   if (lane == 0) mbar_arrive(tb.accfree0 + 8u * buf);  // this warp is done with the buffer
   const int m = 16 * wq + lane;
-  const bool store = !(CHECK && ((long long)c_row + h > p.M || n0 + nw > p.rhs));
-  if (CHECK && !store && wq == 0 && lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, c_row);
-  if (lane < 16 && m < nw && store) {
-    // partial 0 holds the even 8-column groups, partial 1 the odd ones (if the item has any)
-    const float s0 = (groups > 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) ? 1.0f : 0.0f;
-    const float s1 = (groups > 1 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) ? 1.0f : 0.0f;
-    float4* dst = reinterpret_cast<float4*>(p.C + (long long)(n0 + m) * p.M + c_row);
+  const bool store = !(CHECK && ((long long)it.c_row + h > p.M || it.n0 + it.nw > p.rhs));
+  if (CHECK && !store && wq == 0 && lane == 0)
+    record_status(p.status, VBSR_BOUNDS_VIOLATION, it.c_row);
+  if (lane < 16 && m < it.nw && store) {
+    const bool use0 = it.groups > 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+    const bool use1 = it.groups > 1 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+    float4* dst = reinterpret_cast<float4*>(p.C + (long long)(it.n0 + m) * p.M + it.c_row);
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       if (c * 8 < h) {
         float r[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = s0 != 0.0f ? v[8 * c + i] : 0.0f;
-          const float b = s1 != 0.0f ? u[8 * c + i] : 0.0f;
-          r[i] = a + b;
-        }
+        for (int i = 0; i < 8; ++i)
+          r[i] = (use0 ? v[8 * c + i] : 0.0f) + (use1 ? u[8 * c + i] : 0.0f);
         dst[2 * c] = make_float4(r[0], r[1], r[2], r[3]);
         dst[2 * c + 1] = make_float4(r[4], r[5], r[6], r[7]);
       }
@@ -297,25 +295,19 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
                           uint32_t tmem_team, int team, int wq, int lane, volatile int* abort_flag) {
   const int D = task.stages;
   const int tid = wq * 32 + lane;
-  StreamWin win;
-  win.init(p.stream, task.team_off[team], task.team_off[team + 1], lane);
+  StageWin win;
+  win.init(p.stages, task.team_off[team], task.team_off[team + 1], lane);
   int s = 0;
   uint32_t ph = 0;
-  int j = 0;
-  u64 prev_hdr = 0;
-  int prev_groups = 0;
+  int j = 0;  // items completed (stages seen with the last-of-item flag)
+  ItemInfo cur{8, 8, 0, 0, 0}, prev{8, 8, 0, 0, 0};
   bool ok = true;
   VBSR_PROF_T0(t_all);
   while (ok && !win.done()) {
-    const u64 hdr = win.peek();
-    win.advance(p.stream, lane);
-    if (!is_header(hdr)) {
-      if (lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, win.pos);
-      break;
-    }
-    const int h = hdr_h(hdr), nw = hdr_nw(hdr);
-    int groups = 0;  // 8-column groups of the item (the issuers alternate over them)
-    while (!win.done() && !is_header(win.peek())) {
+    const Stage st = win.peek();
+    win.advance(p.stages, lane);
+    if (st.first()) cur = ItemInfo{st.h(), st.nw(), st.n0(), st.c_row(), 0};
+    if (!st.empty()) {
       VBSR_PROF_T0(t_w);
       if (!wait_phase(tb.full0 + 8u * s, ph, p, abort_flag, lane)) {
         ok = false;
@@ -323,104 +315,97 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
       }
       VBSR_PROF_ADD(p, 6, t_w);
       VBSR_PROF_T0(t_s);
-      int cols = 0;
-      while (!win.done()) {
-        const u64 ce = win.peek();
-        win.advance(p.stream, lane);
-        cols += chk_kc(ce);
-        if (chk_stage_end(ce)) break;
-      }
-      float* st = my + s * kTcStageFloats;
+      const int cols = st.cols();
       if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-        split_hi_lo(st + kStA, kStALo - kStA, (h * cols) / 4, tid);
+        float* sp = my + s * kTcStageFloats;
+        split_hi_lo(sp + kStA, kStALo - kStA, (cur.h * cols) / 4, tid);
         for (int g = 0; g < cols / 8; ++g)
-          split_hi_lo(st + kStB + g * kBoxFloats, kStBLo - kStB, nw * 2, tid);
+          split_hi_lo(sp + kStB + g * kBoxFloats, kStBLo - kStB, cur.nw * 2, tid);
         fence_proxy_async_smem();
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(tb.split0 + 8u * s);
       VBSR_PROF_ADD(p, 7, t_s);
-      groups += cols / 8;
+      cur.groups += cols / 8;
       if (++s == D) {
         s = 0;
         ph ^= 1u;
       }
     }
-    if (!ok) break;
-    if (j > 0) {
-      const int pj = j - 1;
-      VBSR_PROF_T0(t_e);
-      const bool eok = true;
-      (void)eok;
-      if (!tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1),
-                              tmem_team + uint32_t(128 * (pj & 1)), wq, lane, prev_hdr,
-                              prev_groups, abort_flag)) {
-        ok = false;
-        break;
+    if (st.last()) {
+      if (j > 0) {
+        const int pj = j - 1;
+        VBSR_PROF_T0(t_e);
+        if (!tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1),
+                                tmem_team + uint32_t(128 * (pj & 1)), wq, lane, prev, abort_flag)) {
+          ok = false;
+          break;
+        }
+        VBSR_PROF_ADD(p, 9, t_e);
       }
-      VBSR_PROF_ADD(p, 9, t_e);
+      prev = cur;
+      ++j;
     }
-    prev_hdr = hdr;
-    prev_groups = groups;
-    ++j;
   }
   if (ok && j > 0) {
     const int pj = j - 1;
-    tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1), tmem_team + uint32_t(128 * (pj & 1)),
-                       wq, lane, prev_hdr, prev_groups, abort_flag);
+    tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1),
+                       tmem_team + uint32_t(128 * (pj & 1)), wq, lane, prev, abort_flag);
   }
   VBSR_PROF_ADD(p, 5, t_all);
 }
 
 // Issuer warp `half` (0 or 1) of a team: lane 0 issues the MMAs of every other 8-column group
-// (those with group index % 2 == half, counted from the item's start) into its partial
-// accumulator once the workers have split the stage; issuer 0 also keeps the TMA ring D-1 stages
-// ahead.
+// (group index % 2 == half, counted from the item's start) into its partial accumulator once the
+// workers have split the stage; issuer 0 also keeps the TMA ring D-1 stages ahead.
 template <bool CHECK>
 __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, const TeamBars& tb,
                           uint32_t tmem_team, int team, int half, int lane,
                           volatile int* abort_flag) {
   const int D = task.stages;
   const int b = task.team_off[team], e = task.team_off[team + 1];
-  StreamWin win;
-  win.init(p.stream, b, e, lane);
-  Issuer is;
-  is.h = 8;
-  is.n0 = 0;
-  is.nw = 8;
-  is.slot = 0;
-  is.ph = 0;
-  is.filled = is.lastpar = 0;
-  is.issued = 0;
-  is.win.init(p.stream, b, e, lane);
+  StageWin win;
+  win.init(p.stages, b, e, lane);
+  Feeder f;
+  f.slot = 0;
+  f.ph = 0;
+  f.filled = f.lastpar = 0;
+  f.issued = 0;
+  const bool feeder = half == 0;
   bool ok = true;
-  const bool feeder = half == 0;  // issues the TMA copies
-  for (int i = 0; feeder && i < D - 1 && ok; ++i)
-    ok = tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag);
+  if (feeder) {
+    f.win.init(p.stages, b, e, lane);
+    for (int i = 0; i < D - 1 && ok; ++i)
+      ok = feed_next<CHECK>(p, f, my, D, tb, team, lane, abort_flag);
+  }
   int s = 0;
   uint32_t ph = 0;
-  int j = 0;
+  int j = 0;  // items started
   const uint32_t sbase = smem_addr(my);
+  uint32_t tmem_d = tmem_team, idesc = 0, accumulate = 0;
+  int gi = 0, h = 8;
   VBSR_PROF_T0(t_all);
   while (ok && !win.done()) {
-    const u64 hdr = win.peek();
-    win.advance(p.stream, lane);
-    if (!is_header(hdr)) break;
-    const int h = hdr_h(hdr);
-    const int buf = j & 1;
-    const uint32_t tmem_d = tmem_team + uint32_t(128 * buf + 64 * half);
-    VBSR_PROF_T0(t_f);
-    if (j >= 2 && !wait_phase(tb.accfree0 + 8u * buf, uint32_t(((j - 2) >> 1) & 1), p, abort_flag,
-                              lane)) {
-      ok = false;
-      break;
+    const Stage st = win.peek();
+    win.advance(p.stages, lane);
+    if (st.first()) {
+      const int buf = j & 1;
+      tmem_d = tmem_team + uint32_t(128 * buf + 64 * half);
+      // the buffer's previous item (j-2) must have been read out by the workers
+      VBSR_PROF_T0(t_f);
+      if (j >= 2 && !wait_phase(tb.accfree0 + 8u * buf, uint32_t(((j - 2) >> 1) & 1), p,
+                                abort_flag, lane)) {
+        ok = false;
+        break;
+      }
+      VBSR_PROF_ADD(p, 3, t_f);
+      tc_fence_after();
+      h = st.h();
+      idesc = tf32_idesc(kTcM, h);
+      accumulate = 0;
+      gi = 0;
     }
-    VBSR_PROF_ADD(p, 3, t_f);
-    tc_fence_after();
-    const uint32_t idesc = tf32_idesc(kTcM, h);
-    uint32_t accumulate = 0;
-    int gi = 0;  // group index within the item
-    while (!win.done() && !is_header(win.peek())) {
+    if (!st.empty()) {
       VBSR_PROF_T0(t_sp);
       if (!wait_phase(tb.split0 + 8u * s, ph, p, abort_flag, lane)) {
         ok = false;
@@ -429,35 +414,32 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
       VBSR_PROF_ADD(p, 1, t_sp);
       VBSR_PROF_T0(t_m);
       tc_fence_after();
-      // descriptors of the stage's first 8-column group; advance by fixed strides
-      const uint32_t st = sbase + 4u * uint32_t(s * kTcStageFloats);
-      uint64_t a_hi = sw32_desc(st + 4u * kStB);
-      const uint64_t lo_delta_a = uint64_t((4u * (kStBLo - kStB)) >> 4);
-      int c0 = 0;
-      while (!win.done()) {
-        const u64 ce = win.peek();
-        win.advance(p.stream, lane);
-        const int kc = chk_kc(ce);
-        uint64_t b_hi = sw32_desc(st + 4u * uint32_t(kStA + h * c0));
-        const uint64_t lo_delta_b = uint64_t((4u * (kStALo - kStA)) >> 4);
-        for (int g = 0; g < kc / 8; ++g, ++gi) {
-          if (lane == 0 && (gi & 1) == half && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+      if (lane == 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+        const uint32_t sp = sbase + 4u * uint32_t(s * kTcStageFloats);
+        uint64_t a_hi = sw32_desc(sp + 4u * kStB);
+        uint64_t b_hi = sw32_desc(sp + 4u * kStA);
+        const uint64_t da_lo = uint64_t((4u * (kStBLo - kStB)) >> 4);
+        const uint64_t db_lo = uint64_t((4u * (kStALo - kStA)) >> 4);
+        const uint64_t da = uint64_t((4u * kBoxFloats) >> 4), db = uint64_t((32u * h) >> 4);
+        const int groups = st.cols() / 8;
+        for (int g = 0; g < groups; ++g, ++gi) {
+          if ((gi & 1) == half) {
             tc_mma_tf32(tmem_d, a_hi, b_hi, idesc, accumulate);
-            tc_mma_tf32(tmem_d, a_hi, b_hi + lo_delta_b, idesc, 1u);
-            tc_mma_tf32(tmem_d, a_hi + lo_delta_a, b_hi, idesc, 1u);
+            tc_mma_tf32(tmem_d, a_hi, b_hi + db_lo, idesc, 1u);
+            tc_mma_tf32(tmem_d, a_hi + da_lo, b_hi, idesc, 1u);
             accumulate = 1u;
           }
-          a_hi += uint64_t((4u * kBoxFloats) >> 4);
-          b_hi += uint64_t((4u * 8u * uint32_t(h)) >> 4);
+          a_hi += da;
+          b_hi += db;
         }
-        c0 += kc;
-        if (chk_stage_end(ce)) break;
+      } else {
+        gi += st.cols() / 8;
       }
       if (lane == 0) tc_commit(tb.empty0 + 8u * s);  // frees the slot once these MMAs read it
       __syncwarp();
       VBSR_PROF_ADD(p, 4, t_m);
       VBSR_PROF_T0(t_i);
-      if (feeder && !tc_issue_next<CHECK>(p, is, my, D, tb.full0, tb.empty0, team, lane, abort_flag)) {
+      if (feeder && !feed_next<CHECK>(p, f, my, D, tb, team, lane, abort_flag)) {
         ok = false;
         break;
       }
@@ -467,10 +449,11 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
         ph ^= 1u;
       }
     }
-    if (!ok) break;
-    if (lane == 0) tc_commit(tb.acc0 + 8u * buf);  // the item's accumulator is complete
-    __syncwarp();
-    ++j;
+    if (st.last()) {
+      if (lane == 0) tc_commit(tb.acc0 + 8u * (j & 1));  // the item's accumulator is complete
+      __syncwarp();
+      ++j;
+    }
   }
   VBSR_PROF_ADD(p, 0, t_all);
   // Every MMA this warp issued has completed before the CTA releases its tensor memory (bounded).
@@ -484,9 +467,9 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
   // After an abort also wait (bounded) for every copy still in flight.
   if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
     for (int sl = 0; sl < D; ++sl) {
-      if (!(is.filled & (1u << sl))) continue;
+      if (!(f.filled & (1u << sl))) continue;
       const uint32_t bar = tb.full0 + 8u * sl;
-      const uint32_t par = (is.lastpar >> sl) & 1u;
+      const uint32_t par = (f.lastpar >> sl) & 1u;
       const long long t1 = clock64();
       while (!mbar_try(bar, par) && clock64() - t1 < p.wait_limit) {
       }
