@@ -380,7 +380,7 @@ struct vbsr_plan {
 
 namespace {
 
-constexpr int kSmemBudget = 220 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
+constexpr int kSmemBudget = 224 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
 
 // Per-team time model of one item: the bytes its stages move (A and B) plus a fixed cost per stage
 // and per item, in bytes-equivalent units.
@@ -449,7 +449,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
   std::vector<StageDesc> stream;
   stream.reserve(size_t(R) + size_t(d.nnzb) * 2);
   std::vector<Task> h_tasks;
-  const int stages = std::min(kMaxStages, kSmemBudget / (kTcTeams * kTcStageFloats * 4));
+  const int stages = std::min(
+      kMaxStages, (kSmemBudget / kTcTeams - kTcComp * kCompFloats * 4) / (kLandFloats * 4));
   if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
   const uint64_t nwc = uint64_t(stage::nw_code(rhs));
   for (int t = 0; t < ctas; ++t) {
@@ -518,7 +519,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
-  p->smem_bytes = kTcTeams * stages * kTcStageFloats * 4 + 1024;
+  p->smem_bytes = kTcTeams * (stages * kLandFloats + kTcComp * kCompFloats) * 4 + 1024;
   p->num_tasks = int(h_tasks.size());
   p->stream_entries = int64_t(stream.size());
 

@@ -18,11 +18,11 @@
 //     (contiguous in the device format, which already holds every 8-column group as the K-major
 //     32-byte-swizzled operand tile the MMA reads), B with one 2-D cp.async.bulk.tensor box of
 //     8 columns x nw rows (SWIZZLE_32B) per group;
-//   * when a stage lands, the team's 128 threads split A and B into hi (in place) and lo (a second
-//     buffer), fence the generic-proxy writes for the async proxy and arrive on the stage's
-//     "split" mbarrier (one arrival per warp; no named barriers, so every wait stays bounded);
-//   * one thread issues the stage's MMAs and tcgen05.commit, whose mbarrier arrival frees the
-//     stage for the next copies;
+//   * when a stage lands, the team's 128 threads split A and B into hi and lo in a compute slot,
+//     fence the generic-proxy writes for the async proxy and arrive on the slot's "split"
+//     mbarrier (one arrival per warp; no named barriers, so every wait stays bounded), which also
+//     frees the landing slot for the next copies;
+//   * the issuers' MMAs read the compute slot; their tcgen05.commit frees it;
 //   * at the end of an item the thread commits to the team's accumulator barrier, and the four
 //     warps load D with tcgen05.ld and store C (each thread: one RHS column, h consecutive rows).
 // Every wait is bounded (see wait_phase); after an abort each leader drains its copies and MMAs
@@ -48,13 +48,21 @@ constexpr int kTcWarps = (4 + kTcIssuers) * kTcTeams;  // per team: 4 worker war
 constexpr int kTcThreads = 32 * kTcWarps;
 constexpr int kTcCols = 32;                 // block columns per stage
 constexpr int kTcM = 64;                    // MMA M (RHS columns, padded)
-// Stage layout (floats): A hi | A lo | B hi | B lo, fixed offsets.
-constexpr int kStA = 0;
-constexpr int kStALo = 64 * kTcCols;                    // A: up to 64 rows x 32 columns
-constexpr int kStB = 2 * 64 * kTcCols;
+// Two rings per team (floats):
+//   landing slot (kTcLand of them, filled by TMA): A raw at kLdA (up to 64 rows x 32 columns),
+//     B raw boxes at kLdB (one 8-column box per group, padded to 64 rows);
+//   compute slot (kTcComp of them, read by the MMAs): A hi | A lo | B hi | B lo.
+// A landing slot is free again as soon as the workers have split it; a compute slot when the MMAs
+// that read it have completed.
 constexpr int kBoxFloats = kTcM * 8;                    // one 8-column B box, padded to 64 rows
-constexpr int kStBLo = kStB + (kTcCols / 8) * kBoxFloats;
-constexpr int kTcStageFloats = kStBLo + (kTcCols / 8) * kBoxFloats;  // 8192 floats = 32 KB
+constexpr int kLdA = 0;
+constexpr int kLdB = 64 * kTcCols;
+constexpr int kLandFloats = kLdB + (kTcCols / 8) * kBoxFloats;       // 4096 floats = 16 KB
+constexpr int kCpA = 0, kCpALo = 64 * kTcCols;
+constexpr int kCpB = 2 * 64 * kTcCols, kCpBLo = kCpB + (kTcCols / 8) * kBoxFloats;
+constexpr int kCompFloats = kCpBLo + (kTcCols / 8) * kBoxFloats;     // 8192 floats = 32 KB
+constexpr int kTcComp = 2;                                           // compute slots per team
+constexpr int kTcStageFloats = kLandFloats;  // (reported as the stage size)
 // per team: 2 buffers (items alternate) x kTcIssuers partial accumulators x 64 columns
 constexpr int kTmemCols = 2 * kTcIssuers * 64 * kTcTeams;
 constexpr int kTmemAlloc = kTmemCols <= 128 ? 128 : (kTmemCols <= 256 ? 256 : 512);
@@ -137,7 +145,8 @@ __device__ __forceinline__ uint32_t tf32_idesc(int m, int n) {
 
 // Barriers of one team (shared-memory addresses).
 struct TeamBars {
-  uint32_t full0, empty0, split0;  // per ring slot: TMA landed / MMAs done / hi-lo split done
+  uint32_t full0, landfree0;       // per landing slot: TMA landed / split done reading it
+  uint32_t split0, cfree0;         // per compute slot: hi-lo written / MMAs done reading it
   uint32_t acc0, accfree0;         // per accumulator buffer: MMAs of the item done / D read
   uint32_t drain;                  // end-of-kernel drain of the issuers' MMAs
 };
@@ -167,8 +176,8 @@ struct Feeder {
   int issued;           // stages issued so far (debug drop hook)
 };
 
-// Issues the copies of the next non-empty stage into the next ring slot, after the MMAs of the
-// slot's previous stage have completed. Warp-collective. Returns false on abort.
+// Issues the copies of the next non-empty stage into the next landing slot, once the workers have
+// split the slot's previous contents. Warp-collective. Returns false on abort.
 template <bool CHECK>
 __device__ __forceinline__ bool feed_next(const KernelParams& p, Feeder& f, float* team_stages,
                                           int D, const TeamBars& tb, int team, int lane,
@@ -179,7 +188,7 @@ __device__ __forceinline__ bool feed_next(const KernelParams& p, Feeder& f, floa
   f.win.advance(p.stages, lane);
   const int s = f.slot;
   const uint32_t full_bar = tb.full0 + 8u * s;
-  if (!wait_phase(tb.empty0 + 8u * s, f.ph ^ 1u, p, abort_flag, lane)) return false;
+  if (!wait_phase(tb.landfree0 + 8u * s, f.ph ^ 1u, p, abort_flag, lane)) return false;
   const int h = st.h(), nw = st.nw(), n0 = st.n0(), cols = st.cols();
   const long long a0 = st.a_start();
   const bool drop = (team == 0 && f.issued == p.drop_stage);
@@ -197,15 +206,15 @@ __device__ __forceinline__ bool feed_next(const KernelParams& p, Feeder& f, floa
       mbar_arrive(full_bar);  // release the workers without touching memory
     }
   } else {
-    float* sp = team_stages + s * kTcStageFloats;
+    float* sp = team_stages + s * kLandFloats;
     if (lane == 0) {
       mbar_arrive_expect_tx(full_bar, uint32_t((h + nw) * 4 * cols));
-      bulk_g2s(smem_addr(sp + kStA), p.values + a0, uint32_t(h * 4 * cols), full_bar,
+      bulk_g2s(smem_addr(sp + kLdA), p.values + a0, uint32_t(h * 4 * cols), full_bar,
                policy_evict_first());
     } else if (lane <= (cols >> 3)) {
       const int g = lane - 1;
       const CUtensorMap* map = (nw == p.rhs) ? &p.b_full : &p.b_half;
-      tensor2d_g2s(smem_addr(sp + kStB + g * kBoxFloats), map, st.group_col(g), n0, full_bar,
+      tensor2d_g2s(smem_addr(sp + kLdB + g * kBoxFloats), map, st.group_col(g), n0, full_bar,
                    policy_evict_last());
     }
     f.filled |= 1u << s;
@@ -218,12 +227,12 @@ __device__ __forceinline__ bool feed_next(const KernelParams& p, Feeder& f, floa
   return true;
 }
 
-// hi = x with the low 13 mantissa bits cleared, lo = x - hi, over n4 float4s at base (hi in
-// place, lo at base + lo_off), spread over the team's 128 worker threads.
-__device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int tid) {
+// hi = x with the low 13 mantissa bits cleared, lo = x - hi, over n4 float4s read at src and
+// written at the same positions of dst_hi / dst_lo, spread over the team's 128 worker threads.
+__device__ __forceinline__ void split_hi_lo(const float* src, float* dst_hi, float* dst_lo, int n4,
+                                            int tid) {
   for (int i = tid; i < n4; i += 128) {
-    float4* ph = reinterpret_cast<float4*>(base) + i;
-    const float4 x = *ph;
+    const float4 x = reinterpret_cast<const float4*>(src)[i];
     float4 hi, lo;
     hi.x = __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
     hi.y = __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
@@ -233,8 +242,8 @@ __device__ __forceinline__ void split_hi_lo(float* base, int lo_off, int n4, int
     lo.y = x.y - hi.y;
     lo.z = x.z - hi.z;
     lo.w = x.w - hi.w;
-    *ph = hi;
-    *reinterpret_cast<float4*>(base + lo_off + 4 * i) = lo;
+    reinterpret_cast<float4*>(dst_hi)[i] = hi;
+    reinterpret_cast<float4*>(dst_lo)[i] = lo;
   }
 }
 
@@ -255,46 +264,57 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const TeamBar
   tc_fence_after();
   const int h = it.h;
   const uint32_t taddr = tmem_acc + (uint32_t(32 * wq) << 16);
-  float v[64], u[64];
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-    if (c * 8 < h) {
-      tc_ld8_nowait(taddr + uint32_t(8 * c), v + 8 * c);
-      tc_ld8_nowait(taddr + 64u + uint32_t(8 * c), u + 8 * c);
-    }
-  tc_wait_ld();
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(tb.accfree0 + 8u * buf);  // this warp is done with the buffer
   const int m = 16 * wq + lane;
   const bool store = !(CHECK && ((long long)it.c_row + h > p.M || it.n0 + it.nw > p.rhs));
   if (CHECK && !store && wq == 0 && lane == 0)
     record_status(p.status, VBSR_BOUNDS_VIOLATION, it.c_row);
-  if (lane < 16 && m < it.nw && store) {
-    const bool use0 = it.groups > 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
-    const bool use1 = it.groups > 1 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
-    float4* dst = reinterpret_cast<float4*>(p.C + (long long)(it.n0 + m) * p.M + it.c_row);
+  const bool use0 = it.groups > 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+  const bool use1 = it.groups > 1 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+  float4* dst = reinterpret_cast<float4*>(p.C + (long long)(it.n0 + m) * p.M + it.c_row);
+  // two passes of up to 32 columns (both partials), to bound the registers
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-      if (c * 8 < h) {
-        float r[8];
+  for (int half = 0; half < 2; ++half) {
+    float v[32], u[32];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          r[i] = (use0 ? v[8 * c + i] : 0.0f) + (use1 ? u[8 * c + i] : 0.0f);
-        dst[2 * c] = make_float4(r[0], r[1], r[2], r[3]);
-        dst[2 * c + 1] = make_float4(r[4], r[5], r[6], r[7]);
+    for (int c = 0; c < 4; ++c) {
+      const int col = 32 * half + 8 * c;
+      if (col < h) {
+        tc_ld8_nowait(taddr + uint32_t(col), v + 8 * c);
+        tc_ld8_nowait(taddr + 64u + uint32_t(col), u + 8 * c);
       }
+    }
+    tc_wait_ld();
+    if (lane < 16 && m < it.nw && store) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int col = 32 * half + 8 * c;
+        if (col < h) {
+          float r[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            r[i] = (use0 ? v[8 * c + i] : 0.0f) + (use1 ? u[8 * c + i] : 0.0f);
+          dst[col / 4] = make_float4(r[0], r[1], r[2], r[3]);
+          dst[col / 4 + 1] = make_float4(r[4], r[5], r[6], r[7]);
+        }
+      }
+    }
   }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tb.accfree0 + 8u * buf);  // this warp is done with the buffer
   return true;
 }
 
 // Worker warp wq (0..3) of a team: split every stage into hi / lo as it lands, and store each
 // item's result one item later (so the tensor cores work on item j while item j-1 is stored).
 template <bool CHECK>
-__device__ void tc_worker(const KernelParams& p, const Task& task, float* my, const TeamBars& tb,
-                          uint32_t tmem_team, int team, int wq, int lane, volatile int* abort_flag) {
+__device__ void tc_worker(const KernelParams& p, const Task& task, float* land, float* comp,
+                          const TeamBars& tb, uint32_t tmem_team, int team, int wq, int lane,
+                          volatile int* abort_flag) {
   const int D = task.stages;
   const int tid = wq * 32 + lane;
+  int c = 0;            // compute slot
+  uint32_t cph = 0;     // its phase
   StageWin win;
   win.init(p.stages, task.team_off[team], task.team_off[team + 1], lane);
   int s = 0;
@@ -313,23 +333,37 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
         ok = false;
         break;
       }
+      // the compute slot must have been released by the MMAs of its previous stage
+      if (!wait_phase(tb.cfree0 + 8u * c, cph ^ 1u, p, abort_flag, lane)) {
+        ok = false;
+        break;
+      }
       VBSR_PROF_ADD(p, 6, t_w);
       VBSR_PROF_T0(t_s);
       const int cols = st.cols();
       if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-        float* sp = my + s * kTcStageFloats;
-        split_hi_lo(sp + kStA, kStALo - kStA, (cur.h * cols) / 4, tid);
+        const float* lp = land + s * kLandFloats;
+        float* cp = comp + c * kCompFloats;
+        split_hi_lo(lp + kLdA, cp + kCpA, cp + kCpALo, (cur.h * cols) / 4, tid);
         for (int g = 0; g < cols / 8; ++g)
-          split_hi_lo(sp + kStB + g * kBoxFloats, kStBLo - kStB, cur.nw * 2, tid);
+          split_hi_lo(lp + kLdB + g * kBoxFloats, cp + kCpB + g * kBoxFloats,
+                      cp + kCpBLo + g * kBoxFloats, cur.nw * 2, tid);
         fence_proxy_async_smem();
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(tb.split0 + 8u * s);
+      if (lane == 0) {
+        mbar_arrive(tb.landfree0 + 8u * s);  // the landing slot can be refilled
+        mbar_arrive(tb.split0 + 8u * c);     // the compute slot is ready for the MMAs
+      }
       VBSR_PROF_ADD(p, 7, t_s);
       cur.groups += cols / 8;
       if (++s == D) {
         s = 0;
         ph ^= 1u;
+      }
+      if (++c == kTcComp) {
+        c = 0;
+        cph ^= 1u;
       }
     }
     if (st.last()) {
@@ -337,7 +371,8 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
         const int pj = j - 1;
         VBSR_PROF_T0(t_e);
         if (!tc_epilogue<CHECK>(p, tb, pj & 1, uint32_t((pj >> 1) & 1),
-                                tmem_team + uint32_t(128 * (pj & 1)), wq, lane, prev, abort_flag)) {
+                                tmem_team + uint32_t(128 * (pj & 1)), wq, lane, prev,
+                                abort_flag)) {
           ok = false;
           break;
         }
@@ -359,8 +394,8 @@ __device__ void tc_worker(const KernelParams& p, const Task& task, float* my, co
 // (group index % 2 == half, counted from the item's start) into its partial accumulator once the
 // workers have split the stage; issuer 0 also keeps the TMA ring D-1 stages ahead.
 template <bool CHECK>
-__device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, const TeamBars& tb,
-                          uint32_t tmem_team, int team, int half, int lane,
+__device__ void tc_issuer(const KernelParams& p, const Task& task, float* land, float* comp,
+                          const TeamBars& tb, uint32_t tmem_team, int team, int half, int lane,
                           volatile int* abort_flag) {
   const int D = task.stages;
   const int b = task.team_off[team], e = task.team_off[team + 1];
@@ -376,12 +411,12 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
   if (feeder) {
     f.win.init(p.stages, b, e, lane);
     for (int i = 0; i < D - 1 && ok; ++i)
-      ok = feed_next<CHECK>(p, f, my, D, tb, team, lane, abort_flag);
+      ok = feed_next<CHECK>(p, f, land, D, tb, team, lane, abort_flag);
   }
-  int s = 0;
+  int s = 0;  // compute slot
   uint32_t ph = 0;
   int j = 0;  // items started
-  const uint32_t sbase = smem_addr(my);
+  const uint32_t sbase = smem_addr(comp);
   uint32_t tmem_d = tmem_team, idesc = 0, accumulate = 0;
   int gi = 0, h = 8;
   VBSR_PROF_T0(t_all);
@@ -415,11 +450,11 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
       VBSR_PROF_T0(t_m);
       tc_fence_after();
       if (lane == 0 && !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-        const uint32_t sp = sbase + 4u * uint32_t(s * kTcStageFloats);
-        uint64_t a_hi = sw32_desc(sp + 4u * kStB);
-        uint64_t b_hi = sw32_desc(sp + 4u * kStA);
-        const uint64_t da_lo = uint64_t((4u * (kStBLo - kStB)) >> 4);
-        const uint64_t db_lo = uint64_t((4u * (kStALo - kStA)) >> 4);
+        const uint32_t sp = sbase + 4u * uint32_t(s * kCompFloats);
+        uint64_t a_hi = sw32_desc(sp + 4u * kCpB);
+        uint64_t b_hi = sw32_desc(sp + 4u * kCpA);
+        const uint64_t da_lo = uint64_t((4u * (kCpBLo - kCpB)) >> 4);
+        const uint64_t db_lo = uint64_t((4u * (kCpALo - kCpA)) >> 4);
         const uint64_t da = uint64_t((4u * kBoxFloats) >> 4), db = uint64_t((32u * h) >> 4);
         const int groups = st.cols() / 8;
         for (int g = 0; g < groups; ++g, ++gi) {
@@ -435,16 +470,16 @@ __device__ void tc_issuer(const KernelParams& p, const Task& task, float* my, co
       } else {
         gi += st.cols() / 8;
       }
-      if (lane == 0) tc_commit(tb.empty0 + 8u * s);  // frees the slot once these MMAs read it
+      if (lane == 0) tc_commit(tb.cfree0 + 8u * s);  // frees the slot once these MMAs read it
       __syncwarp();
       VBSR_PROF_ADD(p, 4, t_m);
       VBSR_PROF_T0(t_i);
-      if (feeder && !feed_next<CHECK>(p, f, my, D, tb, team, lane, abort_flag)) {
+      if (feeder && !feed_next<CHECK>(p, f, land, D, tb, team, lane, abort_flag)) {
         ok = false;
         break;
       }
       VBSR_PROF_ADD(p, 2, t_i);
-      if (++s == D) {
+      if (++s == kTcComp) {
         s = 0;
         ph ^= 1u;
       }
@@ -482,7 +517,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   float* stages = reinterpret_cast<float*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bars[3][kTcTeams][kMaxStages];  // full, empty, split
+  __shared__ __align__(8) uint64_t bars[2][kTcTeams][kMaxStages];  // full, landfree
+  __shared__ __align__(8) uint64_t cbars[2][kTcTeams][kTcComp];    // split, cfree
   __shared__ __align__(8) uint64_t accbars[2][kTcTeams][2];        // acc done, acc free
   __shared__ __align__(8) uint64_t drainbars[kTcTeams];
   __shared__ uint32_t tmem_slot;
@@ -498,8 +534,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     for (int j = 0; j < kTcTeams; ++j) {
       for (int s = 0; s < task.stages; ++s) {
         mbar_init(smem_addr(&bars[0][j][s]), 1u);  // TMA: one arrival + transaction bytes
-        mbar_init(smem_addr(&bars[1][j][s]), uint32_t(kTcIssuers));  // tcgen05.commit per issuer
-        mbar_init(smem_addr(&bars[2][j][s]), 4u);  // one arrival per worker warp
+        mbar_init(smem_addr(&bars[1][j][s]), 4u);  // one arrival per worker warp
+      }
+      for (int c = 0; c < kTcComp; ++c) {
+        mbar_init(smem_addr(&cbars[0][j][c]), 4u);                    // one per worker warp
+        mbar_init(smem_addr(&cbars[1][j][c]), uint32_t(kTcIssuers));  // tcgen05.commit per issuer
       }
       for (int b = 0; b < 2; ++b) {
         mbar_init(smem_addr(&accbars[0][j][b]), uint32_t(kTcIssuers));
@@ -521,17 +560,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   const int team = worker ? (warp >> 2) : (iw / kTcIssuers);
   TeamBars tb;
   tb.full0 = smem_addr(&bars[0][team][0]);
-  tb.empty0 = smem_addr(&bars[1][team][0]);
-  tb.split0 = smem_addr(&bars[2][team][0]);
+  tb.landfree0 = smem_addr(&bars[1][team][0]);
+  tb.split0 = smem_addr(&cbars[0][team][0]);
+  tb.cfree0 = smem_addr(&cbars[1][team][0]);
   tb.acc0 = smem_addr(&accbars[0][team][0]);
   tb.accfree0 = smem_addr(&accbars[1][team][0]);
   tb.drain = smem_addr(&drainbars[team]);
-  float* my = stages + team * task.stages * kTcStageFloats;
+  float* land = stages + team * (task.stages * kLandFloats + kTcComp * kCompFloats);
+  float* comp = land + task.stages * kLandFloats;
   const uint32_t tmem_team = tmem_base + uint32_t(kTeamTmem * team);
   if (worker)
-    tc_worker<CHECK>(p, task, my, tb, tmem_team, team, warp & 3, lane, &abort_flag);
+    tc_worker<CHECK>(p, task, land, comp, tb, tmem_team, team, warp & 3, lane, &abort_flag);
   else
-    tc_issuer<CHECK>(p, task, my, tb, tmem_team, team, iw % kTcIssuers, lane, &abort_flag);
+    tc_issuer<CHECK>(p, task, land, comp, tb, tmem_team, team, iw % kTcIssuers, lane,
+                     &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
