@@ -173,21 +173,27 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// B (K x rhs, column-major, ld K) as a 2-D tensor with an 8-column x `rows`-row box, written to
-// shared memory with the 32-byte swizzle (the K-major operand layout of tcgen05.mma).
-vbsr_status encode_b_map(CUtensorMap* map, const float* B, int64_t K, int rhs, int rows) {
+// B (K x rhs, column-major, ld K) as the 3-D tensor (k, j, q) of the kernel's operand stack: RHS
+// column c = half * q + j (half = 8 for rhs <= 32, 16 for rhs = 64), written to shared memory with
+// the 32-byte swizzle (the K-major operand layout of tcgen05.mma): one 8 x half x 1 box per
+// 8-column group and quadrant, which lands on the quadrant's hi rows of the stack.
+vbsr_status encode_b_map(KernelParams* kp, const float* B, int64_t K, int rhs) {
   auto enc = tensor_map_encoder();
   if (enc == nullptr) return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rhs)};
-  const cuuint64_t strides[1] = {cuuint64_t(K) * sizeof(float)};
-  const cuuint32_t box[2] = {8u, cuuint32_t(rows)};
-  const cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const int half = stack_m(rhs) / 8, quads = rhs / half;
+  const cuuint64_t dims[3] = {cuuint64_t(K), cuuint64_t(half), cuuint64_t(quads)};
+  const cuuint64_t strides[2] = {cuuint64_t(K) * sizeof(float),
+                                 cuuint64_t(K) * sizeof(float) * cuuint64_t(half)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const cuuint32_t box[3] = {8u, cuuint32_t(half), 1u};
+  const CUresult r = enc(&kp->b_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(B),
+                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  kp->b_boxes = quads;
+  kp->b_group_bytes = uint32_t(8 * half * quads * sizeof(float));
   return VBSR_OK;
 }
 
@@ -397,9 +403,9 @@ cudaError_t set_kernel_attrs() {
                               kSmemBudget + 1024);
 }
 
-// Schedule for spmm_tc_kernel: one item per block row, kTcTeams teams of four warps per CTA, one
-// CTA per SM; items assigned to teams by longest-processing-time-first on the cost model; each
-// team's stream packs the item's k-chunks into stages of kTcCols block columns.
+// Schedule for spmm_tc_kernel: one item per block row, one CTA per SM; items assigned to CTAs by
+// longest-processing-time-first on the cost model; each CTA's stream cuts the item's 8-column
+// groups into stages of stage_groups(rhs) groups.
 vbsr_status build_schedule(vbsr_plan* p) {
   const MatrixData& d = p->m->d;
   const int rhs = p->rhs;
@@ -411,24 +417,17 @@ vbsr_status build_schedule(vbsr_plan* p) {
   const int R = d.block_rows;
   std::vector<int> row_stages(R);
   std::vector<double> cost(R);
+  const int G = stage_groups(rhs);  // 8-column groups per stage
   for (int i = 0; i < R; ++i) {
-    int st = 0, used = 0;
-    for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
-      const int w = int((d.h_blk_desc[b] & 7u) + 1u) * 8;
-      for (int k0 = 0; k0 < w; k0 += kChunk) {
-        const int kc = std::min(kChunk, w - k0);
-        if (used == 0 || used + kc > kTcCols) {
-          ++st;
-          used = 0;
-        }
-        used += kc;
-      }
-    }
+    int64_t groups = 0;
+    for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b)
+      groups += int64_t((d.h_blk_desc[b] & 7u) + 1u);
+    const int st = int((groups + G - 1) / G);
     row_stages[i] = st;
     cost[i] = item_cost(d.h_row_size[i], rhs, d.h_sum_w[i], st);
   }
-  const int ctas = std::max(1, std::min(num_sm, (R + kTcTeams - 1) / kTcTeams));
-  const int teams = ctas * kTcTeams;
+  const int ctas = std::max(1, std::min(num_sm, R));
+  const int teams = ctas;
   std::vector<int> order(R);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
@@ -449,48 +448,47 @@ vbsr_status build_schedule(vbsr_plan* p) {
   std::vector<StageDesc> stream;
   stream.reserve(size_t(R) + size_t(d.nnzb) * 2);
   std::vector<Task> h_tasks;
-  const int stages = std::min(
-      kMaxStages, (kSmemBudget / kTcTeams - kTcComp * kCompFloats * 4) / (kLandFloats * 4));
+  const int slot = slot_floats(rhs);
+  // A multiple of kTcMmaWarps (and so of kTcFeeders): every slot then has one feeder and one MMA
+  // warp, which pass through its uses in order, so a wait never meets a phase of another use.
+  const int stages = std::min(kMaxStages, kSmemBudget / (slot * 4)) / kTcMmaWarps * kTcMmaWarps;
   if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
   const uint64_t nwc = uint64_t(stage::nw_code(rhs));
   for (int t = 0; t < ctas; ++t) {
     Task task{};
-    for (int j = 0; j < kTcTeams; ++j) {
-      task.team_off[j] = int(stream.size());
-      std::vector<int>& l = lists[t * kTcTeams + j];
+    {
+      task.team_off[0] = int(stream.size());
+      std::vector<int>& l = lists[t];
       std::sort(l.begin(), l.end());
       for (int i : l) {
         const int h = d.h_row_size[i];
         const uint64_t base0 = (uint64_t(h / 8 - 1) << 32) | (nwc << 39);
         const uint64_t w1 = uint64_t(d.h_row_off[i]);
         const size_t item_first = stream.size();
-        // k-chunks packed greedily into stages of kTcCols columns; a chunk never straddles two.
-        // A stage's chunks are consecutive in the value array, so its A is one contiguous range.
+        // The item's 8-column groups, block after block, in runs of G per stage. In the device
+        // format group g of a block starts 8*h*g floats after the block's values and a block row's
+        // blocks are consecutive, so a stage's A values are one contiguous range.
         int64_t val = d.h_val_off_row[i];
-        int used = 0;
+        int used = 0;  // columns in the current stage
         StageDesc cur{};
         for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
           const uint32_t desc = d.h_blk_desc[b];
           const int w = int((desc & 7u) + 1u) * 8;
           const int64_t col = int64_t(desc & ~7u);
-          for (int k0 = 0; k0 < w; k0 += kChunk) {
-            const int kc = std::min(kChunk, w - k0);
-            if (used > 0 && used + kc > kTcCols) {
+          for (int g = 0; g < w / 8; ++g) {
+            if (used == 8 * G) {
               cur.w[0] |= uint64_t(used / 8 - 1) << 28;
               stream.push_back(cur);
               used = 0;
             }
             if (used == 0) {
               cur = StageDesc{};
-              cur.w[0] = base0 | uint64_t((val + int64_t(h) * k0) / 64);
+              cur.w[0] = base0 | uint64_t((val + int64_t(8) * h * g) / 64);
               cur.w[1] = w1;
             }
-            for (int g = 0; g < kc / 8; ++g) {
-              const int gg = used / 8 + g;
-              const uint64_t c8 = uint64_t((col + k0 + 8 * g) / 8);
-              cur.w[2 + gg / 2] |= c8 << (32 * (gg & 1));
-            }
-            used += kc;
+            const int gg = used / 8;
+            cur.w[2 + gg / 2] |= uint64_t((col + 8 * g) / 8) << (32 * (gg & 1));
+            used += 8;
           }
           val += int64_t(h) * w;
         }
@@ -507,26 +505,25 @@ vbsr_status build_schedule(vbsr_plan* p) {
         stream.back().w[0] |= stage::kLast;
       }
     }
-    for (int j = kTcTeams; j <= 8; ++j) task.team_off[j] = int(stream.size());
-    task.team_warps = 4 + kTcIssuers;
-    task.stage_floats = kTcStageFloats;
-    task.stage_cols = kTcCols;
+    for (int j = 1; j <= 8; ++j) task.team_off[j] = int(stream.size());
+    task.team_warps = kTcWarps;
+    task.stage_floats = slot;
+    task.stage_cols = 8 * G;
     task.stages = stages;
     h_tasks.push_back(task);
-    p->task_warps.push_back(4 + kTcIssuers);
-    p->task_cost.push_back(*std::max_element(load.begin() + t * kTcTeams,
-                                             load.begin() + (t + 1) * kTcTeams));
+    p->task_warps.push_back(kTcWarps);
+    p->task_cost.push_back(load[t]);
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
-  p->smem_bytes = kTcTeams * (stages * kLandFloats + kTcComp * kCompFloats) * 4 + 1024;
+  p->smem_bytes = stages * slot * 4 + 1024;
   p->num_tasks = int(h_tasks.size());
   p->stream_entries = int64_t(stream.size());
 
   char buf[512];
   std::snprintf(buf, sizeof buf,
                 "rhs=%d items=%d pipeline_stages=%zu tasks=%d teams=%d ring=%d smem=%d sms=%d "
-                "kernel=tcgen05-3xtf32",
+                "kernel=tcgen05-3xtf32-stacked",
                 rhs, R, stream.size(), p->num_tasks, teams, stages, p->smem_bytes, num_sm);
   p->summary = buf;
 
@@ -560,6 +557,29 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
     spmm_tc_kernel<true><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
   else
     spmm_tc_kernel<false><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
+}
+
+// Launch parameters of one execute: the plan's schedule, the caller's B and C, and the B tensor map.
+vbsr_status fill_params(const vbsr_plan* p, const float* B, float* C, int* status,
+                        unsigned long long* timing, KernelParams* kp) {
+  const MatrixData& d = p->m->d;
+  vbsr_status st = encode_b_map(kp, B, d.K, p->rhs);
+  if (st != VBSR_OK) return st;
+  kp->stages = p->d_stream;
+  kp->tasks = p->d_tasks;
+  kp->values = d.d_values;
+  kp->B = B;
+  kp->C = C;
+  kp->M = d.M;
+  kp->K = d.K;
+  kp->nvalues = d.nvalues;
+  kp->rhs = p->rhs;
+  kp->status = status;
+  kp->drop_stage = p->drop_stage;
+  kp->wait_limit = p->wait_limit;
+  kp->timing = timing;
+  kp->diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
+  return VBSR_OK;
 }
 
 vbsr_status launch_view_kernel(const vbsr_device_matrix* a, const float* B, float* C, int rhs,
@@ -696,7 +716,6 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   clear_error();
   if (p == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null plan");
   if (B == nullptr || C == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null B or C");
-  const MatrixData& d = p->m->d;
   DeviceGuard guard(p->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if ((reinterpret_cast<uintptr_t>(B) & 15u) || (reinterpret_cast<uintptr_t>(C) & 15u)) {
@@ -708,24 +727,8 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   }
   if (p->num_tasks == 0) return VBSR_OK;
   KernelParams kp;
-  vbsr_status st = encode_b_map(&kp.b_full, B, d.K, p->rhs, p->rhs);
+  vbsr_status st = fill_params(p, B, C, p->d_status, p->timing_on ? p->d_timing : nullptr, &kp);
   if (st != VBSR_OK) return st;
-  st = encode_b_map(&kp.b_half, B, d.K, p->rhs, p->rhs > 8 ? p->rhs / 2 : p->rhs);
-  if (st != VBSR_OK) return st;
-  kp.stages = p->d_stream;
-  kp.tasks = p->d_tasks;
-  kp.values = d.d_values;
-  kp.B = B;
-  kp.C = C;
-  kp.M = d.M;
-  kp.K = d.K;
-  kp.nvalues = d.nvalues;
-  kp.rhs = p->rhs;
-  kp.status = p->d_status;
-  kp.drop_stage = p->drop_stage;
-  kp.wait_limit = p->wait_limit;
-  kp.timing = p->timing_on ? p->d_timing : nullptr;
-  kp.diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
   launch_spmm(p, kp, s);
   VBSR_CUDA(cudaGetLastError());
   return VBSR_OK;
@@ -781,7 +784,6 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
                      "plan launches " + std::to_string(p->num_tasks) +
                          " CTAs; vbsr_plan_execute_noalloc supports at most " +
                          std::to_string(kNoAllocMaxCtas));
-  const MatrixData& d = p->m->d;
   DeviceGuard guard(p->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if ((reinterpret_cast<uintptr_t>(B) & 15u) || (reinterpret_cast<uintptr_t>(C) & 15u)) {
@@ -797,24 +799,8 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
   const size_t used = (2 + 2 * size_t(p->num_tasks)) * sizeof(unsigned long long);
   VBSR_CUDA(cudaMemsetAsync(scratch, 0, used, s));
   KernelParams kp;
-  st = encode_b_map(&kp.b_full, B, d.K, p->rhs, p->rhs);
+  st = fill_params(p, B, C, reinterpret_cast<int*>(scratch), scratch + 2, &kp);
   if (st != VBSR_OK) return st;
-  st = encode_b_map(&kp.b_half, B, d.K, p->rhs, p->rhs > 8 ? p->rhs / 2 : p->rhs);
-  if (st != VBSR_OK) return st;
-  kp.stages = p->d_stream;
-  kp.tasks = p->d_tasks;
-  kp.values = d.d_values;
-  kp.B = B;
-  kp.C = C;
-  kp.M = d.M;
-  kp.K = d.K;
-  kp.nvalues = d.nvalues;
-  kp.rhs = p->rhs;
-  kp.status = reinterpret_cast<int*>(scratch);
-  kp.drop_stage = p->drop_stage;
-  kp.wait_limit = p->wait_limit;
-  kp.timing = scratch + 2;
-  kp.diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
   launch_spmm(p, kp, s);
   VBSR_CUDA(cudaGetLastError());
   if (cta_times == nullptr) return VBSR_OK;

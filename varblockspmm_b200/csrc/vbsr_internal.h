@@ -15,13 +15,14 @@ vbsr_status set_error(vbsr_status s, const std::string& msg);
 void clear_error();
 
 // ---- work schedule ---------------------------------------------------------------------------
-// The plan compiles the matrix into one list of pipeline stages per team. A stage covers up to
-// kTcCols (32) consecutive block columns of one work item (one block row: an h x nw tile of C).
-// Because a block row's blocks are contiguous in the value array and each block's k-chunks are
-// stored in order, the A values of a stage are one contiguous range; B is one 8-column box per
-// 8-column group. A block row with no blocks is one "empty" stage (C rows stored as zeros).
+// The plan compiles the matrix into one list of pipeline stages per CTA. A stage covers up to four
+// consecutive 8-column groups of one work item (one block row: an h x nw tile of C), possibly
+// from several blocks. Because a block row's blocks are contiguous in the value array and each
+// block stores its groups in order (h x 8 floats each), the A values of a stage are one contiguous
+// range; B is fetched per 8-column group. A block row with no blocks is one "empty" stage (its C
+// rows are stored as zeros).
 // Descriptor, 4 x 64 bits:
-//   w0: bits  0..27 A start / 64 (value offsets of blocks and chunks are multiples of 64 floats)
+//   w0: bits  0..27 A start / 64 (offsets of blocks and groups are multiples of 64 floats)
 //       bits 28..29 columns/8 - 1   bit 30 first stage of the item   bit 31 last stage of the item
 //       bits 32..34 h/8 - 1         bit 35 empty item   bits 36..38 n0/8   bits 39..40 log2(nw/8)
 //   w1: bits  0..30 c_row (first scalar row of the tile in C)

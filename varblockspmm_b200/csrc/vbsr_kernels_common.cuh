@@ -14,8 +14,11 @@ namespace vbsr_b200 {
 typedef unsigned long long u64;
 
 struct KernelParams {
-  CUtensorMap b_full;   // B as a K x rhs tensor, box 8 columns x rhs rows
-  CUtensorMap b_half;   // same, box 8 columns x rhs/2 rows
+  // B (K x rhs, column-major) as a 3-D tensor (k, j, q) with RHS column c = q * half + j, where
+  // half = 8 (rhs <= 32) or 16 (rhs = 64); see the operand stack in vbsr_tc.cuh.
+  CUtensorMap b_map;
+  int b_boxes;          // TMA boxes per 8-column group (one per quadrant: rhs/half)
+  uint32_t b_group_bytes;  // bytes the boxes of one group write to shared memory
   const StageDesc* stages;  // per-team stage descriptors
   const Task* tasks;
   const float* values;  // device-format values

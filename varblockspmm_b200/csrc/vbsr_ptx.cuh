@@ -90,4 +90,15 @@ __device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const void* tmap, int
       : "memory");
 }
 
+// 3-D tensor TMA load (box from a tensor map) into shared memory, completion on `bar`.
+// x must be a multiple of 4 for 32-bit elements (16-byte aligned start).
+__device__ __forceinline__ void tensor3d_g2s(uint32_t dst, const void* tmap, int x, int y, int z,
+                                             uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 }  // namespace vbsr_b200

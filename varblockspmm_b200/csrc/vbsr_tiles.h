@@ -23,7 +23,7 @@
 namespace vbsr_b200 {
 
 constexpr int kChunk = 32;                        // block columns per device k-chunk
-constexpr int kMaxStages = 6;                     // pipeline depth limit per team
+constexpr int kMaxStages = 12;                    // pipeline depth limit per CTA
 
 // Position of element (r, k) of an h x w block inside the block's device storage.
 VBSR_HD int blk_pos(int h, int w, int r, int k) {
