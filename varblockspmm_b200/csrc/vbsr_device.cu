@@ -1,7 +1,6 @@
 // vbsr_device.cu — device side of the engine: the owning device format (Matrix), the planner
 // (Plan), the execute path and the C-ABI entry points that touch a GPU.
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -156,45 +155,6 @@ __global__ void rowwise_direct_kernel(vbsr_device_matrix a, const float* __restr
     for (int j = 0; j < 8; ++j)
       C[a.row_scalar_off[row] + r + (long long)(n0 + j) * a.scalar_rows] = acc[j];
   }
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
-// B (K x rhs, column-major, ld K) as the 3-D tensor (k, j, q) of the kernel's operand stack: RHS
-// column c = half * q + j (half = 8 for rhs <= 32, 16 for rhs = 64), written to shared memory with
-// the 32-byte swizzle (the K-major operand layout of tcgen05.mma): one 8 x half x 1 box per
-// 8-column group and quadrant, which lands on the quadrant's hi rows of the stack.
-vbsr_status encode_b_map(KernelParams* kp, const float* B, int64_t K, int rhs) {
-  auto enc = tensor_map_encoder();
-  if (enc == nullptr) return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
-  const int half = stack_m(rhs) / 8, quads = rhs / half;
-  const cuuint64_t dims[3] = {cuuint64_t(K), cuuint64_t(half), cuuint64_t(quads)};
-  const cuuint64_t strides[2] = {cuuint64_t(K) * sizeof(float),
-                                 cuuint64_t(K) * sizeof(float) * cuuint64_t(half)};
-  const cuuint32_t estr[3] = {1u, 1u, 1u};
-  const cuuint32_t box[3] = {8u, cuuint32_t(half), 1u};
-  const CUresult r = enc(&kp->b_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(B),
-                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
-  kp->b_boxes = quads;
-  kp->b_group_bytes = uint32_t(8 * half * quads * sizeof(float));
-  return VBSR_OK;
 }
 
 bool valid_rhs(int rhs) { return rhs == 8 || rhs == 16 || rhs == 32 || rhs == 64; }
@@ -373,6 +333,7 @@ struct vbsr_plan {
   int smem_bytes = 0;
   int64_t stream_entries = 0;
   StageDesc* d_stream = nullptr;
+  ItemDesc* d_items = nullptr;
   Task* d_tasks = nullptr;
   int* d_status = nullptr;
   unsigned long long* d_timing = nullptr;  // allocated on first request
@@ -446,66 +407,69 @@ vbsr_status build_schedule(vbsr_plan* p) {
   }
 
   std::vector<StageDesc> stream;
-  stream.reserve(size_t(R) + size_t(d.nnzb) * 2);
+  stream.reserve(size_t(d.nnzb) * 2 + 16);
+  std::vector<ItemDesc> items;
+  items.reserve(size_t(R));
   std::vector<Task> h_tasks;
   const int slot = slot_floats(rhs);
-  // A multiple of kTcMmaWarps (and so of kTcFeeders): every slot then has one feeder and one MMA
-  // warp, which pass through its uses in order, so a wait never meets a phase of another use.
-  const int stages = std::min(kMaxStages, kSmemBudget / (slot * 4)) / kTcMmaWarps * kTcMmaWarps;
-  if (stages < 2) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
+  // A multiple of kTcSplitWarps (and so of kTcMmaWarps and kTcFeeders): every slot then has one
+  // feeder, one split warp and one MMA warp, which pass through its uses in order, so a wait never
+  // meets a phase of another use.
+  const int stages =
+      std::min(kMaxStages, kSmemBudget / (slot * 4)) / kTcSplitWarps * kTcSplitWarps;
+  if (stages < kTcSplitWarps) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
   const uint64_t nwc = uint64_t(stage::nw_code(rhs));
   for (int t = 0; t < ctas; ++t) {
     Task task{};
-    {
-      task.team_off[0] = int(stream.size());
-      std::vector<int>& l = lists[t];
-      std::sort(l.begin(), l.end());
-      for (int i : l) {
-        const int h = d.h_row_size[i];
-        const uint64_t base0 = (uint64_t(h / 8 - 1) << 32) | (nwc << 39);
-        const uint64_t w1 = uint64_t(d.h_row_off[i]);
-        const size_t item_first = stream.size();
-        // The item's 8-column groups, block after block, in runs of G per stage. In the device
-        // format group g of a block starts 8*h*g floats after the block's values and a block row's
-        // blocks are consecutive, so a stage's A values are one contiguous range.
-        int64_t val = d.h_val_off_row[i];
-        int used = 0;  // columns in the current stage
-        StageDesc cur{};
-        for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
-          const uint32_t desc = d.h_blk_desc[b];
-          const int w = int((desc & 7u) + 1u) * 8;
-          const int64_t col = int64_t(desc & ~7u);
-          for (int g = 0; g < w / 8; ++g) {
-            if (used == 8 * G) {
-              cur.w[0] |= uint64_t(used / 8 - 1) << 28;
-              stream.push_back(cur);
-              used = 0;
-            }
-            if (used == 0) {
-              cur = StageDesc{};
-              cur.w[0] = base0 | uint64_t((val + int64_t(8) * h * g) / 64);
-              cur.w[1] = w1;
-            }
-            const int gg = used / 8;
-            cur.w[2 + gg / 2] |= uint64_t((col + 8 * g) / 8) << (32 * (gg & 1));
-            used += 8;
+    task.item_off = int(items.size());
+    task.stage_off = int(stream.size());
+    std::vector<int>& l = lists[t];
+    std::sort(l.begin(), l.end());
+    for (int i : l) {
+      const int h = d.h_row_size[i];
+      const uint64_t base0 = (uint64_t(h / 8 - 1) << 32) | (nwc << 39);
+      ItemDesc item{};
+      item.c_row = uint32_t(d.h_row_off[i]);
+      item.shape = uint32_t(h / 8 - 1) | (uint32_t(nwc) << 6);
+      item.k0 = uint32_t(stream.size() - size_t(task.stage_off));
+      const uint64_t w1 = uint64_t(items.size() - size_t(task.item_off));
+      // The item's 8-column groups, block after block, in runs of G per stage. In the device
+      // format group g of a block starts 8*h*g floats after the block's values and a block row's
+      // blocks are consecutive, so a stage's A values are one contiguous range.
+      int64_t val = d.h_val_off_row[i];
+      int used = 0;  // columns in the current stage
+      StageDesc cur{};
+      for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
+        const uint32_t desc = d.h_blk_desc[b];
+        const int w = int((desc & 7u) + 1u) * 8;
+        const int64_t col = int64_t(desc & ~7u);
+        for (int g = 0; g < w / 8; ++g) {
+          if (used == 8 * G) {
+            cur.w[0] |= uint64_t(used / 8 - 1) << 28;
+            stream.push_back(cur);
+            used = 0;
           }
-          val += int64_t(h) * w;
+          if (used == 0) {
+            cur = StageDesc{};
+            cur.w[0] = base0 | uint64_t((val + int64_t(8) * h * g) / 64);
+            cur.w[1] = w1;
+          }
+          const int gg = used / 8;
+          cur.w[2 + gg / 2] |= uint64_t((col + 8 * g) / 8) << (32 * (gg & 1));
+          used += 8;
         }
-        if (used > 0) {
-          cur.w[0] |= uint64_t(used / 8 - 1) << 28;
-          stream.push_back(cur);
-        } else {  // a block row without blocks: one empty stage, its C rows become zeros
-          StageDesc e{};
-          e.w[0] = base0 | stage::kEmpty;
-          e.w[1] = w1;
-          stream.push_back(e);
-        }
-        stream[item_first].w[0] |= stage::kFirst;
-        stream.back().w[0] |= stage::kLast;
+        val += int64_t(h) * w;
       }
+      if (used > 0) {
+        cur.w[0] |= uint64_t(used / 8 - 1) << 28;
+        stream.push_back(cur);
+      }
+      // a block row without blocks keeps n = 0: its C rows are stored as zeros
+      item.n = uint32_t(stream.size() - size_t(task.stage_off)) - item.k0;
+      items.push_back(item);
     }
-    for (int j = 1; j <= 8; ++j) task.team_off[j] = int(stream.size());
+    task.item_end = int(items.size());
+    task.stage_end = int(stream.size());
     task.team_warps = kTcWarps;
     task.stage_floats = slot;
     task.stage_cols = 8 * G;
@@ -529,6 +493,10 @@ vbsr_status build_schedule(vbsr_plan* p) {
 
   DeviceGuard guard(d.device);
   VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
+  VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
+  if (!items.empty())
+    VBSR_CUDA(cudaMemcpy(p->d_items, items.data(), items.size() * sizeof(ItemDesc),
+                         cudaMemcpyHostToDevice));
   VBSR_CUDA(cudaMalloc(&p->d_tasks, std::max<size_t>(1, h_tasks.size()) * sizeof(Task)));
   VBSR_CUDA(cudaMalloc(&p->d_status, kStatusWords * sizeof(int)));
   if (!stream.empty())
@@ -546,6 +514,7 @@ void free_plan(vbsr_plan* p) {
   if (p == nullptr) return;
   DeviceGuard guard(p->device);
   cudaFree(p->d_stream);
+  cudaFree(p->d_items);
   cudaFree(p->d_tasks);
   cudaFree(p->d_status);
   cudaFree(p->d_timing);
@@ -559,13 +528,12 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
     spmm_tc_kernel<false><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
 }
 
-// Launch parameters of one execute: the plan's schedule, the caller's B and C, and the B tensor map.
+// Launch parameters of one execute: the plan's schedule and the caller's B and C.
 vbsr_status fill_params(const vbsr_plan* p, const float* B, float* C, int* status,
                         unsigned long long* timing, KernelParams* kp) {
   const MatrixData& d = p->m->d;
-  vbsr_status st = encode_b_map(kp, B, d.K, p->rhs);
-  if (st != VBSR_OK) return st;
   kp->stages = p->d_stream;
+  kp->items = p->d_items;
   kp->tasks = p->d_tasks;
   kp->values = d.d_values;
   kp->B = B;

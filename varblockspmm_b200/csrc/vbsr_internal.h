@@ -15,17 +15,17 @@ vbsr_status set_error(vbsr_status s, const std::string& msg);
 void clear_error();
 
 // ---- work schedule ---------------------------------------------------------------------------
-// The plan compiles the matrix into one list of pipeline stages per CTA. A stage covers up to four
-// consecutive 8-column groups of one work item (one block row: an h x nw tile of C), possibly
-// from several blocks. Because a block row's blocks are contiguous in the value array and each
-// block stores its groups in order (h x 8 floats each), the A values of a stage are one contiguous
-// range; B is fetched per 8-column group. A block row with no blocks is one "empty" stage (its C
-// rows are stored as zeros).
-// Descriptor, 4 x 64 bits:
+// The plan compiles the matrix into, per CTA, a list of work items (one block row each: an h x nw
+// tile of C) and the list of their pipeline stages. A stage covers up to four consecutive 8-column
+// groups of one item, possibly from several blocks. Because a block row's blocks are contiguous in
+// the value array and each block stores its groups in order (h x 8 floats each), the A values of a
+// stage are one contiguous range; B is fetched per 8-column group. A block row with no blocks is an
+// item without stages (its C rows are stored as zeros).
+// Stage descriptor, 4 x 64 bits:
 //   w0: bits  0..27 A start / 64 (offsets of blocks and groups are multiples of 64 floats)
-//       bits 28..29 columns/8 - 1   bit 30 first stage of the item   bit 31 last stage of the item
-//       bits 32..34 h/8 - 1         bit 35 empty item   bits 36..38 n0/8   bits 39..40 log2(nw/8)
-//   w1: bits  0..30 c_row (first scalar row of the tile in C)
+//       bits 28..29 columns/8 - 1
+//       bits 32..34 h/8 - 1         bits 36..38 n0/8   bits 39..40 log2(nw/8)
+//   w1: the item's index in the CTA's item list
 //   w2: group 0 column / 8 (bits 0..27), group 1 column / 8 (bits 32..59)
 //   w3: group 2 column / 8, group 3 column / 8
 struct alignas(32) StageDesc {
@@ -33,7 +33,6 @@ struct alignas(32) StageDesc {
 };
 static_assert(sizeof(StageDesc) == 32, "StageDesc layout");
 namespace stage {
-constexpr uint64_t kFirst = 1ull << 30, kLast = 1ull << 31, kEmpty = 1ull << 35;
 constexpr int64_t kMaxVal = (int64_t(1) << 28) * 64;  // value offsets must stay below this
 constexpr int64_t kMaxCol = (int64_t(1) << 28) * 8;   // scalar columns must stay below this
 inline int nw_code(int nw) {
@@ -43,14 +42,24 @@ inline int nw_code(int nw) {
 }
 }  // namespace stage
 
-// One CTA task: team t walks stage descriptors [team_off[t], team_off[t+1]).
+// Item descriptor, 4 x 32 bits:
+//   x: c_row (first scalar row of the tile in C)
+//   y: bits 0..2 h/8 - 1, bits 3..5 n0/8, bits 6..7 log2(nw/8)
+//   z: index of the item's first stage in the CTA's stage list
+//   w: number of stages of the item (0 for a block row without blocks)
+struct alignas(16) ItemDesc {
+  uint32_t c_row, shape, k0, n;
+};
+static_assert(sizeof(ItemDesc) == 16, "ItemDesc layout");
+
+// One CTA task: items [item_off, item_end) and stages [stage_off, stage_end) of the plan's lists.
 struct alignas(16) Task {
-  int team_off[9];
-  int team_warps;     // warps per team
-  int stages;         // ring depth per team
-  int stage_floats;   // floats per stage
-  int stage_cols;     // block columns one stage holds
-  int pad[3];
+  int item_off, item_end, stage_off, stage_end;
+  int team_warps;     // warps per CTA
+  int stages;         // ring depth (slots)
+  int stage_floats;   // floats per slot
+  int stage_cols;     // block columns one stage holds at most
+  int pad[8];
 };
 static_assert(sizeof(Task) == 64, "Task layout");
 

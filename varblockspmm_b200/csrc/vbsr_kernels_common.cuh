@@ -14,12 +14,8 @@ namespace vbsr_b200 {
 typedef unsigned long long u64;
 
 struct KernelParams {
-  // B (K x rhs, column-major) as a 3-D tensor (k, j, q) with RHS column c = q * half + j, where
-  // half = 8 (rhs <= 32) or 16 (rhs = 64); see the operand stack in vbsr_tc.cuh.
-  CUtensorMap b_map;
-  int b_boxes;          // TMA boxes per 8-column group (one per quadrant: rhs/half)
-  uint32_t b_group_bytes;  // bytes the boxes of one group write to shared memory
-  const StageDesc* stages;  // per-team stage descriptors
+  const StageDesc* stages;  // stage descriptors of all CTAs
+  const ItemDesc* items;    // item descriptors of all CTAs
   const Task* tasks;
   const float* values;  // device-format values
   const float* B;
@@ -36,57 +32,96 @@ struct KernelParams {
 // ---- stage descriptors -----------------------------------------------------------------------------
 
 struct Stage {
-  u64 w0, w1, w2, w3;
+  u64 w0, w2, w3;
   __device__ __forceinline__ long long a_start() const { return (long long)(w0 & 0xfffffffull) * 64; }
   __device__ __forceinline__ int cols() const { return int(((w0 >> 28) & 3u) + 1u) * 8; }
-  __device__ __forceinline__ bool first() const { return (w0 >> 30) & 1u; }
-  __device__ __forceinline__ bool last() const { return (w0 >> 31) & 1u; }
   __device__ __forceinline__ int h() const { return int(((w0 >> 32) & 7u) + 1u) * 8; }
-  __device__ __forceinline__ bool empty() const { return (w0 >> 35) & 1u; }
   __device__ __forceinline__ int n0() const { return int((w0 >> 36) & 7u) * 8; }
   __device__ __forceinline__ int nw() const { return 8 << int((w0 >> 39) & 3u); }
-  __device__ __forceinline__ int c_row() const { return int(w1 & 0x7fffffffull); }
   __device__ __forceinline__ int group_col(int g) const {  // scalar column of 8-column group g
     const u64 w = g < 2 ? w2 : w3;
     return int((w >> (32 * (g & 1))) & 0xfffffffull) * 8;
   }
 };
 
-// A team's stage list [pos, end) seen through a window of 32 descriptors (lane i holds stage
-// wbase + i) and the following window, loaded one window ahead; reading a stage is four
-// independent shuffles. All lanes keep identical pos / wbase / end.
+struct Item {
+  uint32_t c_row, shape, k0, n;
+  __device__ __forceinline__ int h() const { return int((shape & 7u) + 1u) * 8; }
+  __device__ __forceinline__ int n0() const { return int((shape >> 3) & 7u) * 8; }
+  __device__ __forceinline__ int nw() const { return 8 << int((shape >> 6) & 3u); }
+};
+
+// Every `stride`-th stage descriptor from `first` on (count of them), seen through a window of 32
+// (lane i holds element wbase + i) and the following window, loaded one window ahead; reading a
+// word is two shuffles. All lanes keep identical pos / wbase.
 struct StageWin {
   ulonglong4 cur, next;
-  int pos, wbase, end;
+  const StageDesc* base;
+  int pos, wbase, count, stride;
 
-  __device__ __forceinline__ static ulonglong4 load(const StageDesc* s, int i, int end) {
-    if (i >= end) return make_ulonglong4(0, 0, 0, 0);
-    const ulonglong2* q = reinterpret_cast<const ulonglong2*>(s + i);
+  __device__ __forceinline__ ulonglong4 load(int i) const {
+    if (i >= count) return make_ulonglong4(0, 0, 0, 0);
+    const ulonglong2* q = reinterpret_cast<const ulonglong2*>(base + (long long)i * stride);
     const ulonglong2 a = __ldg(q), b = __ldg(q + 1);
     return make_ulonglong4(a.x, a.y, b.x, b.y);
   }
-  __device__ __forceinline__ void init(const StageDesc* s, int b, int e, int lane) {
-    pos = b;
-    wbase = b;
-    end = e;
-    cur = load(s, b + lane, e);
-    next = load(s, b + 32 + lane, e);
+  __device__ __forceinline__ void init(const StageDesc* s, int first, int stride_, int n, int lane) {
+    base = s + first;
+    stride = stride_;
+    count = first < n ? (n - first + stride_ - 1) / stride_ : 0;
+    pos = 0;
+    wbase = 0;
+    cur = load(lane);
+    next = load(32 + lane);
   }
-  __device__ __forceinline__ bool done() const { return pos >= end; }
-  __device__ __forceinline__ Stage peek() const {
+  template <int I>
+  __device__ __forceinline__ u64 word() const {
     const int src = (pos - wbase) & 31;
-    Stage st;
-    st.w0 = __shfl_sync(0xffffffffu, cur.x, src);
-    st.w1 = __shfl_sync(0xffffffffu, cur.y, src);
-    st.w2 = __shfl_sync(0xffffffffu, cur.z, src);
-    st.w3 = __shfl_sync(0xffffffffu, cur.w, src);
-    return st;
+    const u64 v = I == 0 ? cur.x : (I == 1 ? cur.y : (I == 2 ? cur.z : cur.w));
+    return __shfl_sync(0xffffffffu, v, src);
   }
-  __device__ __forceinline__ void advance(const StageDesc* s, int lane) {
+  __device__ __forceinline__ void advance(int lane) {
     if (++pos - wbase == 32) {
       wbase += 32;
       cur = next;
-      next = load(s, wbase + 32 + lane, end);
+      next = load(wbase + 32 + lane);
+    }
+  }
+};
+
+// The CTA's item descriptors through a window of 32, like StageWin (stride 1).
+struct ItemWin {
+  uint4 cur, next;
+  const ItemDesc* base;
+  int pos, wbase, count;
+
+  __device__ __forceinline__ uint4 load(int i) const {
+    if (i >= count) return make_uint4(0, 0, 0, 0);
+    return __ldg(reinterpret_cast<const uint4*>(base + i));
+  }
+  __device__ __forceinline__ void init(const ItemDesc* s, int n, int lane) {
+    base = s;
+    count = n;
+    pos = 0;
+    wbase = 0;
+    cur = load(lane);
+    next = load(32 + lane);
+  }
+  __device__ __forceinline__ bool done() const { return pos >= count; }
+  __device__ __forceinline__ Item get() const {
+    const int src = (pos - wbase) & 31;
+    Item it;
+    it.c_row = __shfl_sync(0xffffffffu, cur.x, src);
+    it.shape = __shfl_sync(0xffffffffu, cur.y, src);
+    it.k0 = __shfl_sync(0xffffffffu, cur.z, src);
+    it.n = __shfl_sync(0xffffffffu, cur.w, src);
+    return it;
+  }
+  __device__ __forceinline__ void advance(int lane) {
+    if (++pos - wbase == 32) {
+      wbase += 32;
+      cur = next;
+      next = load(wbase + 32 + lane);
     }
   }
 };
@@ -115,7 +150,8 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
   if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
   const long long t0 = clock64();
   while (true) {
-    if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
+    // suspended in hardware for up to ~20 us per probe, so a waiting warp issues few instructions
+    if (__all_sync(0xffffffffu, mbar_try_hint(bar, parity, 20000u))) return true;
     int stop = 0;
     if (lane == 0) {
       if (*abort_flag) {

@@ -1,5 +1,6 @@
-// vbsr_ptx.cuh — thin inline-PTX wrappers for the sm_100a features the kernels use: mbarriers
-// and 1-D TMA bulk copies (cp.async.bulk) with L2 cache hints. Hand-written; no library code.
+// vbsr_ptx.cuh — thin inline-PTX wrappers for the sm_100a features the kernels use: mbarriers,
+// 16-byte cp.async copies, 1-D bulk copies (cp.async.bulk) with L2 cache hints, and 16-byte
+// shared-memory accesses. Hand-written; no library code.
 #pragma once
 #include <cstdint>
 
@@ -7,6 +8,36 @@ namespace vbsr_b200 {
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte shared-memory load / store at a 32-bit shared address.
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w));
+}
+
+// 16-byte asynchronous copy global -> shared (L2 only), completion tracked with cp_async_arrive.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+// The mbarrier receives one arrival once every cp.async this thread issued so far has completed
+// (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Hint: bring the 128-byte line holding `p` into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -56,6 +87,18 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Probe that may suspend the thread until the phase completes, for at most about `hint_ns`.
+__device__ __forceinline__ bool mbar_try_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -79,26 +122,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
-// 2-D tensor TMA load (box from a tensor map) into shared memory, completion on `bar`.
-// x must be a multiple of 4 for 32-bit elements (16-byte aligned start).
-__device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const void* tmap, int x, int y,
-                                             uint32_t bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
-      : "memory");
-}
 
-// 3-D tensor TMA load (box from a tensor map) into shared memory, completion on `bar`.
-// x must be a multiple of 4 for 32-bit elements (16-byte aligned start).
-__device__ __forceinline__ void tensor3d_g2s(uint32_t dst, const void* tmap, int x, int y, int z,
-                                             uint32_t bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
-      : "memory");
-}
 
 }  // namespace vbsr_b200

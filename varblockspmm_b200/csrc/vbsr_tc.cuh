@@ -1,38 +1,40 @@
 // vbsr_tc.cuh — the sm_100a SpMM kernel on 5th-generation tensor cores (tcgen05, TMEM).
 //
 // Per work item (one block row i: an h x nw tile of C) the kernel computes the transposed product
-//     D (M x h) = sum over the row's blocks b of  S_b (M x w) * A_b^T (w x h)
-// with tcgen05.mma kind::tf32 (N = h, K = 8 per MMA) and an fp32 accumulator in tensor memory.
+//     D (M x 2h) = sum over the row's 8-column groups g of  S_g (M x 8) * [A_g ; A_g,lo]^T
+// with tcgen05.mma kind::tf32 (K = 8) and an fp32 accumulator in tensor memory.
 //
-// FP32 accuracy (3xTF32 with a stacked operand). The tensor core reads an fp32 operand as tf32 by
+// FP32 accuracy (3xTF32 in one MMA per group). The tensor core reads an fp32 operand as tf32 by
 // ignoring its low 13 mantissa bits (truncation), so for x = hi + lo with hi = trunc_tf32(x) the
 // raw value already acts as hi and only lo = x - hi has to be formed (exactly, in fp32). The M side
 // of the MMA is the operand stack S: for every RHS column c the raw B value (hi) and its lo part
-// sit in two rows of S. One MMA with the raw A then yields B_hi*A_hi and B_lo*A_hi, a second MMA
-// with A_lo yields B_hi*A_lo and B_lo*A_lo, and the epilogue adds each column's two rows: all
-// cross terms of 3xTF32 in two MMAs per 8 block columns instead of three. M = 64 for nw <= 32 and
-// M = 128 for nw = 64. The stack is built per quadrant q (32 TMEM lanes, the part of the
+// sit in two rows of S. The N side holds the group's h rows of raw A followed by its h rows of
+// A_lo. One MMA therefore produces all four products B_hi*A_hi, B_lo*A_hi, B_hi*A_lo, B_lo*A_lo
+// (the last one is below the tolerance but harmless), and the epilogue adds, for every C element,
+// the two S rows of its column at the two D columns of its row. M = 64 for nw <= 32 and M = 128
+// for nw = 64; N = 2h <= 128. The stack is built per quadrant q (32 TMEM lanes, the part of the
 // accumulator one warp may read): with half = M / 8 columns per quadrant, S rows 2*half*q + j and
 // 2*half*q + half + j hold hi and lo of column c = half*q + j, and in TMEM (M = 64: row r lives in
 // lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of quadrant q, so
 // a warp adds them with one shuffle.
 //
-// CTA = four MMA warps and two feeder warps, one CTA per SM. A single wait-and-release round on an
-// mbarrier costs a warp ~200 cycles even when the barrier has already completed, so every warp
-// handles only a share of the stages: stage k of the CTA (counting non-empty stages) is fed by
-// feeder k % 2 and multiplied by MMA warp k % 4. The CTA's list of stage descriptors (compiled by
-// the planner; vbsr_internal.h) is walked by every warp; the ring has D slots, stage k uses slot
-// k % D. A feeder copies the stage's A values with one cp.async.bulk (contiguous in the device
-// format, which holds every 8-column group as the K-major, 32-byte-swizzled operand tile the MMA
-// reads) and the B rows with one 3-D cp.async.bulk.tensor box per group and
-// quadrant, placed directly on the stack's hi rows. The owning MMA warp forms the stage's lo parts
-// (A_lo next to A, B_lo into the stack; loads batched for memory-level parallelism), fences them
-// for the async proxy, issues two MMAs per group into its own partial accumulator, and releases
-// the slot with tcgen05.commit. An item's result is read one item later (so the tensor cores work
-// on item j while item j-1 is stored): each warp reads its quadrant of the partials that received
-// stages with tcgen05.ld, sums them, adds hi and lo rows, and stores h consecutive floats of its
-// RHS columns. Every wait is bounded (see wait_phase); after an abort each warp drains its copies
-// and MMAs before the CTA releases its tensor memory.
+// CTA = eight warps, one CTA per SM:
+//   warps 0..3  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4, which
+//               forms A_lo next to each group's A and B_lo in the stack's lo rows, fences the
+//               writes for the async proxy and hands the slot to the MMA warp; they also store
+//               each item's result one item later (warp q reads TMEM quadrant q);
+//   warps 4, 5  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
+//               own accumulator, and the slot is released with tcgen05.commit;
+//   warps 6, 7  feeders: stage k is copied by feeder k % 2, in 16-byte cp.async pieces over its
+//               32 lanes (A to the groups' regions, B straight onto the stack's hi rows; per-request
+//               TMA descriptors cost ~130 cycles each, far more than these copies).
+// A single wait-and-release round on an mbarrier costs a warp ~200 cycles even when the barrier
+// has already completed, which is why every role is spread over several warps. The ring has D
+// slots, D a multiple of 4, stage k uses slot k % D: each slot then has one feeder, one split
+// warp and one MMA warp, all passing through its uses in order. Every warp walks the CTA's list of
+// stage descriptors (compiled by the planner; vbsr_internal.h). Every wait is bounded (see
+// wait_phase); the feeders wait for their copies and the MMA warps for their MMAs before the CTA
+// releases its tensor memory.
 #pragma once
 #include <cuda.h>
 
@@ -45,23 +47,23 @@
 
 namespace vbsr_b200 {
 
-constexpr int kTcMmaWarps = 4;              // MMA warps (one per TMEM quadrant)
+constexpr int kTcSplitWarps = 4;            // split / epilogue warps (one per TMEM quadrant)
+constexpr int kTcMmaWarps = 2;              // MMA-issuing warps
 constexpr int kTcFeeders = 2;               // feeder warps
-constexpr int kTcWarps = kTcMmaWarps + kTcFeeders;
+constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 // 8-column groups per stage: 4 (32 block columns) for rhs <= 32, 3 for rhs = 64, so that a slot
 // is 24 KB either way and eight slots fit in shared memory.
 __host__ __device__ constexpr int stage_groups(int rhs) { return rhs > 32 ? 3 : 4; }
-// Slot layout (floats), G = groups per stage: raw A (up to 64 rows x 8G columns, group after
-// group, h x 8 each) at 0, A_lo at the same offsets + 512 G, then the operand stacks of the
-// groups (M x 8 each) from 1024 G.
-__host__ __device__ constexpr int slot_alo(int G) { return 512 * G; }
+// Slot layout (floats), G = groups per stage: group g's N-side operand at 1024 g (h rows of raw A,
+// 8 floats each, followed by the h rows of A_lo), then the operand stacks of the groups (M x 8
+// each) from 1024 G.
 __host__ __device__ constexpr int slot_stack(int G) { return 1024 * G; }
 __host__ __device__ constexpr int slot_floats(int rhs) {
   return slot_stack(stage_groups(rhs)) + stage_groups(rhs) * stack_m(rhs) * 8;
 }
-// TMEM: 2 accumulator buffers (items alternate) x 4 partials (one per MMA warp) x 64 columns.
+// TMEM: 2 accumulator buffers (items alternate) x 2 partials (one per MMA warp) x 128 columns.
 constexpr int kTmemAlloc = 512;
 
 // ---- tcgen05 wrappers ------------------------------------------------------------------------------
@@ -148,7 +150,9 @@ __device__ __forceinline__ float4 lo_part4(float4 x) {
 
 // Barriers (shared-memory addresses).
 struct CtaBars {
-  uint32_t full0, empty0;   // per slot: copies landed / the stage's MMAs have read the slot
+  uint32_t full0;           // per slot: copies landed
+  uint32_t split0;          // per slot: lo parts written
+  uint32_t empty0;          // per slot: the stage's MMAs have read the slot
   uint32_t acc0, accfree0;  // per accumulator buffer: MMAs of the item done / D read by all warps
   uint32_t drain0;          // per MMA warp: end-of-kernel drain of its MMAs
 };
@@ -169,123 +173,129 @@ struct CtaBars {
 #endif
 
 // Feeder warp f: fills the slots of the stages k with k % kTcFeeders == f, each once the MMAs of
-// the slot's previous stage have completed.
+// the slot's previous stage have completed. The 32 lanes copy the stage in 16-byte pieces with
+// cp.async: A group g (h rows x 32 bytes, already in operand order in the device format) linearly
+// to the group's region, and B straight onto the stack's hi rows (row 2*half*q + j for RHS column
+// half*q + j, the 32-byte swizzle applied: the two 16-byte halves of a row are exchanged when bit
+// 2 of the row index is set). Each lane then arrives on the slot's full barrier once its copies
+// have landed (cp.async.mbarrier.arrive), so the barrier completes with the last piece.
 template <bool CHECK>
-__device__ void tc_feeder(const KernelParams& p, const Task& task, float* slots,
+__device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
                           const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
-  const int D = task.stages, SF = task.stage_floats;
+  const int D = task.stages, SF = task.stage_floats, G = task.stage_cols >> 3;
+  const int nst = task.stage_end - task.stage_off;
   StageWin win;
-  win.init(p.stages, task.team_off[0], task.team_off[1], lane);
-  int k = 0;  // non-empty stages seen
-  uint32_t filled = 0, lastpar = 0;
-  const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
+  win.init(p.stages + task.stage_off, f, kTcFeeders, nst, lane);
+  int s = f;  // slot of this feeder's next stage (its slots are f, f + kTcFeeders, ...)
+  uint32_t ph = 0;
   VBSR_PROF_T0(t_all);
-  while (!win.done()) {
-    const Stage st = win.peek();
-    win.advance(p.stages, lane);
-    if (st.empty()) continue;
-    const int kk = k++;
-    if (kk % kTcFeeders != f) continue;
-    const int s = kk % D;
-    const uint32_t ph = uint32_t(kk / D) & 1u;
+  for (int kk = f; kk < nst; kk += kTcFeeders) {
+    Stage st;
+    st.w0 = win.word<0>();
+    st.w2 = win.word<2>();
+    st.w3 = win.word<3>();
+    win.advance(lane);
     const uint32_t full_bar = cb.full0 + 8u * s;
     VBSR_PROF_T0(t_w);
     if (!wait_phase(cb.empty0 + 8u * s, ph ^ 1u, p, abort_flag, lane)) break;
     VBSR_PROF_ADD(p, 7, t_w);
-    const int h = st.h(), nw = st.nw(), n0 = st.n0(), cols = st.cols(), groups = cols >> 3;
+    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.cols() >> 3;
     const long long a0 = st.a_start();
     bool ok = true;
     if (CHECK) {
-      ok = a0 + (long long)h * cols <= p.nvalues && n0 + nw <= p.rhs && nw <= 64 &&
-           stack_m(nw) == stack_m(p.rhs) && cols <= task.stage_cols;
+      ok = a0 + 8ll * h * groups <= p.nvalues && n0 + nw <= p.rhs && nw <= 64 &&
+           stack_m(nw) == stack_m(p.rhs) && 8 * groups <= task.stage_cols;
       for (int g = 0; g < groups; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
     }
     if (kk == p.drop_stage) {
       // withhold the stage entirely (debug): no arrival, no copies
     } else if ((p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) || !ok) {
-      if (lane == 0) {
-        if (!ok) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
-        mbar_arrive(full_bar);  // release the MMA warp without touching memory
-      }
+      if (!ok && lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+      mbar_arrive(full_bar);  // every lane: release the split warp without touching memory
     } else {
-      float* sp = slots + s * SF;
-      const int M = stack_m(nw), half = M / 8, nb = p.b_boxes;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(full_bar,
-                              uint32_t(h * 4 * cols) + uint32_t(groups) * p.b_group_bytes);
-        bulk_g2s(smem_addr(sp), p.values + a0, uint32_t(h * 4 * cols), full_bar, pol_a);
-      } else if (lane <= groups * nb) {
-        const int g = (lane - 1) / nb, q = (lane - 1) % nb;
-        tensor3d_g2s(smem_addr(sp + slot_stack(task.stage_cols >> 3) + g * M * 8 + q * 2 * half * 8), &p.b_map,
-                     st.group_col(g), 0, n0 / half + q, full_bar, pol_b);
+      const uint32_t sp = slots + 4u * uint32_t(s * SF);
+      // A: groups x 2h pieces; piece i of group g -> byte 4096 g + 16 i
+      const float* asrc = p.values + a0;
+      const int run = 2 * h, na = run * groups;
+      for (int i = lane; i < na; i += 32) {
+        const int g = i >= run ? (i >= 2 * run ? (i >= 3 * run ? 3 : 2) : 1) : 0;
+        const int r = i - g * run;
+        cp_async16(sp + 4096u * g + 16u * r, asrc + 8ll * h * g + 4 * r);
       }
-      filled |= 1u << s;
-      lastpar = (lastpar & ~(1u << s)) | (ph << s);
+      // B: groups x nw columns x 2 halves; piece i -> (g, c, u)
+      const int M = stack_m(nw), half = M / 8;
+      const int lg_nw2 = __ffs(2 * nw) - 1, lg_half = __ffs(half) - 1;
+      const uint32_t stk = sp + 4u * uint32_t(slot_stack(G));
+      const int nb = 2 * nw * groups;
+      for (int i = lane; i < nb; i += 32) {
+        const int g = i >> lg_nw2, cu = i & (2 * nw - 1), c = cu >> 1, u = cu & 1;
+        const int row = ((c >> lg_half) << (lg_half + 1)) + (c & (half - 1));
+        const int col = g < 2 ? int((st.w2 >> (32 * (g & 1))) & 0xfffffffull) * 8
+                              : int((st.w3 >> (32 * (g & 1))) & 0xfffffffull) * 8;
+        cp_async16(stk + uint32_t(g * M * 32 + row * 32 + 16 * (u ^ ((row >> 2) & 1))),
+                   p.B + (long long)(n0 + c) * p.K + col + 4 * u);
+      }
+      cp_async_arrive(full_bar);
+    }
+    if ((s += kTcFeeders) >= D) {
+      s -= D;
+      ph ^= 1u;
     }
   }
   VBSR_PROF_ADD(p, 6, t_all);
-  // After an abort wait (bounded) for every copy still in flight before the CTA exits.
-  if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
-    for (int sl = 0; sl < D; ++sl) {
-      if (!(filled & (1u << sl))) continue;
-      const uint32_t bar = cb.full0 + 8u * sl;
-      const uint32_t par = (lastpar >> sl) & 1u;
-      const long long t1 = clock64();
-      while (!mbar_try(bar, par) && clock64() - t1 < p.wait_limit) {
-      }
-    }
-  }
+  cp_async_wait_all();  // nothing of this warp is still in flight when the CTA exits
 }
 
-// An item as the MMA warps remember it for the lagged epilogue.
-struct ItemInfo {
-  int h, nw, n0, c_row;
-  int k0;  // the CTA's running non-empty stage count at the item's first stage, mod 4
-  int n;   // non-empty stages of the item
-};
-
-// Epilogue of one item: D -> C, by MMA warp w (TMEM quadrant w). Partial k (64 columns further
-// for each k) holds the stages owned by warp k; only partials that received a stage are read.
-// Lane j < half of quadrant w holds hi of RHS column n0 + half*w + j, lane half + j its lo.
+// Epilogue of one item: D -> C, by split warp w (TMEM quadrant w). Partial i (128 columns after
+// partial 0) holds the stages issued by MMA warp i; only partials that received a stage are
+// read. Within a partial, column r is row r of the tile from raw A and column h + r the same row
+// from A_lo. Lane j < half of quadrant w holds hi of RHS column n0 + half*w + j, lane half + j lo.
 template <bool CHECK>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars& cb, int buf,
                                             uint32_t parity, uint32_t tmem_buf, int w, int lane,
-                                            const ItemInfo& it, volatile int* abort_flag) {
+                                            const Item& it, volatile int* abort_flag) {
   VBSR_PROF_T0(t_w);
   if (!wait_phase(cb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
   VBSR_PROF_ADD(p, 4, t_w);
   tc_fence_after();
-  const int h = it.h;
-  const int M = stack_m(it.nw), half = M / 8, quads = it.nw / half;
+  const int h = it.h(), nw = it.nw(), n0 = it.n0();
+  const int M = stack_m(nw), half = M / 8, quads = nw / half;
   uint32_t use = 0;
-  if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH))
-    for (int i = 0; i < 4 && i < it.n; ++i) use |= 1u << ((it.k0 + i) & 3);
+  if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
+    if (it.n >= 2) use = 3u;
+    else if (it.n == 1) use = 1u << (it.k0 & 1);
+  }
   if (w < quads) {
     const uint32_t taddr = tmem_buf + (uint32_t(32 * w) << 16);
-    const bool store = !(CHECK && ((long long)it.c_row + h > p.M || it.n0 + it.nw > p.rhs));
+    const bool store = !(CHECK && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs));
     if (CHECK && !store && w == 0 && lane == 0)
       record_status(p.status, VBSR_BOUNDS_VIOLATION, it.c_row);
-    const int col = it.n0 + half * w + lane;
+    const int col = n0 + half * w + lane;
     float4* dst = reinterpret_cast<float4*>(p.C + (long long)col * p.M + it.c_row);
-    // passes of 16 accumulator columns: 4 partials x 16 values in flight per pass
+    // passes of 16 tile rows: 2 partials x 2 halves (A, A_lo) x 16 values in flight per pass
     for (int c0 = 0; c0 < h; c0 += 16) {
       const bool two = c0 + 8 < h;
       float v[4][16];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (use & (1u << k)) {
-          tc_ld8_nowait(taddr + uint32_t(64 * k + c0), v[k]);
-          if (two) tc_ld8_nowait(taddr + uint32_t(64 * k + c0 + 8), v[k] + 8);
+      for (int i = 0; i < 2; ++i) {
+        if (use & (1u << i)) {
+          const uint32_t t0 = taddr + uint32_t(128 * i + c0);
+          tc_ld8_nowait(t0, v[2 * i]);
+          tc_ld8_nowait(t0 + uint32_t(h), v[2 * i + 1]);
+          if (two) {
+            tc_ld8_nowait(t0 + 8u, v[2 * i] + 8);
+            tc_ld8_nowait(t0 + uint32_t(h) + 8u, v[2 * i + 1] + 8);
+          }
         }
       }
       tc_wait_ld();
       float r[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int e = 0; e < 16; ++e) {
         float a = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) a += (use & (1u << k)) ? v[k][i] : 0.0f;
-        r[i] = a + __shfl_down_sync(0xffffffffu, a, half);
+        if (use & 1u) a += v[0][e] + v[1][e];
+        if (use & 2u) a += v[2][e] + v[3][e];
+        r[e] = a + __shfl_down_sync(0xffffffffu, a, half);
       }
       if (lane < half && store) {
         dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
@@ -303,141 +313,117 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   return true;
 }
 
-// lo parts of a whole stage: A_lo next to A (2h float4s per group, groups contiguous) and B_lo
-// into the stacks' lo rows. Eight independent loads per lane are in flight before the stores.
-__device__ __forceinline__ void split_stage(float* sp, int G, int groups, int h, int nw, int lane) {
-  const float4* a = reinterpret_cast<const float4*>(sp);
-  float4* alo = reinterpret_cast<float4*>(sp + slot_alo(G));
-  const int na = 2 * h * groups;
-  for (int i0 = 0; i0 < na; i0 += 256) {
-    float4 x[8];
+// lo parts of a whole stage at shared address sp: A_lo after each group's A (2h float4s per group)
+// and B_lo into the stacks' lo rows. Eight independent loads per lane are in flight before the
+// stores.
+__device__ __forceinline__ void split_stage(uint32_t sp, int G, int groups, int h, int nw, int lane) {
+  {
+    // A: group g's A at byte 4096 g (2h float4s), its A_lo right after it
+    const int run = 2 * h, na = run * groups;
+    for (int i0 = 0; i0 < na; i0 += 256) {
+      float4 x[8];
+      uint32_t o[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + 32 * u + lane;
-      if (i < na) x[u] = a[i];
-    }
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 32 * u + lane;
+        const int g = i >= run ? (i >= 2 * run ? (i >= 3 * run ? 3 : 2) : 1) : 0;
+        o[u] = sp + 4096u * g + 16u * uint32_t(i - g * run);
+        if (i < na) x[u] = lds128(o[u]);
+      }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + 32 * u + lane;
-      if (i < na) alo[i] = lo_part4(x[u]);
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 32 * u + lane;
+        if (i < na) sts128(o[u] + 32u * h, lo_part4(x[u]));
+      }
     }
   }
   const int M = stack_m(nw), half = M / 8;
-  float4* stk = reinterpret_cast<float4*>(sp + slot_stack(G));
-  // per group: M * 2 float4s; hi rows of quadrant q are float4s [4*half*q, 4*half*q + 2*half),
-  // the lo rows 2*half float4s later
-  const int per_group = 2 * nw, nb = per_group * groups;
+  const uint32_t stk = sp + 4u * uint32_t(slot_stack(G));
+  // per group: 2M float4s; the hi rows of quadrant q are float4s [4*half*q, 4*half*q + 2*half),
+  // the lo rows 2*half float4s later. Run t = g * quads + q of 2*half float4s (all powers of two).
+  const int lg_run = M == 128 ? 5 : 4;            // log2(2 * half)
+  const int lg_q = __ffs(nw / half) - 1;          // log2(quads)
+  const int nb = (2 * nw) * groups;
   for (int i0 = 0; i0 < nb; i0 += 256) {
     float4 x[8];
-    int o[8];
+    uint32_t o[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + 32 * u + lane;
-      const int g = i / per_group, r = i - g * per_group;
-      const int q = r / (2 * half), rr = r - q * 2 * half;
-      o[u] = g * 2 * M + 4 * half * q + rr;
-      if (i < nb) x[u] = stk[o[u]];
+      const int t = i >> lg_run, rr = i & ((1 << lg_run) - 1);
+      const int g = t >> lg_q, q = t & ((1 << lg_q) - 1);
+      o[u] = stk + 16u * uint32_t(g * 2 * M + (q << (lg_run + 1)) + rr);
+      if (i < nb) x[u] = lds128(o[u]);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + 32 * u + lane;
-      if (i < nb) stk[o[u] + 2 * half] = lo_part4(x[u]);
+      if (i < nb) sts128(o[u] + 32u * half, lo_part4(x[u]));
     }
   }
 }
 
-// MMA warp w (0..3): splits and multiplies the stages it owns (k % 4 == w), and stores each
-// item's result (its TMEM quadrant) one item later.
+// Split warp w (0..3): forms the lo parts of the stages k with k % 4 == w and stores each item's
+// result (TMEM quadrant w) one item later.
 template <bool CHECK>
-__device__ void tc_mma_warp(const KernelParams& p, const Task& task, float* slots,
-                            const CtaBars& cb, uint32_t tmem_base, int w, int lane,
-                            volatile int* abort_flag) {
+__device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
+                              const CtaBars& cb, uint32_t tmem_base, int w, int lane,
+                              volatile int* abort_flag) {
   const int D = task.stages, SF = task.stage_floats, G = task.stage_cols >> 3;
-  StageWin win;
-  win.init(p.stages, task.team_off[0], task.team_off[1], lane);
-  int k = 0;       // non-empty stages seen
-  int j = 0;       // items started
-  ItemInfo cur{8, 8, 0, 0, 0, 0}, prev{8, 8, 0, 0, 0, 0};
-  uint32_t tmem_d = tmem_base, idesc = 0, started = 0;
+  const int nst = task.stage_end - task.stage_off;
+  ItemWin iw;
+  iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
+  StageWin sw;
+  sw.init(p.stages + task.stage_off, w, kTcSplitWarps, nst, lane);
+  int kk = w;      // this warp's next stage
+  int ms = w;      // its slot (this warp's slots are w, w + 4, ...)
+  uint32_t mph = 0;
+  int j = 0;       // items done
+  Item prev{};
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
-  const uint32_t sbase = smem_addr(slots);
   bool ok = true;
   VBSR_PROF_T0(t_all);
-  while (!win.done()) {
-    const Stage st = win.peek();
-    win.advance(p.stages, lane);
-    if (st.first()) {
-      cur = ItemInfo{st.h(), st.nw(), st.n0(), st.c_row(), k & 3, 0};
-      const int buf = j & 1;
-      // the buffer's previous item (j-2) must have been read out by every warp
-      VBSR_PROF_T0(t_f);
-      if (j >= 2 && !wait_phase(cb.accfree0 + 8u * buf, uint32_t(((j - 2) >> 1) & 1), p,
-                                abort_flag, lane)) {
+  while (ok && !iw.done()) {
+    const Item it = iw.get();
+    iw.advance(lane);
+    const int h = it.h(), nw = it.nw();
+    for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcSplitWarps) {
+      const int cols = int(((sw.word<0>() >> 28) & 3u) + 1u) * 8;
+      sw.advance(lane);
+      const int s = ms;
+      const uint32_t par = mph;
+      if ((ms += kTcSplitWarps) >= D) {
+        ms -= D;
+        mph ^= 1u;
+      }
+      VBSR_PROF_T0(t_w);
+      if (!wait_phase(cb.full0 + 8u * s, par, p, abort_flag, lane)) {
         ok = false;
         break;
       }
-      VBSR_PROF_ADD(p, 5, t_f);
-      tc_fence_after();
-      tmem_d = tmem_base + uint32_t(256 * buf + 64 * w);
-      idesc = tf32_idesc(stack_m(cur.nw), cur.h);
-      started = 0;
-    }
-    if (!st.empty()) {
-      const int kk = k++;
-      ++cur.n;
-      if ((kk & 3) == w) {
-        const int s = kk % D;
-        VBSR_PROF_T0(t_w);
-        if (!wait_phase(cb.full0 + 8u * s, uint32_t(kk / D) & 1u, p, abort_flag, lane)) {
-          ok = false;
-          break;
-        }
-        VBSR_PROF_ADD(p, 1, t_w);
-        const int groups = st.cols() >> 3;
-        if (math) {
-          VBSR_PROF_T0(t_s);
-          split_stage(slots + s * SF, G, groups, cur.h, cur.nw, lane);
-          fence_proxy_async_smem();
-          __syncwarp();
-          VBSR_PROF_ADD(p, 2, t_s);
-        }
-        VBSR_PROF_T0(t_m);
-        if (lane == 0) {
-          if (math) {
-            tc_fence_after();
-            const uint32_t sa = sbase + 4u * uint32_t(s * SF);
-            const int M = stack_m(cur.nw);
-            for (int g = 0; g < groups; ++g) {
-              const uint64_t sdesc = sw32_desc(sa + 4u * uint32_t(slot_stack(G) + g * M * 8));
-              const uint64_t adesc = sw32_desc(sa + 4u * uint32_t(g * 8 * cur.h));
-              const uint64_t ldesc = sw32_desc(sa + 4u * uint32_t(slot_alo(G) + g * 8 * cur.h));
-              tc_mma_tf32(tmem_d, sdesc, adesc, idesc, started);
-              tc_mma_tf32(tmem_d, sdesc, ldesc, idesc, 1u);
-              started = 1u;
-            }
-          }
-          tc_commit(cb.empty0 + 8u * s);  // the slot is free once these MMAs have read it
-        }
-        __syncwarp();
-        VBSR_PROF_ADD(p, 3, t_m);
+      VBSR_PROF_ADD(p, 1, t_w);
+      VBSR_PROF_T0(t_s);
+      if (math) {
+        split_stage(slots + 4u * uint32_t(s * SF), G, cols >> 3, h, nw, lane);
+        fence_proxy_async_smem();
       }
-    }
-    if (st.last()) {
-      if (lane == 0) tc_commit(cb.acc0 + 8u * (j & 1));  // this warp's part of the item is issued
       __syncwarp();
-      if (j > 0) {
-        const int pj = j - 1;
-        VBSR_PROF_T0(t_e);
-        if (!tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1),
-                                tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, abort_flag)) {
-          ok = false;
-          break;
-        }
-        VBSR_PROF_ADD(p, 8, t_e);
-      }
-      prev = cur;
-      ++j;
+      if (lane == 0) mbar_arrive(cb.split0 + 8u * s);
+      VBSR_PROF_ADD(p, 2, t_s);
     }
+    if (!ok) break;
+    if (j > 0) {
+      const int pj = j - 1;
+      VBSR_PROF_T0(t_e);
+      if (!tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1),
+                              tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, abort_flag)) {
+        ok = false;
+        break;
+      }
+      VBSR_PROF_ADD(p, 8, t_e);
+    }
+    prev = it;
+    ++j;
   }
   if (ok && j > 0) {
     const int pj = j - 1;
@@ -445,12 +431,83 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, float* slot
                        w, lane, prev, abort_flag);
   }
   VBSR_PROF_ADD(p, 0, t_all);
+}
+
+// MMA warp i (0..1): issues the stages k with k % 2 == i, one MMA per group into its partial
+// accumulator (TMEM columns 256 * buffer + 128 * i).
+template <bool CHECK>
+__device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
+                            const CtaBars& cb, uint32_t tmem_base, int i, int lane,
+                            volatile int* abort_flag) {
+  const int D = task.stages, SF = task.stage_floats, G = task.stage_cols >> 3;
+  const int nst = task.stage_end - task.stage_off;
+  ItemWin iw;
+  iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
+  StageWin sw;
+  sw.init(p.stages + task.stage_off, i, kTcMmaWarps, nst, lane);
+  int kk = i;      // this warp's next stage
+  int ms = i;      // its slot (this warp's slots are i, i + 2, ...)
+  uint32_t mph = 0;
+  int j = 0;       // items started
+  const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
+  bool ok = true;
+  VBSR_PROF_T0(t_all);
+  while (ok && !iw.done()) {
+    const Item it = iw.get();
+    iw.advance(lane);
+    const int buf = j & 1;
+    // the buffer's previous item (j-2) must have been read out by every split warp
+    VBSR_PROF_T0(t_f);
+    if (j >= 2 && !wait_phase(cb.accfree0 + 8u * buf, uint32_t(((j - 2) >> 1) & 1), p,
+                              abort_flag, lane))
+      break;
+    VBSR_PROF_ADD(p, 5, t_f);
+    tc_fence_after();
+    const int M = stack_m(it.nw());
+    const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 128 * i);
+    const uint32_t idesc = tf32_idesc(M, 2 * it.h());
+    uint32_t started = 0;
+    for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
+      const int groups = int((sw.word<0>() >> 28) & 3u) + 1;
+      sw.advance(lane);
+      const int s = ms;
+      const uint32_t par = mph;
+      if ((ms += kTcMmaWarps) >= D) {
+        ms -= D;
+        mph ^= 1u;
+      }
+      VBSR_PROF_T0(t_w);
+      if (!wait_phase(cb.split0 + 8u * s, par, p, abort_flag, lane)) {
+        ok = false;
+        break;
+      }
+      VBSR_PROF_ADD(p, 3, t_w);
+      if (lane == 0) {
+        if (math) {
+          tc_fence_after();
+          const uint32_t sa = slots + 4u * uint32_t(s * SF);
+          for (int g = 0; g < groups; ++g) {
+            tc_mma_tf32(tmem_d, sw32_desc(sa + 4u * uint32_t(slot_stack(G) + g * M * 8)),
+                        sw32_desc(sa + 4096u * g), idesc, started);
+            started = 1u;
+          }
+        }
+        tc_commit(cb.empty0 + 8u * s);  // the slot is free once these MMAs have read it
+      }
+      __syncwarp();
+    }
+    if (!ok) break;
+    if (lane == 0) tc_commit(cb.acc0 + 8u * buf);  // this warp's part of the item is issued
+    __syncwarp();
+    ++j;
+  }
+  VBSR_PROF_ADD(p, 9, t_all);
   // Every MMA this warp issued has completed before the CTA releases its tensor memory (bounded).
-  if (lane == 0) tc_commit(cb.drain0 + 8u * w);
+  if (lane == 0) tc_commit(cb.drain0 + 8u * i);
   __syncwarp();
   {
     const long long t0 = clock64();
-    while (!mbar_try(cb.drain0 + 8u * w, 0) && clock64() - t0 < p.wait_limit) {
+    while (!mbar_try(cb.drain0 + 8u * i, 0) && clock64() - t0 < p.wait_limit) {
     }
   }
 }
@@ -458,9 +515,8 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, float* slot
 template <bool CHECK>
 __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  float* slots = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bars[2][kMaxStages];  // full, empty
+  const uint32_t slots = (smem_addr(smem_raw) + 1023u) & ~1023u;  // 1024-aligned ring
+  __shared__ __align__(8) uint64_t bars[3][kMaxStages];  // full, split, empty
   __shared__ __align__(8) uint64_t accbars[2][2];        // acc done, acc free
   __shared__ __align__(8) uint64_t drainbars[kTcMmaWarps];
   __shared__ uint32_t tmem_slot;
@@ -474,14 +530,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   if (threadIdx.x == 32) {
     if (p.timing) p.timing[2 * blockIdx.x] = global_ns();
     for (int s = 0; s < task.stages; ++s) {
-      mbar_init(smem_addr(&bars[0][s]), 1u);                    // TMA: one arrival + tx bytes
-      mbar_init(smem_addr(&bars[1][s]), 1u);                    // the owner's tcgen05.commit
+      mbar_init(smem_addr(&bars[0][s]), 32u);  // one cp.async arrival per feeder lane
+      mbar_init(smem_addr(&bars[1][s]), 1u);  // the split warp
+      mbar_init(smem_addr(&bars[2][s]), 1u);  // the MMA warp's tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_addr(&accbars[0][b]), uint32_t(kTcMmaWarps));
-      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcMmaWarps));
+      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcSplitWarps));
     }
-    for (int w = 0; w < kTcMmaWarps; ++w) mbar_init(smem_addr(&drainbars[w]), 1u);
+    for (int i = 0; i < kTcMmaWarps; ++i) mbar_init(smem_addr(&drainbars[i]), 1u);
     abort_flag = 0;
     mbar_fence_init();
   }
@@ -491,14 +548,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   const uint32_t tmem_base = tmem_slot;
   CtaBars cb;
   cb.full0 = smem_addr(&bars[0][0]);
-  cb.empty0 = smem_addr(&bars[1][0]);
+  cb.split0 = smem_addr(&bars[1][0]);
+  cb.empty0 = smem_addr(&bars[2][0]);
   cb.acc0 = smem_addr(&accbars[0][0]);
   cb.accfree0 = smem_addr(&accbars[1][0]);
   cb.drain0 = smem_addr(&drainbars[0]);
-  if (warp < kTcMmaWarps)
-    tc_mma_warp<CHECK>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
+  if (warp < kTcSplitWarps)
+    tc_split_warp<CHECK>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
+  else if (warp < kTcSplitWarps + kTcMmaWarps)
+    tc_mma_warp<CHECK>(p, task, slots, cb, tmem_base, warp - kTcSplitWarps, lane, &abort_flag);
   else
-    tc_feeder<CHECK>(p, task, slots, cb, warp - kTcMmaWarps, lane, &abort_flag);
+    tc_feeder<CHECK>(p, task, slots, cb, warp - kTcSplitWarps - kTcMmaWarps, lane, &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
