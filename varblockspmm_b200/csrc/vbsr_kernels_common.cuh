@@ -14,6 +14,7 @@ namespace vbsr_b200 {
 typedef unsigned long long u64;
 
 struct KernelParams {
+  CUtensorMap b_map;    // B (K x rhs, column-major) as a 2-D tensor, box 8 columns x rhs rows
   const StageDesc* stages;  // stage descriptors of all CTAs
   const ItemDesc* items;    // item descriptors of all CTAs
   const Task* tasks;

@@ -1,6 +1,6 @@
 // vbsr_ptx.cuh — thin inline-PTX wrappers for the sm_100a features the kernels use: mbarriers,
-// 16-byte cp.async copies, 1-D bulk copies (cp.async.bulk) with L2 cache hints, and 16-byte
-// shared-memory accesses. Hand-written; no library code.
+// TMA copies (1-D cp.async.bulk, 2-D cp.async.bulk.tensor) with L2 cache hints, 16-byte cp.async
+// copies, and 16-byte shared-memory accesses. Hand-written; no library code.
 #pragma once
 #include <cstdint>
 
@@ -31,10 +31,6 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
 // (the barrier's expected count includes this arrival).
 __device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-// Hint: bring the 128-byte line holding `p` into L2.
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -123,5 +119,16 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 }
 
 
+
+// 2-D tensor TMA load (box from a tensor map) into shared memory, completion on `bar`.
+// x must be a multiple of 4 for 32-bit elements (16-byte aligned start).
+__device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const void* tmap, int x, int y,
+                                             uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
 
 }  // namespace vbsr_b200

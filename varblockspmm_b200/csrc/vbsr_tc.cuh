@@ -12,11 +12,10 @@
 // A_lo. One MMA therefore produces all four products B_hi*A_hi, B_lo*A_hi, B_hi*A_lo, B_lo*A_lo
 // (the last one is below the tolerance but harmless), and the epilogue adds, for every C element,
 // the two S rows of its column at the two D columns of its row. M = 64 for nw <= 32 and M = 128
-// for nw = 64; N = 2h <= 128. The stack is built per quadrant q (32 TMEM lanes, the part of the
-// accumulator one warp may read): with half = M / 8 columns per quadrant, S rows 2*half*q + j and
-// 2*half*q + half + j hold hi and lo of column c = half*q + j, and in TMEM (M = 64: row r lives in
-// lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of quadrant q, so
-// a warp adds them with one shuffle.
+// for nw = 64; N = 2h <= 128. S holds raw B in rows 0..nw-1 (one TMA box) and B_lo M/2 rows
+// further; in TMEM (M = 64: row r lives in lane r % 16 of quadrant r / 16; M = 128: lane r % 32 of
+// quadrant r / 32) hi and lo of a column therefore sit in the same lane of quadrants q and q + 2,
+// and the epilogue adds them through a small shared-memory exchange between those two warps.
 //
 // CTA = eight warps, one CTA per SM:
 //   warps 0..3  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4, which
@@ -25,16 +24,16 @@
 //               each item's result one item later (warp q reads TMEM quadrant q);
 //   warps 4, 5  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 6, 7  feeders: stage k is copied by feeder k % 2, in 16-byte cp.async pieces over its
-//               32 lanes (A to the groups' regions, B straight onto the stack's hi rows; per-request
-//               TMA descriptors cost ~130 cycles each, far more than these copies).
+//   warps 6, 7  feeders: stage k is copied by feeder k % 2 with two TMA operations per group (one
+//               cp.async.bulk for the group's A, one 2-D cp.async.bulk.tensor box of 8 columns x nw
+//               rows of B onto the stack's hi rows).
 // A single wait-and-release round on an mbarrier costs a warp ~200 cycles even when the barrier
 // has already completed, which is why every role is spread over several warps. The ring has D
 // slots, D a multiple of 4, stage k uses slot k % D: each slot then has one feeder, one split
 // warp and one MMA warp, all passing through its uses in order. Every warp walks the CTA's list of
 // stage descriptors (compiled by the planner; vbsr_internal.h). Every wait is bounded (see
-// wait_phase); the feeders wait for their copies and the MMA warps for their MMAs before the CTA
-// releases its tensor memory.
+// wait_phase); after an abort the feeders wait for their copies and the MMA warps for their MMAs
+// before the CTA releases its tensor memory.
 #pragma once
 #include <cuda.h>
 
@@ -58,8 +57,10 @@ __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 __host__ __device__ constexpr int stage_groups(int rhs) { return rhs > 32 ? 3 : 4; }
 // Slot layout (floats), G = groups per stage: group g's N-side operand at 1024 g (h rows of raw A,
 // 8 floats each, followed by the h rows of A_lo), then the operand stacks of the groups (M x 8
-// each) from 1024 G.
+// each: raw B in rows 0..nw-1, B_lo in rows M/2..M/2+nw-1) from 1024 G.
 __host__ __device__ constexpr int slot_stack(int G) { return 1024 * G; }
+// Epilogue exchange after the ring: per hi/lo warp pair, 32 lanes x 64 floats.
+constexpr int kXchgBytes = 2 * 32 * 64 * 4;
 __host__ __device__ constexpr int slot_floats(int rhs) {
   return slot_stack(stage_groups(rhs)) + stage_groups(rhs) * stack_m(rhs) * 8;
 }
@@ -154,6 +155,7 @@ struct CtaBars {
   uint32_t split0;          // per slot: lo parts written
   uint32_t empty0;          // per slot: the stage's MMAs have read the slot
   uint32_t acc0, accfree0;  // per accumulator buffer: MMAs of the item done / D read by all warps
+  uint32_t xfull0, xfree0;  // per warp pair: lo sums written / read
   uint32_t drain0;          // per MMA warp: end-of-kernel drain of its MMAs
 };
 
@@ -173,12 +175,7 @@ struct CtaBars {
 #endif
 
 // Feeder warp f: fills the slots of the stages k with k % kTcFeeders == f, each once the MMAs of
-// the slot's previous stage have completed. The 32 lanes copy the stage in 16-byte pieces with
-// cp.async: A group g (h rows x 32 bytes, already in operand order in the device format) linearly
-// to the group's region, and B straight onto the stack's hi rows (row 2*half*q + j for RHS column
-// half*q + j, the 32-byte swizzle applied: the two 16-byte halves of a row are exchanged when bit
-// 2 of the row index is set). Each lane then arrives on the slot's full barrier once its copies
-// have landed (cp.async.mbarrier.arrive), so the barrier completes with the last piece.
+// the slot's previous stage have completed.
 template <bool CHECK>
 __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
                           const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
@@ -188,6 +185,8 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   win.init(p.stages + task.stage_off, f, kTcFeeders, nst, lane);
   int s = f;  // slot of this feeder's next stage (its slots are f, f + kTcFeeders, ...)
   uint32_t ph = 0;
+  uint32_t filled = 0, lastpar = 0;
+  const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
   VBSR_PROF_T0(t_all);
   for (int kk = f; kk < nst; kk += kTcFeeders) {
     Stage st;
@@ -203,39 +202,33 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     const long long a0 = st.a_start();
     bool ok = true;
     if (CHECK) {
-      ok = a0 + 8ll * h * groups <= p.nvalues && n0 + nw <= p.rhs && nw <= 64 &&
-           stack_m(nw) == stack_m(p.rhs) && 8 * groups <= task.stage_cols;
+      ok = a0 + 8ll * h * groups <= p.nvalues && n0 + nw <= p.rhs && nw == p.rhs &&
+           8 * groups <= task.stage_cols;
       for (int g = 0; g < groups; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
     }
     if (kk == p.drop_stage) {
       // withhold the stage entirely (debug): no arrival, no copies
     } else if ((p.diag & VBSR_PLAN_DIAG_SKIP_COPIES) || !ok) {
-      if (!ok && lane == 0) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
-      mbar_arrive(full_bar);  // every lane: release the split warp without touching memory
+      if (lane == 0) {
+        if (!ok) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
+        mbar_arrive(full_bar);  // release the split warp without touching memory
+      }
     } else {
       const uint32_t sp = slots + 4u * uint32_t(s * SF);
-      // A: groups x 2h pieces; piece i of group g -> byte 4096 g + 16 i
-      const float* asrc = p.values + a0;
-      const int run = 2 * h, na = run * groups;
-      for (int i = lane; i < na; i += 32) {
-        const int g = i >= run ? (i >= 2 * run ? (i >= 3 * run ? 3 : 2) : 1) : 0;
-        const int r = i - g * run;
-        cp_async16(sp + 4096u * g + 16u * r, asrc + 8ll * h * g + 4 * r);
+      const int M = stack_m(nw);
+      if (lane == 0) mbar_arrive_expect_tx(full_bar, uint32_t(groups * 32 * (h + nw)));
+      __syncwarp();
+      if (lane < groups) {
+        // group `lane`: h rows x 8 floats, contiguous in the device format
+        bulk_g2s(sp + 4096u * lane, p.values + a0 + 8ll * h * lane, uint32_t(32 * h), full_bar,
+                 pol_a);
+      } else if (lane < 2 * groups) {
+        const int g = lane - groups;
+        tensor2d_g2s(sp + 4u * uint32_t(slot_stack(G) + g * M * 8), &p.b_map, st.group_col(g), n0,
+                     full_bar, pol_b);
       }
-      // B: groups x nw columns x 2 halves; piece i -> (g, c, u)
-      const int M = stack_m(nw), half = M / 8;
-      const int lg_nw2 = __ffs(2 * nw) - 1, lg_half = __ffs(half) - 1;
-      const uint32_t stk = sp + 4u * uint32_t(slot_stack(G));
-      const int nb = 2 * nw * groups;
-      for (int i = lane; i < nb; i += 32) {
-        const int g = i >> lg_nw2, cu = i & (2 * nw - 1), c = cu >> 1, u = cu & 1;
-        const int row = ((c >> lg_half) << (lg_half + 1)) + (c & (half - 1));
-        const int col = g < 2 ? int((st.w2 >> (32 * (g & 1))) & 0xfffffffull) * 8
-                              : int((st.w3 >> (32 * (g & 1))) & 0xfffffffull) * 8;
-        cp_async16(stk + uint32_t(g * M * 32 + row * 32 + 16 * (u ^ ((row >> 2) & 1))),
-                   p.B + (long long)(n0 + c) * p.K + col + 4 * u);
-      }
-      cp_async_arrive(full_bar);
+      filled |= 1u << s;
+      lastpar = (lastpar & ~(1u << s)) | (ph << s);
     }
     if ((s += kTcFeeders) >= D) {
       s -= D;
@@ -243,35 +236,58 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     }
   }
   VBSR_PROF_ADD(p, 6, t_all);
-  cp_async_wait_all();  // nothing of this warp is still in flight when the CTA exits
+  // After an abort wait (bounded) for every copy still in flight before the CTA exits.
+  if (__shfl_sync(0xffffffffu, *abort_flag, 0)) {
+    for (int sl = 0; sl < D; ++sl) {
+      if (!(filled & (1u << sl))) continue;
+      const uint32_t bar = cb.full0 + 8u * sl;
+      const uint32_t par = (lastpar >> sl) & 1u;
+      const long long t1 = clock64();
+      while (!mbar_try(bar, par) && clock64() - t1 < p.wait_limit) {
+      }
+    }
+  }
 }
 
-// Epilogue of one item: D -> C, by split warp w (TMEM quadrant w). Partial i (128 columns after
-// partial 0) holds the stages issued by MMA warp i; only partials that received a stage are
-// read. Within a partial, column r is row r of the tile from raw A and column h + r the same row
-// from A_lo. Lane j < half of quadrant w holds hi of RHS column n0 + half*w + j, lane half + j lo.
+// Epilogue of item j: D -> C, by split warp w (TMEM quadrant w). Partial i (128 columns after
+// partial 0) holds the stages issued by MMA warp i; only partials that received a stage are read.
+// Within a partial, column r is row r of the tile from raw A and column h + r the same row from
+// A_lo. With rq = M/4 stack rows per quadrant, lane l of quadrant w < 2 holds the hi part of RHS
+// column c = rq*w + l and the same lane of quadrant w + 2 its lo part: the lo warp writes its sums
+// to the pair's exchange buffer, the hi warp adds them and stores h consecutive floats of column
+// n0 + c.
 template <bool CHECK>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars& cb, int buf,
                                             uint32_t parity, uint32_t tmem_buf, int w, int lane,
-                                            const Item& it, volatile int* abort_flag) {
+                                            const Item& it, int j, uint32_t xbuf,
+                                            volatile int* abort_flag) {
   VBSR_PROF_T0(t_w);
   if (!wait_phase(cb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
   VBSR_PROF_ADD(p, 4, t_w);
   tc_fence_after();
   const int h = it.h(), nw = it.nw(), n0 = it.n0();
-  const int M = stack_m(nw), half = M / 8, quads = nw / half;
+  const int rq = stack_m(nw) / 4, hq = (nw + rq - 1) / rq;
   uint32_t use = 0;
   if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
     if (it.n >= 2) use = 3u;
     else if (it.n == 1) use = 1u << (it.k0 & 1);
   }
-  if (w < quads) {
+  const int pr = w & 1;
+  const bool hi = w < hq, lo = w >= 2 && pr < hq;
+  if (hi || lo) {
     const uint32_t taddr = tmem_buf + (uint32_t(32 * w) << 16);
-    const bool store = !(CHECK && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs));
-    if (CHECK && !store && w == 0 && lane == 0)
-      record_status(p.status, VBSR_BOUNDS_VIOLATION, it.c_row);
-    const int col = n0 + half * w + lane;
-    float4* dst = reinterpret_cast<float4*>(p.C + (long long)col * p.M + it.c_row);
+    const uint32_t xb = xbuf + uint32_t(pr * 32 * 64 * 4 + lane * 64 * 4);
+    if (lo && j >= 1 &&
+        !wait_phase(cb.xfree0 + 8u * pr, uint32_t((j - 1) & 1), p, abort_flag, lane))
+      return false;
+    if (hi && !wait_phase(cb.xfull0 + 8u * pr, uint32_t(j & 1), p, abort_flag, lane))
+      return false;
+    const int c = rq * w + lane;  // hi warps: RHS column within the tile
+    const bool store = hi && lane < rq && c < nw &&
+                       !(CHECK && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs));
+    if (CHECK && hi && w == 0 && lane == 0 && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs))
+      record_status(p.status, VBSR_BOUNDS_VIOLATION, int(it.c_row));
+    float4* dst = reinterpret_cast<float4*>(p.C + (long long)(n0 + c) * p.M + it.c_row);
     // passes of 16 tile rows: 2 partials x 2 halves (A, A_lo) x 16 values in flight per pass
     for (int c0 = 0; c0 < h; c0 += 16) {
       const bool two = c0 + 8 < h;
@@ -295,17 +311,37 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
         float a = 0.0f;
         if (use & 1u) a += v[0][e] + v[1][e];
         if (use & 2u) a += v[2][e] + v[3][e];
-        r[e] = a + __shfl_down_sync(0xffffffffu, a, half);
+        r[e] = a;
       }
-      if (lane < half && store) {
-        dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
-        dst[c0 / 4 + 1] = make_float4(r[4], r[5], r[6], r[7]);
+      const uint32_t xa = xb + 4u * uint32_t(c0);
+      if (lo) {
+        sts128(xa, make_float4(r[0], r[1], r[2], r[3]));
+        sts128(xa + 16u, make_float4(r[4], r[5], r[6], r[7]));
         if (two) {
-          dst[c0 / 4 + 2] = make_float4(r[8], r[9], r[10], r[11]);
-          dst[c0 / 4 + 3] = make_float4(r[12], r[13], r[14], r[15]);
+          sts128(xa + 32u, make_float4(r[8], r[9], r[10], r[11]));
+          sts128(xa + 48u, make_float4(r[12], r[13], r[14], r[15]));
+        }
+      } else {
+        const float4 x0 = lds128(xa), x1 = lds128(xa + 16u);
+        r[0] += x0.x; r[1] += x0.y; r[2] += x0.z; r[3] += x0.w;
+        r[4] += x1.x; r[5] += x1.y; r[6] += x1.z; r[7] += x1.w;
+        if (two) {
+          const float4 x2 = lds128(xa + 32u), x3 = lds128(xa + 48u);
+          r[8] += x2.x; r[9] += x2.y; r[10] += x2.z; r[11] += x2.w;
+          r[12] += x3.x; r[13] += x3.y; r[14] += x3.z; r[15] += x3.w;
+        }
+        if (store) {
+          dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
+          dst[c0 / 4 + 1] = make_float4(r[4], r[5], r[6], r[7]);
+          if (two) {
+            dst[c0 / 4 + 2] = make_float4(r[8], r[9], r[10], r[11]);
+            dst[c0 / 4 + 3] = make_float4(r[12], r[13], r[14], r[15]);
+          }
         }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(lo ? cb.xfull0 + 8u * pr : cb.xfree0 + 8u * pr);
   }
   tc_fence_before();
   __syncwarp();
@@ -314,7 +350,7 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
 }
 
 // lo parts of a whole stage at shared address sp: A_lo after each group's A (2h float4s per group)
-// and B_lo into the stacks' lo rows. Eight independent loads per lane are in flight before the
+// and B_lo into the stacks' lo rows (M/2 rows after the hi rows). Eight independent loads per lane are in flight before the
 // stores.
 __device__ __forceinline__ void split_stage(uint32_t sp, int G, int groups, int h, int nw, int lane) {
   {
@@ -337,12 +373,10 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int G, int groups, int 
       }
     }
   }
-  const int M = stack_m(nw), half = M / 8;
+  // B: per group the hi rows 0..nw-1 (2nw float4s, contiguous); the lo rows M/2 rows further
+  const int M = stack_m(nw);
   const uint32_t stk = sp + 4u * uint32_t(slot_stack(G));
-  // per group: 2M float4s; the hi rows of quadrant q are float4s [4*half*q, 4*half*q + 2*half),
-  // the lo rows 2*half float4s later. Run t = g * quads + q of 2*half float4s (all powers of two).
-  const int lg_run = M == 128 ? 5 : 4;            // log2(2 * half)
-  const int lg_q = __ffs(nw / half) - 1;          // log2(quads)
+  const int lg_run = __ffs(2 * nw) - 1;
   const int nb = (2 * nw) * groups;
   for (int i0 = 0; i0 < nb; i0 += 256) {
     float4 x[8];
@@ -350,15 +384,14 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int G, int groups, int 
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + 32 * u + lane;
-      const int t = i >> lg_run, rr = i & ((1 << lg_run) - 1);
-      const int g = t >> lg_q, q = t & ((1 << lg_q) - 1);
-      o[u] = stk + 16u * uint32_t(g * 2 * M + (q << (lg_run + 1)) + rr);
+      const int g = i >> lg_run, r = i & ((1 << lg_run) - 1);
+      o[u] = stk + uint32_t(g * M * 32 + 16 * r);
       if (i < nb) x[u] = lds128(o[u]);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + 32 * u + lane;
-      if (i < nb) sts128(o[u] + 32u * half, lo_part4(x[u]));
+      if (i < nb) sts128(o[u] + 16u * M, lo_part4(x[u]));
     }
   }
 }
@@ -380,6 +413,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   uint32_t mph = 0;
   int j = 0;       // items done
   Item prev{};
+  const uint32_t xbuf = slots + 4u * uint32_t(D * SF);
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
   bool ok = true;
   VBSR_PROF_T0(t_all);
@@ -416,7 +450,8 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       const int pj = j - 1;
       VBSR_PROF_T0(t_e);
       if (!tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1),
-                              tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, abort_flag)) {
+                              tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, pj, xbuf,
+                              abort_flag)) {
         ok = false;
         break;
       }
@@ -428,7 +463,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   if (ok && j > 0) {
     const int pj = j - 1;
     tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1), tmem_base + uint32_t(256 * (pj & 1)),
-                       w, lane, prev, abort_flag);
+                       w, lane, prev, pj, xbuf, abort_flag);
   }
   VBSR_PROF_ADD(p, 0, t_all);
 }
@@ -519,6 +554,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   __shared__ __align__(8) uint64_t bars[3][kMaxStages];  // full, split, empty
   __shared__ __align__(8) uint64_t accbars[2][2];        // acc done, acc free
   __shared__ __align__(8) uint64_t drainbars[kTcMmaWarps];
+  __shared__ __align__(8) uint64_t xbars[2][2];          // exchange full, exchange free
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   const Task task = p.tasks[blockIdx.x];
@@ -530,7 +566,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   if (threadIdx.x == 32) {
     if (p.timing) p.timing[2 * blockIdx.x] = global_ns();
     for (int s = 0; s < task.stages; ++s) {
-      mbar_init(smem_addr(&bars[0][s]), 32u);  // one cp.async arrival per feeder lane
+      mbar_init(smem_addr(&bars[0][s]), 1u);  // TMA: one arrival + transaction bytes
       mbar_init(smem_addr(&bars[1][s]), 1u);  // the split warp
       mbar_init(smem_addr(&bars[2][s]), 1u);  // the MMA warp's tcgen05.commit
     }
@@ -539,6 +575,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
       mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcSplitWarps));
     }
     for (int i = 0; i < kTcMmaWarps; ++i) mbar_init(smem_addr(&drainbars[i]), 1u);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&xbars[0][i]), 1u);
+      mbar_init(smem_addr(&xbars[1][i]), 1u);
+    }
     abort_flag = 0;
     mbar_fence_init();
   }
@@ -553,6 +593,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   cb.acc0 = smem_addr(&accbars[0][0]);
   cb.accfree0 = smem_addr(&accbars[1][0]);
   cb.drain0 = smem_addr(&drainbars[0]);
+  cb.xfull0 = smem_addr(&xbars[0][0]);
+  cb.xfree0 = smem_addr(&xbars[1][0]);
   if (warp < kTcSplitWarps)
     tc_split_warp<CHECK>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < kTcSplitWarps + kTcMmaWarps)
