@@ -185,7 +185,8 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
                                       vbsr_stream_t stream, uint64_t* cta_times,
                                       int cta_times_len);
 
-/* Plan::launch_count (plan.cpp:23-31): kernel launches per execute (always 1 here). */
+/* Plan::launch_count (plan.cpp:23-31): kernel launches per execute (2 here: the B pre-pass and
+ * the SpMM kernel). */
 vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out);
 
 /* Reads and clears the plan's device status word (no reference counterpart): synchronises

@@ -1,7 +1,6 @@
 // vbsr_device.cu — device side of the engine: the owning device format (Matrix), the planner
 // (Plan), the execute path and the C-ABI entry points that touch a GPU.
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -156,39 +155,6 @@ __global__ void rowwise_direct_kernel(vbsr_device_matrix a, const float* __restr
     for (int j = 0; j < 8; ++j)
       C[a.row_scalar_off[row] + r + (long long)(n0 + j) * a.scalar_rows] = acc[j];
   }
-}
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
-// B (K x rhs, column-major, ld K) as a 2-D tensor with an 8-column x rhs-row box, written to shared
-// memory with the 32-byte swizzle: rhs rows of 32 bytes, the K-major operand layout of tcgen05.mma.
-vbsr_status encode_b_map(CUtensorMap* map, const float* B, int64_t K, int rhs) {
-  auto enc = tensor_map_encoder();
-  if (enc == nullptr) return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rhs)};
-  const cuuint64_t strides[1] = {cuuint64_t(K) * sizeof(float)};
-  const cuuint32_t box[2] = {8u, cuuint32_t(rhs)};
-  const cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(VBSR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
-  return VBSR_OK;
 }
 
 bool valid_rhs(int rhs) { return rhs == 8 || rhs == 16 || rhs == 32 || rhs == 64; }
@@ -368,6 +334,8 @@ struct vbsr_plan {
   int64_t stream_entries = 0;
   StageDesc* d_stream = nullptr;
   ItemDesc* d_items = nullptr;
+  float* d_bstack = nullptr;     // B's operand stacks, rewritten by every execute
+  int64_t bstack_floats = 0;
   Task* d_tasks = nullptr;
   int* d_status = nullptr;
   unsigned long long* d_timing = nullptr;  // allocated on first request
@@ -450,7 +418,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   // feeder, one split warp and one MMA warp, which pass through its uses in order, so a wait never
   // meets a phase of another use.
   const int stages =
-      std::min(kMaxStages, (kSmemBudget - kXchgBytes) / (slot * 4)) / kTcSplitWarps * kTcSplitWarps;
+      std::min(kMaxStages, kSmemBudget / (slot * 4)) / kTcSplitWarps * kTcSplitWarps;
   if (stages < kTcSplitWarps) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
   const uint64_t nwc = uint64_t(stage::nw_code(rhs));
   for (int t = 0; t < ctas; ++t) {
@@ -514,7 +482,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
-  p->smem_bytes = stages * slot * 4 + kXchgBytes + 1024;
+  p->smem_bytes = stages * slot * 4 + 1024;
   p->num_tasks = int(h_tasks.size());
   p->stream_entries = int64_t(stream.size());
 
@@ -528,6 +496,9 @@ vbsr_status build_schedule(vbsr_plan* p) {
   DeviceGuard guard(d.device);
   VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
+  // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
+  p->bstack_floats = (d.K / 8) * int64_t(stack_m(rhs)) * 8;
+  VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
   if (!items.empty())
     VBSR_CUDA(cudaMemcpy(p->d_items, items.data(), items.size() * sizeof(ItemDesc),
                          cudaMemcpyHostToDevice));
@@ -549,25 +520,31 @@ void free_plan(vbsr_plan* p) {
   DeviceGuard guard(p->device);
   cudaFree(p->d_stream);
   cudaFree(p->d_items);
+  cudaFree(p->d_bstack);
   cudaFree(p->d_tasks);
   cudaFree(p->d_status);
   cudaFree(p->d_timing);
   delete p;
 }
 
+// One execute: the B pre-pass, then the SpMM kernel, both on `stream`.
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
+  const int64_t pieces = p->bstack_floats / 4;
+  if (pieces > 0) {
+    const int64_t blocks = std::min<int64_t>((pieces + 255) / 256, 148 * 32);
+    bstack_kernel<<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, kp.rhs, p->d_bstack);
+  }
   if (p->flags & VBSR_PLAN_BOUNDS_CHECK)
     spmm_tc_kernel<true><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
   else
     spmm_tc_kernel<false><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
 }
 
-// Launch parameters of one execute: the plan's schedule, the caller's B and C, and B's tensor map.
+// Launch parameters of one execute: the plan's schedule and the caller's B and C.
 vbsr_status fill_params(const vbsr_plan* p, const float* B, float* C, int* status,
                         unsigned long long* timing, KernelParams* kp) {
   const MatrixData& d = p->m->d;
-  vbsr_status st = encode_b_map(&kp->b_map, B, d.K, p->rhs);
-  if (st != VBSR_OK) return st;
+  kp->bstack = p->d_bstack;
   kp->stages = p->d_stream;
   kp->items = p->d_items;
   kp->tasks = p->d_tasks;
@@ -826,7 +803,7 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
 vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out) {
   clear_error();
   if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
-  *out = 1;
+  *out = 2;  // the B pre-pass and the SpMM kernel
   return VBSR_OK;
 }
 

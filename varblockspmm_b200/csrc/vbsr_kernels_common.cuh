@@ -14,12 +14,12 @@ namespace vbsr_b200 {
 typedef unsigned long long u64;
 
 struct KernelParams {
-  CUtensorMap b_map;    // B (K x rhs, column-major) as a 2-D tensor, box 8 columns x rhs rows
   const StageDesc* stages;  // stage descriptors of all CTAs
   const ItemDesc* items;    // item descriptors of all CTAs
   const Task* tasks;
   const float* values;  // device-format values
   const float* B;
+  const float* bstack;  // B's operand stacks (bstack_kernel), M x 8 floats per 8-column group
   float* C;
   long long M, K, nvalues;
   int rhs;

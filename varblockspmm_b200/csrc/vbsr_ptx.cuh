@@ -1,6 +1,6 @@
 // vbsr_ptx.cuh — thin inline-PTX wrappers for the sm_100a features the kernels use: mbarriers,
-// TMA copies (1-D cp.async.bulk, 2-D cp.async.bulk.tensor) with L2 cache hints, 16-byte cp.async
-// copies, and 16-byte shared-memory accesses. Hand-written; no library code.
+// 1-D TMA bulk copies (cp.async.bulk) with L2 cache hints, 16-byte cp.async copies, and 16-byte
+// shared-memory accesses. Hand-written; no library code.
 #pragma once
 #include <cstdint>
 
@@ -120,15 +120,5 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 
 
 
-// 2-D tensor TMA load (box from a tensor map) into shared memory, completion on `bar`.
-// x must be a multiple of 4 for 32-bit elements (16-byte aligned start).
-__device__ __forceinline__ void tensor2d_g2s(uint32_t dst, const void* tmap, int x, int y,
-                                             uint32_t bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
-      : "memory");
-}
 
 }  // namespace vbsr_b200

@@ -12,21 +12,25 @@
 // A_lo. One MMA therefore produces all four products B_hi*A_hi, B_lo*A_hi, B_hi*A_lo, B_lo*A_lo
 // (the last one is below the tolerance but harmless), and the epilogue adds, for every C element,
 // the two S rows of its column at the two D columns of its row. M = 64 for nw <= 32 and M = 128
-// for nw = 64; N = 2h <= 128. S holds raw B in rows 0..nw-1 (one TMA box) and B_lo M/2 rows
-// further; in TMEM (M = 64: row r lives in lane r % 16 of quadrant r / 16; M = 128: lane r % 32 of
-// quadrant r / 32) hi and lo of a column therefore sit in the same lane of quadrants q and q + 2,
-// and the epilogue adds them through a small shared-memory exchange between those two warps.
+// for nw = 64; N = 2h <= 128.
+//
+// The stacks of all 8-column groups of B are formed once per execute by a small pre-pass
+// (bstack_kernel) in global memory, already in the MMA's K-major, 32-byte-swizzled layout, so a
+// group's S arrives with one contiguous bulk copy. S is built per quadrant q (32 TMEM lanes, the
+// part of the accumulator one warp may read): with half = M / 8 columns per quadrant, S rows
+// 2*half*q + j and 2*half*q + half + j hold hi and lo of column c = half*q + j, and in TMEM (M = 64:
+// row r lives in lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of
+// quadrant q, so a warp adds them with one shuffle.
 //
 // CTA = eight warps, one CTA per SM:
 //   warps 0..3  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4, which
-//               forms A_lo next to each group's A and B_lo in the stack's lo rows, fences the
-//               writes for the async proxy and hands the slot to the MMA warp; they also store
-//               each item's result one item later (warp q reads TMEM quadrant q);
+//               forms A_lo next to each group's A, fences the writes for the async proxy and hands
+//               the slot to the MMA warp; they also store each item's result one item later (warp
+//               q reads TMEM quadrant q);
 //   warps 4, 5  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 6, 7  feeders: stage k is copied by feeder k % 2 with two TMA operations per group (one
-//               cp.async.bulk for the group's A, one 2-D cp.async.bulk.tensor box of 8 columns x nw
-//               rows of B onto the stack's hi rows).
+//   warps 6, 7  feeders: stage k is copied by feeder k % 2 with two cp.async.bulk copies per
+//               group (the group's A and its stack S).
 // A single wait-and-release round on an mbarrier costs a warp ~200 cycles even when the barrier
 // has already completed, which is why every role is spread over several warps. The ring has D
 // slots, D a multiple of 4, stage k uses slot k % D: each slot then has one feeder, one split
@@ -57,10 +61,8 @@ __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 __host__ __device__ constexpr int stage_groups(int rhs) { return rhs > 32 ? 3 : 4; }
 // Slot layout (floats), G = groups per stage: group g's N-side operand at 1024 g (h rows of raw A,
 // 8 floats each, followed by the h rows of A_lo), then the operand stacks of the groups (M x 8
-// each: raw B in rows 0..nw-1, B_lo in rows M/2..M/2+nw-1) from 1024 G.
+// each) from 1024 G.
 __host__ __device__ constexpr int slot_stack(int G) { return 1024 * G; }
-// Epilogue exchange after the ring: per hi/lo warp pair, 32 lanes x 64 floats.
-constexpr int kXchgBytes = 2 * 32 * 64 * 4;
 __host__ __device__ constexpr int slot_floats(int rhs) {
   return slot_stack(stage_groups(rhs)) + stage_groups(rhs) * stack_m(rhs) * 8;
 }
@@ -155,7 +157,6 @@ struct CtaBars {
   uint32_t split0;          // per slot: lo parts written
   uint32_t empty0;          // per slot: the stage's MMAs have read the slot
   uint32_t acc0, accfree0;  // per accumulator buffer: MMAs of the item done / D read by all warps
-  uint32_t xfull0, xfree0;  // per warp pair: lo sums written / read
   uint32_t drain0;          // per MMA warp: end-of-kernel drain of its MMAs
 };
 
@@ -202,7 +203,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     const long long a0 = st.a_start();
     bool ok = true;
     if (CHECK) {
-      ok = a0 + 8ll * h * groups <= p.nvalues && n0 + nw <= p.rhs && nw == p.rhs &&
+      ok = a0 + 8ll * h * groups <= p.nvalues && n0 == 0 && nw == p.rhs &&
            8 * groups <= task.stage_cols;
       for (int g = 0; g < groups; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
     }
@@ -216,16 +217,18 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     } else {
       const uint32_t sp = slots + 4u * uint32_t(s * SF);
       const int M = stack_m(nw);
-      if (lane == 0) mbar_arrive_expect_tx(full_bar, uint32_t(groups * 32 * (h + nw)));
+      if (lane == 0) mbar_arrive_expect_tx(full_bar, uint32_t(groups * 32 * (h + M)));
       __syncwarp();
       if (lane < groups) {
         // group `lane`: h rows x 8 floats, contiguous in the device format
         bulk_g2s(sp + 4096u * lane, p.values + a0 + 8ll * h * lane, uint32_t(32 * h), full_bar,
                  pol_a);
       } else if (lane < 2 * groups) {
+        // group g's stack: M rows x 32 bytes of the pre-pass output for 8-column group col/8
         const int g = lane - groups;
-        tensor2d_g2s(sp + 4u * uint32_t(slot_stack(G) + g * M * 8), &p.b_map, st.group_col(g), n0,
-                     full_bar, pol_b);
+        bulk_g2s(sp + 4u * uint32_t(slot_stack(G) + g * M * 8),
+                 p.bstack + (long long)(st.group_col(g) >> 3) * (M * 8), uint32_t(M * 32), full_bar,
+                 pol_b);
       }
       filled |= 1u << s;
       lastpar = (lastpar & ~(1u << s)) | (ph << s);
@@ -249,45 +252,33 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   }
 }
 
-// Epilogue of item j: D -> C, by split warp w (TMEM quadrant w). Partial i (128 columns after
+// Epilogue of one item: D -> C, by split warp w (TMEM quadrant w). Partial i (128 columns after
 // partial 0) holds the stages issued by MMA warp i; only partials that received a stage are read.
 // Within a partial, column r is row r of the tile from raw A and column h + r the same row from
-// A_lo. With rq = M/4 stack rows per quadrant, lane l of quadrant w < 2 holds the hi part of RHS
-// column c = rq*w + l and the same lane of quadrant w + 2 its lo part: the lo warp writes its sums
-// to the pair's exchange buffer, the hi warp adds them and stores h consecutive floats of column
-// n0 + c.
+// A_lo. Lane j < half of quadrant w holds hi of RHS column n0 + half*w + j, lane half + j its lo.
 template <bool CHECK>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars& cb, int buf,
                                             uint32_t parity, uint32_t tmem_buf, int w, int lane,
-                                            const Item& it, int j, uint32_t xbuf,
-                                            volatile int* abort_flag) {
+                                            const Item& it, volatile int* abort_flag) {
   VBSR_PROF_T0(t_w);
   if (!wait_phase(cb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
   VBSR_PROF_ADD(p, 4, t_w);
   tc_fence_after();
   const int h = it.h(), nw = it.nw(), n0 = it.n0();
-  const int rq = stack_m(nw) / 4, hq = (nw + rq - 1) / rq;
+  const int half = stack_m(nw) / 8, quads = nw / half;
   uint32_t use = 0;
   if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
     if (it.n >= 2) use = 3u;
     else if (it.n == 1) use = 1u << (it.k0 & 1);
   }
-  const int pr = w & 1;
-  const bool hi = w < hq, lo = w >= 2 && pr < hq;
-  if (hi || lo) {
+  if (w < quads) {
     const uint32_t taddr = tmem_buf + (uint32_t(32 * w) << 16);
-    const uint32_t xb = xbuf + uint32_t(pr * 32 * 64 * 4 + lane * 64 * 4);
-    if (lo && j >= 1 &&
-        !wait_phase(cb.xfree0 + 8u * pr, uint32_t((j - 1) & 1), p, abort_flag, lane))
-      return false;
-    if (hi && !wait_phase(cb.xfull0 + 8u * pr, uint32_t(j & 1), p, abort_flag, lane))
-      return false;
-    const int c = rq * w + lane;  // hi warps: RHS column within the tile
-    const bool store = hi && lane < rq && c < nw &&
+    const bool store = lane < half &&
                        !(CHECK && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs));
-    if (CHECK && hi && w == 0 && lane == 0 && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs))
+    if (CHECK && w == 0 && lane == 0 && ((long long)it.c_row + h > p.M || n0 + nw > p.rhs))
       record_status(p.status, VBSR_BOUNDS_VIOLATION, int(it.c_row));
-    float4* dst = reinterpret_cast<float4*>(p.C + (long long)(n0 + c) * p.M + it.c_row);
+    const int col = n0 + half * w + lane;
+    float4* dst = reinterpret_cast<float4*>(p.C + (long long)col * p.M + it.c_row);
     // passes of 16 tile rows: 2 partials x 2 halves (A, A_lo) x 16 values in flight per pass
     for (int c0 = 0; c0 < h; c0 += 16) {
       const bool two = c0 + 8 < h;
@@ -311,37 +302,17 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
         float a = 0.0f;
         if (use & 1u) a += v[0][e] + v[1][e];
         if (use & 2u) a += v[2][e] + v[3][e];
-        r[e] = a;
+        r[e] = a + __shfl_down_sync(0xffffffffu, a, half);
       }
-      const uint32_t xa = xb + 4u * uint32_t(c0);
-      if (lo) {
-        sts128(xa, make_float4(r[0], r[1], r[2], r[3]));
-        sts128(xa + 16u, make_float4(r[4], r[5], r[6], r[7]));
+      if (store) {
+        dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
+        dst[c0 / 4 + 1] = make_float4(r[4], r[5], r[6], r[7]);
         if (two) {
-          sts128(xa + 32u, make_float4(r[8], r[9], r[10], r[11]));
-          sts128(xa + 48u, make_float4(r[12], r[13], r[14], r[15]));
-        }
-      } else {
-        const float4 x0 = lds128(xa), x1 = lds128(xa + 16u);
-        r[0] += x0.x; r[1] += x0.y; r[2] += x0.z; r[3] += x0.w;
-        r[4] += x1.x; r[5] += x1.y; r[6] += x1.z; r[7] += x1.w;
-        if (two) {
-          const float4 x2 = lds128(xa + 32u), x3 = lds128(xa + 48u);
-          r[8] += x2.x; r[9] += x2.y; r[10] += x2.z; r[11] += x2.w;
-          r[12] += x3.x; r[13] += x3.y; r[14] += x3.z; r[15] += x3.w;
-        }
-        if (store) {
-          dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
-          dst[c0 / 4 + 1] = make_float4(r[4], r[5], r[6], r[7]);
-          if (two) {
-            dst[c0 / 4 + 2] = make_float4(r[8], r[9], r[10], r[11]);
-            dst[c0 / 4 + 3] = make_float4(r[12], r[13], r[14], r[15]);
-          }
+          dst[c0 / 4 + 2] = make_float4(r[8], r[9], r[10], r[11]);
+          dst[c0 / 4 + 3] = make_float4(r[12], r[13], r[14], r[15]);
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(lo ? cb.xfull0 + 8u * pr : cb.xfree0 + 8u * pr);
   }
   tc_fence_before();
   __syncwarp();
@@ -349,49 +320,26 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   return true;
 }
 
-// lo parts of a whole stage at shared address sp: A_lo after each group's A (2h float4s per group)
-// and B_lo into the stacks' lo rows (M/2 rows after the hi rows). Eight independent loads per lane are in flight before the
-// stores.
-__device__ __forceinline__ void split_stage(uint32_t sp, int G, int groups, int h, int nw, int lane) {
-  {
-    // A: group g's A at byte 4096 g (2h float4s), its A_lo right after it
-    const int run = 2 * h, na = run * groups;
-    for (int i0 = 0; i0 < na; i0 += 256) {
-      float4 x[8];
-      uint32_t o[8];
+// A_lo of a whole stage at shared address sp: group g's A (2h float4s) at byte 4096 g, its A_lo
+// right after it. Per group, lane l handles float4s l, l + 32, ...; all loads of the stage are in
+// flight before the stores.
+__device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane) {
+  const int run = 2 * h;  // <= 128 float4s per group: at most 4 per lane
+  float4 x[4][4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + 32 * u + lane;
-        const int g = i >= run ? (i >= 2 * run ? (i >= 3 * run ? 3 : 2) : 1) : 0;
-        o[u] = sp + 4096u * g + 16u * uint32_t(i - g * run);
-        if (i < na) x[u] = lds128(o[u]);
-      }
+  for (int g = 0; g < 4; ++g) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + 32 * u + lane;
-        if (i < na) sts128(o[u] + 32u * h, lo_part4(x[u]));
-      }
+    for (int u = 0; u < 4; ++u) {
+      const int i = 32 * u + lane;
+      if (g < groups && i < run) x[g][u] = lds128(sp + 4096u * g + 16u * i);
     }
   }
-  // B: per group the hi rows 0..nw-1 (2nw float4s, contiguous); the lo rows M/2 rows further
-  const int M = stack_m(nw);
-  const uint32_t stk = sp + 4u * uint32_t(slot_stack(G));
-  const int lg_run = __ffs(2 * nw) - 1;
-  const int nb = (2 * nw) * groups;
-  for (int i0 = 0; i0 < nb; i0 += 256) {
-    float4 x[8];
-    uint32_t o[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + 32 * u + lane;
-      const int g = i >> lg_run, r = i & ((1 << lg_run) - 1);
-      o[u] = stk + uint32_t(g * M * 32 + 16 * r);
-      if (i < nb) x[u] = lds128(o[u]);
-    }
+  for (int g = 0; g < 4; ++g) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + 32 * u + lane;
-      if (i < nb) sts128(o[u] + 16u * M, lo_part4(x[u]));
+    for (int u = 0; u < 4; ++u) {
+      const int i = 32 * u + lane;
+      if (g < groups && i < run) sts128(sp + 4096u * g + 16u * (i + run), lo_part4(x[g][u]));
     }
   }
 }
@@ -402,7 +350,7 @@ template <bool CHECK>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
-  const int D = task.stages, SF = task.stage_floats, G = task.stage_cols >> 3;
+  const int D = task.stages, SF = task.stage_floats;
   const int nst = task.stage_end - task.stage_off;
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
@@ -413,7 +361,6 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   uint32_t mph = 0;
   int j = 0;       // items done
   Item prev{};
-  const uint32_t xbuf = slots + 4u * uint32_t(D * SF);
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
   bool ok = true;
   VBSR_PROF_T0(t_all);
@@ -438,7 +385,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       VBSR_PROF_ADD(p, 1, t_w);
       VBSR_PROF_T0(t_s);
       if (math) {
-        split_stage(slots + 4u * uint32_t(s * SF), G, cols >> 3, h, nw, lane);
+        split_stage(slots + 4u * uint32_t(s * SF), cols >> 3, h, lane);
         fence_proxy_async_smem();
       }
       __syncwarp();
@@ -450,8 +397,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       const int pj = j - 1;
       VBSR_PROF_T0(t_e);
       if (!tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1),
-                              tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, pj, xbuf,
-                              abort_flag)) {
+                              tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, abort_flag)) {
         ok = false;
         break;
       }
@@ -463,7 +409,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   if (ok && j > 0) {
     const int pj = j - 1;
     tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1), tmem_base + uint32_t(256 * (pj & 1)),
-                       w, lane, prev, pj, xbuf, abort_flag);
+                       w, lane, prev, abort_flag);
   }
   VBSR_PROF_ADD(p, 0, t_all);
 }
@@ -547,6 +493,34 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
   }
 }
 
+// Pre-pass: the operand stacks S of all 8-column groups of B (K x rhs, column-major), one tile of
+// M rows x 8 floats per group (kg = k / 8) in the layout the MMA reads: row 2*half*q + j holds the
+// 8 values of RHS column c = half*q + j (raw, i.e. hi), row 2*half*q + half + j their lo parts,
+// rows of columns >= rhs are zero, and the two 16-byte halves of row r are exchanged when bit 2 of
+// r is set (32-byte swizzle). One thread per 16-byte piece; the two pieces of a row read one
+// 32-byte sector of B.
+__global__ void bstack_kernel(const float* __restrict__ B, long long K, int rhs, float* __restrict__ out) {
+  const int M = stack_m(rhs), half = M / 8;
+  const int lg_m2 = M == 128 ? 8 : 7, lg_half = M == 128 ? 4 : 3;
+  const long long total = (K >> 3) << lg_m2;  // (K / 8) tiles x 2M pieces
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long kg = e >> lg_m2;
+    const int rem = int(e & ((1 << lg_m2) - 1));
+    const int row = rem >> 1, up = rem & 1;
+    const int q = row >> (lg_half + 1), jj = row & (2 * half - 1);
+    const bool is_lo = jj >= half;
+    const int c = (q << lg_half) + (jj & (half - 1));
+    const int u = up ^ ((row >> 2) & 1);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < rhs) {
+      v = __ldg(reinterpret_cast<const float4*>(B + (long long)c * K + 8 * kg + 4 * u));
+      if (is_lo) v = lo_part4(v);
+    }
+    reinterpret_cast<float4*>(out)[e] = v;
+  }
+}
+
 template <bool CHECK>
 __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -554,7 +528,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   __shared__ __align__(8) uint64_t bars[3][kMaxStages];  // full, split, empty
   __shared__ __align__(8) uint64_t accbars[2][2];        // acc done, acc free
   __shared__ __align__(8) uint64_t drainbars[kTcMmaWarps];
-  __shared__ __align__(8) uint64_t xbars[2][2];          // exchange full, exchange free
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   const Task task = p.tasks[blockIdx.x];
@@ -575,10 +548,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
       mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcSplitWarps));
     }
     for (int i = 0; i < kTcMmaWarps; ++i) mbar_init(smem_addr(&drainbars[i]), 1u);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_addr(&xbars[0][i]), 1u);
-      mbar_init(smem_addr(&xbars[1][i]), 1u);
-    }
+
     abort_flag = 0;
     mbar_fence_init();
   }
@@ -593,8 +563,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   cb.acc0 = smem_addr(&accbars[0][0]);
   cb.accfree0 = smem_addr(&accbars[1][0]);
   cb.drain0 = smem_addr(&drainbars[0]);
-  cb.xfull0 = smem_addr(&xbars[0][0]);
-  cb.xfree0 = smem_addr(&xbars[1][0]);
+
   if (warp < kTcSplitWarps)
     tc_split_warp<CHECK>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < kTcSplitWarps + kTcMmaWarps)
