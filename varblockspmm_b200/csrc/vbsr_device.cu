@@ -498,6 +498,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
   // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
   p->bstack_floats = (d.K / 8) * int64_t(stack_m(rhs)) * 8;
+  if (p->bstack_floats / 4 >= (int64_t(1) << 31))
+    return set_error(VBSR_INVALID_ARGUMENT, "B too large for the pre-pass index range");
   VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
   if (!items.empty())
     VBSR_CUDA(cudaMemcpy(p->d_items, items.data(), items.size() * sizeof(ItemDesc),

@@ -321,26 +321,20 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
 }
 
 // A_lo of a whole stage at shared address sp: group g's A (2h float4s) at byte 4096 g, its A_lo
-// right after it. Per group, lane l handles float4s l, l + 32, ...; all loads of the stage are in
-// flight before the stores.
+// right after it. Lane l handles float4s l, l + 32, ... of each group; a group's four loads are in
+// flight before its stores.
 __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane) {
   const int run = 2 * h;  // <= 128 float4s per group: at most 4 per lane
-  float4 x[4][4];
+  const uint32_t base = sp + 16u * lane, lo_off = 32u * h;
+  for (int g = 0; g < groups; ++g) {
+    const uint32_t a = base + 4096u * g;
+    float4 x[4];
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
+    for (int u = 0; u < 4; ++u)
+      if (32 * u + lane < run) x[u] = lds128(a + 512u * u);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = 32 * u + lane;
-      if (g < groups && i < run) x[g][u] = lds128(sp + 4096u * g + 16u * i);
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int i = 32 * u + lane;
-      if (g < groups && i < run) sts128(sp + 4096u * g + 16u * (i + run), lo_part4(x[g][u]));
-    }
+    for (int u = 0; u < 4; ++u)
+      if (32 * u + lane < run) sts128(a + lo_off + 512u * u, lo_part4(x[u]));
   }
 }
 
@@ -463,6 +457,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
         break;
       }
       VBSR_PROF_ADD(p, 3, t_w);
+      VBSR_PROF_T0(t_i);
       if (lane == 0) {
         if (math) {
           tc_fence_after();
@@ -476,6 +471,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
         tc_commit(cb.empty0 + 8u * s);  // the slot is free once these MMAs have read it
       }
       __syncwarp();
+      VBSR_PROF_ADD(p, 10, t_i);
     }
     if (!ok) break;
     if (lane == 0) tc_commit(cb.acc0 + 8u * buf);  // this warp's part of the item is issued
@@ -502,20 +498,18 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 __global__ void bstack_kernel(const float* __restrict__ B, long long K, int rhs, float* __restrict__ out) {
   const int M = stack_m(rhs), half = M / 8;
   const int lg_m2 = M == 128 ? 8 : 7, lg_half = M == 128 ? 4 : 3;
-  const long long total = (K >> 3) << lg_m2;  // (K / 8) tiles x 2M pieces
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long kg = e >> lg_m2;
-    const int rem = int(e & ((1 << lg_m2) - 1));
-    const int row = rem >> 1, up = rem & 1;
+  const int total = int(K >> 3) << lg_m2;  // (K / 8) tiles x 2M pieces
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int kg = e >> lg_m2;
+    const int rem = e & ((1 << lg_m2) - 1);
+    const int row = rem >> 1;
     const int q = row >> (lg_half + 1), jj = row & (2 * half - 1);
-    const bool is_lo = jj >= half;
     const int c = (q << lg_half) + (jj & (half - 1));
-    const int u = up ^ ((row >> 2) & 1);
+    const int u = (rem & 1) ^ ((row >> 2) & 1);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (c < rhs) {
       v = __ldg(reinterpret_cast<const float4*>(B + (long long)c * K + 8 * kg + 4 * u));
-      if (is_lo) v = lo_part4(v);
+      if (jj >= half) v = lo_part4(v);
     }
     reinterpret_cast<float4*>(out)[e] = v;
   }
