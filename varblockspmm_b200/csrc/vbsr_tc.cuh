@@ -22,14 +22,14 @@
 // row r lives in lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of
 // quadrant q, so a warp adds them with one shuffle.
 //
-// CTA = eight warps, one CTA per SM:
+// CTA = ten warps, one CTA per SM:
 //   warps 0..3  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4, which
 //               forms A_lo next to each group's A, fences the writes for the async proxy and hands
 //               the slot to the MMA warp; they also store each item's result one item later (warp
 //               q reads TMEM quadrant q);
 //   warps 4, 5  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 6, 7  feeders: stage k is copied by feeder k % 2 with two cp.async.bulk copies per
+//   warps 6..9  feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
 //               group (the group's A and its stack S).
 // A single wait-and-release round on an mbarrier costs a warp ~200 cycles even when the barrier
 // has already completed, which is why every role is spread over several warps. The ring has D
@@ -52,7 +52,7 @@ namespace vbsr_b200 {
 
 constexpr int kTcSplitWarps = 4;            // split / epilogue warps (one per TMEM quadrant)
 constexpr int kTcMmaWarps = 2;              // MMA-issuing warps
-constexpr int kTcFeeders = 2;               // feeder warps
+constexpr int kTcFeeders = 4;               // feeder warps
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
