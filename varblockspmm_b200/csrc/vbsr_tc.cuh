@@ -22,18 +22,18 @@
 // row r lives in lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of
 // quadrant q, so a warp adds them with one shuffle.
 //
-// CTA = ten warps, one CTA per SM:
-//   warps 0..3  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4, which
+// CTA = fourteen warps, one CTA per SM:
+//   warps 0..7  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 8, which
 //               forms A_lo next to each group's A, fences the writes for the async proxy and hands
-//               the slot to the MMA warp; they also store each item's result one item later (warp
-//               q reads TMEM quadrant q);
-//   warps 4, 5  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
+//               the slot to the MMA warp; warps 0..3 store the results of even items, warps 4..7
+//               those of odd items, one item later (warp w reads TMEM quadrant w % 4);
+//   warps 8, 9  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 6..9  feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
+//   warps 10..13 feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
 //               group (the group's A and its stack S).
 // A single wait-and-release round on an mbarrier costs a warp ~200 cycles even when the barrier
 // has already completed, which is why every role is spread over several warps. The ring has D
-// slots, D a multiple of 4, stage k uses slot k % D: each slot then has one feeder, one split
+// slots, D a multiple of 8, stage k uses slot k % D: each slot then has one feeder, one split
 // warp and one MMA warp, all passing through its uses in order. Every warp walks the CTA's list of
 // stage descriptors (compiled by the planner; vbsr_internal.h). Every wait is bounded (see
 // wait_phase); after an abort the feeders wait for their copies and the MMA warps for their MMAs
@@ -50,7 +50,8 @@
 
 namespace vbsr_b200 {
 
-constexpr int kTcSplitWarps = 4;            // split / epilogue warps (one per TMEM quadrant)
+constexpr int kTcSplitWarps = 8;            // split warps (warp w reads TMEM quadrant w % 4)
+constexpr int kTcEpiWarps = 4;              // split warps storing one item (one per quadrant)
 constexpr int kTcMmaWarps = 2;              // MMA-issuing warps
 constexpr int kTcFeeders = 4;               // feeder warps
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
@@ -279,26 +280,21 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
       record_status(p.status, VBSR_BOUNDS_VIOLATION, int(it.c_row));
     const int col = n0 + half * w + lane;
     float4* dst = reinterpret_cast<float4*>(p.C + (long long)col * p.M + it.c_row);
-    // passes of 16 tile rows: 2 partials x 2 halves (A, A_lo) x 16 values in flight per pass
-    for (int c0 = 0; c0 < h; c0 += 16) {
-      const bool two = c0 + 8 < h;
-      float v[4][16];
+    // passes of 8 tile rows: 2 partials x 2 halves (A, A_lo) x 8 values in flight per pass
+    for (int c0 = 0; c0 < h; c0 += 8) {
+      float v[4][8];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         if (use & (1u << i)) {
           const uint32_t t0 = taddr + uint32_t(128 * i + c0);
           tc_ld8_nowait(t0, v[2 * i]);
           tc_ld8_nowait(t0 + uint32_t(h), v[2 * i + 1]);
-          if (two) {
-            tc_ld8_nowait(t0 + 8u, v[2 * i] + 8);
-            tc_ld8_nowait(t0 + uint32_t(h) + 8u, v[2 * i + 1] + 8);
-          }
         }
       }
       tc_wait_ld();
-      float r[16];
+      float r[8];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
+      for (int e = 0; e < 8; ++e) {
         float a = 0.0f;
         if (use & 1u) a += v[0][e] + v[1][e];
         if (use & 2u) a += v[2][e] + v[3][e];
@@ -307,10 +303,6 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
       if (store) {
         dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
         dst[c0 / 4 + 1] = make_float4(r[4], r[5], r[6], r[7]);
-        if (two) {
-          dst[c0 / 4 + 2] = make_float4(r[8], r[9], r[10], r[11]);
-          dst[c0 / 4 + 3] = make_float4(r[12], r[13], r[14], r[15]);
-        }
       }
     }
   }
@@ -338,8 +330,9 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int 
   }
 }
 
-// Split warp w (0..3): forms the lo parts of the stages k with k % 4 == w and stores each item's
-// result (TMEM quadrant w) one item later.
+// Split warp w (0..7): forms the lo parts of the stages k with k % 8 == w, and stores the results of
+// the items j with j % 2 == w / 4 (TMEM quadrant w % 4) one item later; buffer j % 2 is therefore
+// always read by the same four warps.
 template <bool CHECK>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
@@ -351,9 +344,10 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   StageWin sw;
   sw.init(p.stages + task.stage_off, w, kTcSplitWarps, nst, lane);
   int kk = w;      // this warp's next stage
-  int ms = w;      // its slot (this warp's slots are w, w + 4, ...)
+  int ms = w;      // its slot (this warp's slots are w, w + 8, ...)
   uint32_t mph = 0;
   int j = 0;       // items done
+  const int grp = w >> 2, q = w & 3;
   Item prev{};
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
   bool ok = true;
@@ -387,11 +381,11 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       VBSR_PROF_ADD(p, 2, t_s);
     }
     if (!ok) break;
-    if (j > 0) {
+    if (j > 0 && ((j - 1) & 1) == grp) {
       const int pj = j - 1;
       VBSR_PROF_T0(t_e);
       if (!tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1),
-                              tmem_base + uint32_t(256 * (pj & 1)), w, lane, prev, abort_flag)) {
+                              tmem_base + uint32_t(256 * (pj & 1)), q, lane, prev, abort_flag)) {
         ok = false;
         break;
       }
@@ -400,10 +394,10 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
     prev = it;
     ++j;
   }
-  if (ok && j > 0) {
+  if (ok && j > 0 && ((j - 1) & 1) == grp) {
     const int pj = j - 1;
     tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1), tmem_base + uint32_t(256 * (pj & 1)),
-                       w, lane, prev, abort_flag);
+                       q, lane, prev, abort_flag);
   }
   VBSR_PROF_ADD(p, 0, t_all);
 }
@@ -539,7 +533,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_addr(&accbars[0][b]), uint32_t(kTcMmaWarps));
-      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcSplitWarps));
+      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcEpiWarps));
     }
     for (int i = 0; i < kTcMmaWarps; ++i) mbar_init(smem_addr(&drainbars[i]), 1u);
 
