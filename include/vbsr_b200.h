@@ -146,11 +146,14 @@ enum { VBSR_KERNEL_AUTO = 0, VBSR_KERNEL_ROW_OWNED = 1, VBSR_KERNEL_SPLIT_ROW = 
 /* Plan flags (no reference counterpart). */
 enum {
   VBSR_PLAN_BOUNDS_CHECK = 1u << 0, /* use the bounds-checked kernel build                  */
-  VBSR_PLAN_NO_SPLIT = 1u << 1,     /* never split heavy block rows into column halves      */
-  VBSR_PLAN_NARROW_STAGES = 1u << 2, /* pipeline stages of 32 block columns (default: up to 64) */
+  VBSR_PLAN_NO_SPLIT = 1u << 1,     /* accepted for compatibility; no effect (no row splits) */
+  VBSR_PLAN_NARROW_STAGES = 1u << 2, /* accepted for compatibility; no effect               */
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
-  VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9    /* consumers wait for the data but compute nothing     */
+  VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9,   /* consumers wait for the data but compute nothing     */
+  /* Timing only: skip the B pre-pass and reuse the operand stacks the previous execute of this
+   * plan formed; C is correct only if B is unchanged since then. */
+  VBSR_PLAN_DIAG_SKIP_PREPASS = 1u << 10
 };
 
 /* Plan::Plan (plan.cpp:5-18): rhs must be 8, 16, 32 or 64. The plan schedules the block rows

@@ -167,6 +167,7 @@ PLAN_NO_SPLIT = 2
 PLAN_NARROW_STAGES = 4
 PLAN_DIAG_SKIP_COPIES = 1 << 8  # diagnostics only: C is wrong
 PLAN_DIAG_SKIP_MATH = 1 << 9    # diagnostics only: C is wrong
+PLAN_DIAG_SKIP_PREPASS = 1 << 10  # timing only: reuses the previous execute's B stacks
 
 
 class Distribution(enum.IntEnum):

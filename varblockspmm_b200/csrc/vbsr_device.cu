@@ -498,9 +498,11 @@ vbsr_status build_schedule(vbsr_plan* p) {
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
   // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
   p->bstack_floats = (d.K / 8) * int64_t(stack_m(rhs)) * 8;
-  if (p->bstack_floats / 4 >= (int64_t(1) << 31))
+  if ((d.K / 8) * rhs >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "B too large for the pre-pass index range");
   VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
+  // rows of RHS columns >= rhs (rhs < 32) are never written by the pre-pass: zero them once
+  VBSR_CUDA(cudaMemset(p->d_bstack, 0, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
   if (!items.empty())
     VBSR_CUDA(cudaMemcpy(p->d_items, items.data(), items.size() * sizeof(ItemDesc),
                          cudaMemcpyHostToDevice));
@@ -531,9 +533,9 @@ void free_plan(vbsr_plan* p) {
 
 // One execute: the B pre-pass, then the SpMM kernel, both on `stream`.
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
-  const int64_t pieces = p->bstack_floats / 4;
-  if (pieces > 0) {
-    const int64_t blocks = std::min<int64_t>((pieces + 255) / 256, 148 * 32);
+  const int64_t rows = (kp.K / 8) * kp.rhs;  // one thread per (8-column group, RHS column)
+  if (rows > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
+    const int64_t blocks = std::min<int64_t>((rows + 255) / 256, 148 * 64);
     bstack_kernel<<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, kp.rhs, p->d_bstack);
   }
   if (p->flags & VBSR_PLAN_BOUNDS_CHECK)

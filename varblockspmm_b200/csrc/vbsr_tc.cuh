@@ -486,26 +486,25 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // Pre-pass: the operand stacks S of all 8-column groups of B (K x rhs, column-major), one tile of
 // M rows x 8 floats per group (kg = k / 8) in the layout the MMA reads: row 2*half*q + j holds the
 // 8 values of RHS column c = half*q + j (raw, i.e. hi), row 2*half*q + half + j their lo parts,
-// rows of columns >= rhs are zero, and the two 16-byte halves of row r are exchanged when bit 2 of
-// r is set (32-byte swizzle). One thread per 16-byte piece; the two pieces of a row read one
-// 32-byte sector of B.
+// and the two 16-byte halves of row r are exchanged when bit 2 of r is set (32-byte swizzle).
+// Rows of columns >= rhs (only for rhs < 32, where M = 64 exceeds 2 rhs) stay as the plan wrote
+// them once (zero). One thread per (group, column): it reads the column's 32-byte sector and writes
+// the column's hi row and lo row; a warp covers whole tiles.
 __global__ void bstack_kernel(const float* __restrict__ B, long long K, int rhs, float* __restrict__ out) {
   const int M = stack_m(rhs), half = M / 8;
-  const int lg_m2 = M == 128 ? 8 : 7, lg_half = M == 128 ? 4 : 3;
-  const int total = int(K >> 3) << lg_m2;  // (K / 8) tiles x 2M pieces
-  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
-    const int kg = e >> lg_m2;
-    const int rem = e & ((1 << lg_m2) - 1);
-    const int row = rem >> 1;
-    const int q = row >> (lg_half + 1), jj = row & (2 * half - 1);
-    const int c = (q << lg_half) + (jj & (half - 1));
-    const int u = (rem & 1) ^ ((row >> 2) & 1);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (c < rhs) {
-      v = __ldg(reinterpret_cast<const float4*>(B + (long long)c * K + 8 * kg + 4 * u));
-      if (jj >= half) v = lo_part4(v);
-    }
-    reinterpret_cast<float4*>(out)[e] = v;
+  const int lg_rhs = __ffs(rhs) - 1, lg_half = __ffs(half) - 1;
+  const int total = int(K >> 3) << lg_rhs;  // (K / 8) groups x rhs columns
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+    const int kg = t >> lg_rhs, c = t & (rhs - 1);
+    const float4* src = reinterpret_cast<const float4*>(B + (long long)c * K + 8ll * kg);
+    const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
+    const int hi = ((c >> lg_half) << (lg_half + 1)) + (c & (half - 1)), lo = hi + half;
+    float4* tile = reinterpret_cast<float4*>(out) + (long long)kg * (2 * M);
+    const int sw = (hi >> 2) & 1;  // the same for the lo row (half is a multiple of 8)
+    tile[2 * hi + sw] = v0;
+    tile[2 * hi + (sw ^ 1)] = v1;
+    tile[2 * lo + sw] = lo_part4(v0);
+    tile[2 * lo + (sw ^ 1)] = lo_part4(v1);
   }
 }
 
