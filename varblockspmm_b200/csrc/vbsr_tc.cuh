@@ -1,18 +1,17 @@
 // vbsr_tc.cuh — the sm_100a SpMM kernel on 5th-generation tensor cores (tcgen05, TMEM).
 //
 // Per work item (one block row i: an h x nw tile of C) the kernel computes the transposed product
-//     D (M x 2h) = sum over the row's 8-column groups g of  S_g (M x 8) * [A_g ; A_g,lo]^T
+//     D (M x h) = sum over the row's 8-column groups g of  S_g (M x 8) * (A_g + A_g,lo)^T
 // with tcgen05.mma kind::tf32 (K = 8) and an fp32 accumulator in tensor memory.
 //
-// FP32 accuracy (3xTF32 in one MMA per group). The tensor core reads an fp32 operand as tf32 by
+// FP32 accuracy (3xTF32 in two MMAs per group). The tensor core reads an fp32 operand as tf32 by
 // ignoring its low 13 mantissa bits (truncation), so for x = hi + lo with hi = trunc_tf32(x) the
 // raw value already acts as hi and only lo = x - hi has to be formed (exactly, in fp32). The M side
 // of the MMA is the operand stack S: for every RHS column c the raw B value (hi) and its lo part
-// sit in two rows of S. The N side holds the group's h rows of raw A followed by its h rows of
-// A_lo. One MMA therefore produces all four products B_hi*A_hi, B_lo*A_hi, B_hi*A_lo, B_lo*A_lo
-// (the last one is below the tolerance but harmless), and the epilogue adds, for every C element,
-// the two S rows of its column at the two D columns of its row. M = 64 for nw <= 32 and M = 128
-// for nw = 64; N = 2h <= 128.
+// sit in two rows of S. The N side is the group's h rows of raw A, then (second MMA, same
+// accumulator) its h rows of A_lo. The two MMAs produce all four products B_hi*A_hi, B_lo*A_hi,
+// B_hi*A_lo, B_lo*A_lo (the last one is below the tolerance but harmless), and the epilogue adds,
+// for every C element, the two S rows of its column. M = 64 for nw <= 32 and M = 128 for nw = 64.
 //
 // The stacks of all 8-column groups of B are formed once per execute by a small pre-pass
 // (bstack_kernel) in global memory, already in the MMA's K-major, 32-byte-swizzled layout, so a
@@ -22,17 +21,18 @@
 // row r lives in lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of
 // quadrant q, so a warp adds them with one shuffle.
 //
-// CTA = fourteen warps, one CTA per SM:
+// CTA = sixteen warps, one CTA per SM:
 //   warps 0..7  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 8, which
 //               forms A_lo next to each group's A, fences the writes for the async proxy and hands
 //               the slot to the MMA warp; warps 0..3 store the results of even items, warps 4..7
 //               those of odd items, one item later (warp w reads TMEM quadrant w % 4);
-//   warps 8, 9  MMA warps: stage k is issued by MMA warp k % 2, one MMA per group into the warp's
+//   warps 8..11 MMA warps: stage k is issued by MMA warp k % 4, two MMAs per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 10..13 feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
+//   warps 12..15 feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
 //               group (the group's A and its stack S).
-// A single wait-and-release round on an mbarrier costs a warp ~200 cycles even when the barrier
-// has already completed, which is why every role is spread over several warps. The ring has D
+// A single wait-and-release round on an mbarrier costs a warp ~150-200 cycles even when the
+// barrier has already completed (and a wait next to MMA issue as much), which is why every role
+// is spread over several warps. The ring has D
 // slots, D a multiple of 8, stage k uses slot k % D: each slot then has one feeder, one split
 // warp and one MMA warp, all passing through its uses in order. Every warp walks the CTA's list of
 // stage descriptors (compiled by the planner; vbsr_internal.h). Every wait is bounded (see
@@ -52,7 +52,7 @@ namespace vbsr_b200 {
 
 constexpr int kTcSplitWarps = 8;            // split warps (warp w reads TMEM quadrant w % 4)
 constexpr int kTcEpiWarps = 4;              // split warps storing one item (one per quadrant)
-constexpr int kTcMmaWarps = 2;              // MMA-issuing warps
+constexpr int kTcMmaWarps = 4;              // MMA-issuing warps
 constexpr int kTcFeeders = 4;               // feeder warps
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
 constexpr int kTcThreads = 32 * kTcWarps;
@@ -67,7 +67,7 @@ __host__ __device__ constexpr int slot_stack(int G) { return 1024 * G; }
 __host__ __device__ constexpr int slot_floats(int rhs) {
   return slot_stack(stage_groups(rhs)) + stage_groups(rhs) * stack_m(rhs) * 8;
 }
-// TMEM: 2 accumulator buffers (items alternate) x 2 partials (one per MMA warp) x 128 columns.
+// TMEM: 2 accumulator buffers (items alternate) x 4 partials (one per MMA warp) x 64 columns.
 constexpr int kTmemAlloc = 512;
 
 // ---- tcgen05 wrappers ------------------------------------------------------------------------------
@@ -253,10 +253,10 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   }
 }
 
-// Epilogue of one item: D -> C, by split warp w (TMEM quadrant w). Partial i (128 columns after
+// Epilogue of one item: D -> C, by split warp w (TMEM quadrant w). Partial i (64 columns after
 // partial 0) holds the stages issued by MMA warp i; only partials that received a stage are read.
-// Within a partial, column r is row r of the tile from raw A and column h + r the same row from
-// A_lo. Lane j < half of quadrant w holds hi of RHS column n0 + half*w + j, lane half + j its lo.
+// Within a partial, column r is row r of the tile. Lane j < half of quadrant w holds hi of RHS
+// column n0 + half*w + j, lane half + j its lo.
 template <bool CHECK>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars& cb, int buf,
                                             uint32_t parity, uint32_t tmem_buf, int w, int lane,
@@ -267,11 +267,9 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   tc_fence_after();
   const int h = it.h(), nw = it.nw(), n0 = it.n0();
   const int half = stack_m(nw) / 8, quads = nw / half;
-  uint32_t use = 0;
-  if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH)) {
-    if (it.n >= 2) use = 3u;
-    else if (it.n == 1) use = 1u << (it.k0 & 1);
-  }
+  uint32_t use = 0;  // bit i: partial i received a stage of the item
+  if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH))
+    for (uint32_t i = 0; i < kTcMmaWarps && i < it.n; ++i) use |= 1u << ((it.k0 + i) & 3u);
   if (w < quads) {
     const uint32_t taddr = tmem_buf + (uint32_t(32 * w) << 16);
     const bool store = lane < half &&
@@ -280,24 +278,20 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
       record_status(p.status, VBSR_BOUNDS_VIOLATION, int(it.c_row));
     const int col = n0 + half * w + lane;
     float4* dst = reinterpret_cast<float4*>(p.C + (long long)col * p.M + it.c_row);
-    // passes of 8 tile rows: 2 partials x 2 halves (A, A_lo) x 8 values in flight per pass
+    // passes of 8 tile rows: 4 partials x 8 values in flight per pass
     for (int c0 = 0; c0 < h; c0 += 8) {
       float v[4][8];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        if (use & (1u << i)) {
-          const uint32_t t0 = taddr + uint32_t(128 * i + c0);
-          tc_ld8_nowait(t0, v[2 * i]);
-          tc_ld8_nowait(t0 + uint32_t(h), v[2 * i + 1]);
-        }
-      }
+      for (int i = 0; i < 4; ++i)
+        if (use & (1u << i)) tc_ld8_nowait(taddr + uint32_t(64 * i + c0), v[i]);
       tc_wait_ld();
       float r[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float a = 0.0f;
-        if (use & 1u) a += v[0][e] + v[1][e];
-        if (use & 2u) a += v[2][e] + v[3][e];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (use & (1u << i)) a += v[i][e];
         r[e] = a + __shfl_down_sync(0xffffffffu, a, half);
       }
       if (store) {
@@ -402,8 +396,8 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   VBSR_PROF_ADD(p, 0, t_all);
 }
 
-// MMA warp i (0..1): issues the stages k with k % 2 == i, one MMA per group into its partial
-// accumulator (TMEM columns 256 * buffer + 128 * i).
+// MMA warp i (0..3): issues the stages k with k % 4 == i, two MMAs per group (S x A, S x A_lo) into its partial
+// accumulator (TMEM columns 256 * buffer + 64 * i).
 template <bool CHECK>
 __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
                             const CtaBars& cb, uint32_t tmem_base, int i, int lane,
@@ -433,8 +427,9 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
     VBSR_PROF_ADD(p, 5, t_f);
     tc_fence_after();
     const int M = stack_m(it.nw());
-    const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 128 * i);
-    const uint32_t idesc = tf32_idesc(M, 2 * it.h());
+    const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 64 * i);
+    const uint32_t idesc = tf32_idesc(M, it.h());
+    const uint32_t lo_off = 32u * uint32_t(it.h());  // A_lo follows A (h rows of 32 bytes)
     uint32_t started = 0;
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
       const int groups = int((sw.word<0>() >> 28) & 3u) + 1;
@@ -457,8 +452,9 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
           tc_fence_after();
           const uint32_t sa = slots + 4u * uint32_t(s * SF);
           for (int g = 0; g < groups; ++g) {
-            tc_mma_tf32(tmem_d, sw32_desc(sa + 4u * uint32_t(slot_stack(G) + g * M * 8)),
-                        sw32_desc(sa + 4096u * g), idesc, started);
+            const uint64_t sdesc = sw32_desc(sa + 4u * uint32_t(slot_stack(G) + g * M * 8));
+            tc_mma_tf32(tmem_d, sdesc, sw32_desc(sa + 4096u * g), idesc, started);       // S x A
+            tc_mma_tf32(tmem_d, sdesc, sw32_desc(sa + 4096u * g + lo_off), idesc, 1u);  // S x A_lo
             started = 1u;
           }
         }
