@@ -81,6 +81,17 @@ struct StageWin {
     const u64 v = I == 0 ? cur.x : (I == 1 ? cur.y : (I == 2 ? cur.z : cur.w));
     return __shfl_sync(0xffffffffu, v, src);
   }
+  // Word I of the descriptor d < 32 positions ahead (from this window or the next).
+  template <int I>
+  __device__ __forceinline__ u64 word_ahead(int d) const {
+    const int idx = pos - wbase + d;
+    const int src = idx & 31;
+    const u64 a = I == 0 ? cur.x : (I == 1 ? cur.y : (I == 2 ? cur.z : cur.w));
+    const u64 b = I == 0 ? next.x : (I == 1 ? next.y : (I == 2 ? next.z : next.w));
+    const u64 va = __shfl_sync(0xffffffffu, a, src), vb = __shfl_sync(0xffffffffu, b, src);
+    return idx < 32 ? va : vb;
+  }
+  __device__ __forceinline__ bool has_ahead(int d) const { return pos + d < count; }
   __device__ __forceinline__ void advance(int lane) {
     if (++pos - wbase == 32) {
       wbase += 32;

@@ -54,6 +54,10 @@ constexpr int kTcSplitWarps = 8;            // split warps (warp w reads TMEM qu
 constexpr int kTcEpiWarps = 4;              // split warps storing one item (one per quadrant)
 constexpr int kTcMmaWarps = 4;              // MMA-issuing warps
 constexpr int kTcFeeders = 4;               // feeder warps
+#ifndef VBSR_PREFETCH
+#define VBSR_PREFETCH 4
+#endif
+constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this many own stages ahead
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
@@ -195,6 +199,13 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     st.w0 = win.word<0>();
     st.w2 = win.word<2>();
     st.w3 = win.word<3>();
+    if (kPrefetchAhead > 0 && win.has_ahead(kPrefetchAhead) &&
+        !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES)) {
+      // the A values of this feeder's stage kPrefetchAhead turns later, into L2 (one TMA op)
+      Stage pf;
+      pf.w0 = win.word_ahead<0>(kPrefetchAhead);
+      if (lane == 0) bulk_prefetch_l2(p.values + pf.a_start(), uint32_t(pf.h() * 4 * pf.cols()));
+    }
     win.advance(lane);
     const uint32_t full_bar = cb.full0 + 8u * s;
     VBSR_PROF_T0(t_w);
