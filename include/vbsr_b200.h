@@ -157,18 +157,21 @@ enum {
 };
 
 /* Plan::Plan (plan.cpp:5-18): rhs must be 8, 16, 32 or 64. The plan schedules the block rows
- * of `m` once (row-shape classes, heavy-row splitting, static load balance over the SMs) and
- * uploads that schedule to the matrix's device; the matrix must outlive the plan. */
+ * of `m` once (per-SM work lists balanced by a byte cost model, pipeline stages of 8-column
+ * groups), uploads that schedule to the matrix's device and allocates the buffer the B pre-pass
+ * writes (K/8 tiles of B's hi and lo rows); the matrix must outlive the plan. */
 vbsr_status vbsr_plan_create(const vbsr_matrix* m, int rhs, int kernel, vbsr_plan** out);
 vbsr_status vbsr_plan_create_ex(const vbsr_matrix* m, int rhs, int kernel, uint32_t flags,
                                 vbsr_plan** out);
 vbsr_status vbsr_plan_destroy(vbsr_plan* p);
 
-/* Plan::execute (plan.cpp:19-22): enqueues C = A * B on `stream` and returns. B is K x rhs and
- * C is M x rhs, column-major device buffers on the matrix's device. C is fully overwritten
- * (rows with no blocks become 0). No allocation, no host synchronisation, const on the plan:
- * concurrent calls from several host threads or streams are safe as long as their C buffers
- * differ. Launch failures return VBSR_CUDA_ERROR (cudaGetLastError right after the launch). */
+/* Plan::execute (plan.cpp:19-22): enqueues C = A * B on `stream` (two kernels: the B pre-pass
+ * into the plan's buffer, then the SpMM) and returns. B is K x rhs and C is M x rhs, column-major
+ * device buffers on the matrix's device. C is fully overwritten (rows with no blocks become 0). No
+ * allocation, no host synchronisation. Concurrent calls on one plan from several host threads or
+ * streams are safe when they pass the same B and different C; with different B use one plan per
+ * stream (the pre-pass buffer belongs to the plan). Launch failures return VBSR_CUDA_ERROR
+ * (cudaGetLastError right after the launch). */
 vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr_stream_t stream);
 
 /* Same computation as vbsr_plan_execute, for callers that must not have device memory allocated
