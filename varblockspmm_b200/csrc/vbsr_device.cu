@@ -368,7 +368,7 @@ cudaError_t set_kernel_attrs() {
 
 // Schedule for spmm_tc_kernel: one item per block row, one CTA per SM; items assigned to CTAs by
 // longest-processing-time-first on the cost model; each CTA's stream cuts the item's 8-column
-// groups into stages of stage_groups(rhs) groups.
+// groups into stages of stage_groups(h, rhs) groups.
 vbsr_status build_schedule(vbsr_plan* p) {
   const MatrixData& d = p->m->d;
   const int rhs = p->rhs;
@@ -380,8 +380,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
   const int R = d.block_rows;
   std::vector<int> row_stages(R);
   std::vector<double> cost(R);
-  const int G = stage_groups(rhs);  // 8-column groups per stage
   for (int i = 0; i < R; ++i) {
+    const int G = stage_groups(d.h_row_size[i], rhs);  // 8-column groups per stage
     int64_t groups = 0;
     for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b)
       groups += int64_t((d.h_blk_desc[b] & 7u) + 1u);
@@ -439,6 +439,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
       // format group g of a block starts 8*h*g floats after the block's values and a block row's
       // blocks are consecutive, so a stage's A values are one contiguous range.
       int64_t val = d.h_val_off_row[i];
+      const int G = stage_groups(h, rhs);
       int used = 0;  // columns in the current stage
       StageDesc cur{};
       for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
@@ -456,7 +457,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
             cur.w[0] = base0 | uint64_t((val + int64_t(8) * h * g) / 64);
             cur.w[1] = w1;
           }
-          const int gg = used / 8;
+          const int gg = used / 8;  // < kMaxStageGroups
           cur.w[2 + gg / 2] |= uint64_t((col + 8 * g) / 8) << (32 * (gg & 1));
           used += 8;
         }
@@ -468,13 +469,17 @@ vbsr_status build_schedule(vbsr_plan* p) {
       }
       // a block row without blocks keeps n = 0: its C rows are stored as zeros
       item.n = uint32_t(stream.size() - size_t(task.stage_off)) - item.k0;
+      const int64_t item_groups = d.h_sum_w[i] / 8;
+      if (item_groups >= (int64_t(1) << 24))
+        return set_error(VBSR_INVALID_ARGUMENT, "block row too wide for the schedule");
+      item.shape |= uint32_t(item_groups) << 8;
       items.push_back(item);
     }
     task.item_end = int(items.size());
     task.stage_end = int(stream.size());
     task.team_warps = kTcWarps;
     task.stage_floats = slot;
-    task.stage_cols = 8 * G;
+    task.stage_cols = 8 * kMaxStageGroups;
     task.stages = stages;
     h_tasks.push_back(task);
     p->task_warps.push_back(kTcWarps);
@@ -533,9 +538,9 @@ void free_plan(vbsr_plan* p) {
 
 // One execute: the B pre-pass, then the SpMM kernel, both on `stream`.
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
-  const int64_t rows = (kp.K / 8) * kp.rhs;  // one thread per (8-column group, RHS column)
-  if (rows > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
-    const int64_t blocks = std::min<int64_t>((rows + 255) / 256, 148 * 64);
+  const int64_t chunks = (kp.K / 8 + kBsGroups - 1) / kBsGroups;  // kBsGroups groups per block
+  if (chunks > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
+    const int64_t blocks = std::min<int64_t>(chunks, 148 * 8);
     bstack_kernel<<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, kp.rhs, p->d_bstack);
   }
   if (p->flags & VBSR_PLAN_BOUNDS_CHECK)

@@ -16,22 +16,24 @@ void clear_error();
 
 // ---- work schedule ---------------------------------------------------------------------------
 // The plan compiles the matrix into, per CTA, a list of work items (one block row each: an h x nw
-// tile of C) and the list of their pipeline stages. A stage covers up to four consecutive 8-column
-// groups of one item, possibly from several blocks. Because a block row's blocks are contiguous in
+// tile of C) and the list of their pipeline stages. A stage covers up to eight consecutive
+// 8-column groups of one item (as many as fit one shared-memory slot at the item's h), possibly
+// from several blocks. Because a block row's blocks are contiguous in
 // the value array and each block stores its groups in order (h x 8 floats each), the A values of a
 // stage are one contiguous range; B is fetched per 8-column group. A block row with no blocks is an
 // item without stages (its C rows are stored as zeros).
-// Stage descriptor, 4 x 64 bits:
+// Stage descriptor, 8 x 64 bits:
 //   w0: bits  0..27 A start / 64 (offsets of blocks and groups are multiples of 64 floats)
-//       bits 28..29 columns/8 - 1
+//       bits 28..31 groups - 1 (a stage holds 1..8 groups of 8 block columns)
 //       bits 32..34 h/8 - 1         bits 36..38 n0/8   bits 39..40 log2(nw/8)
 //   w1: the item's index in the CTA's item list
-//   w2: group 0 column / 8 (bits 0..27), group 1 column / 8 (bits 32..59)
-//   w3: group 2 column / 8, group 3 column / 8
-struct alignas(32) StageDesc {
-  uint64_t w[4];
+//   w2..w5: the groups' scalar columns / 8, two per word (group 2i in bits 0..27 of w[2+i],
+//           group 2i+1 in bits 32..59)
+//   w6, w7: unused
+struct alignas(64) StageDesc {
+  uint64_t w[8];
 };
-static_assert(sizeof(StageDesc) == 32, "StageDesc layout");
+static_assert(sizeof(StageDesc) == 64, "StageDesc layout");
 namespace stage {
 constexpr int64_t kMaxVal = (int64_t(1) << 28) * 64;  // value offsets must stay below this
 constexpr int64_t kMaxCol = (int64_t(1) << 28) * 8;   // scalar columns must stay below this
@@ -44,7 +46,8 @@ inline int nw_code(int nw) {
 
 // Item descriptor, 4 x 32 bits:
 //   x: c_row (first scalar row of the tile in C)
-//   y: bits 0..2 h/8 - 1, bits 3..5 n0/8, bits 6..7 log2(nw/8)
+//   y: bits 0..2 h/8 - 1, bits 3..5 n0/8, bits 6..7 log2(nw/8), bits 8..31 the item's number of
+//      8-column groups (its stages hold stage_groups(h, rhs) groups each, the last one the rest)
 //   z: index of the item's first stage in the CTA's stage list
 //   w: number of stages of the item (0 for a block row without blocks)
 struct alignas(16) ItemDesc {
@@ -58,7 +61,7 @@ struct alignas(16) Task {
   int team_warps;     // warps per CTA
   int stages;         // ring depth (slots)
   int stage_floats;   // floats per slot
-  int stage_cols;     // block columns one stage holds at most
+  int stage_cols;     // block columns one stage holds at most (any h)
   int pad[8];
 };
 static_assert(sizeof(Task) == 64, "Task layout");

@@ -33,15 +33,16 @@ struct KernelParams {
 // ---- stage descriptors -----------------------------------------------------------------------------
 
 struct Stage {
-  u64 w0, w2, w3;
+  u64 w0, g[4];  // descriptor words 0 and 2..5
   __device__ __forceinline__ long long a_start() const { return (long long)(w0 & 0xfffffffull) * 64; }
-  __device__ __forceinline__ int cols() const { return int(((w0 >> 28) & 3u) + 1u) * 8; }
+  __device__ __forceinline__ int groups() const { return int((w0 >> 28) & 15u) + 1; }
   __device__ __forceinline__ int h() const { return int(((w0 >> 32) & 7u) + 1u) * 8; }
   __device__ __forceinline__ int n0() const { return int((w0 >> 36) & 7u) * 8; }
   __device__ __forceinline__ int nw() const { return 8 << int((w0 >> 39) & 3u); }
-  __device__ __forceinline__ int group_col(int g) const {  // scalar column of 8-column group g
-    const u64 w = g < 2 ? w2 : w3;
-    return int((w >> (32 * (g & 1))) & 0xfffffffull) * 8;
+  __device__ __forceinline__ int group_col(int i) const {  // scalar column of group i
+    const int k = i >> 1;  // selected without indexing, so the words stay in registers
+    const u64 w = k == 0 ? g[0] : (k == 1 ? g[1] : (k == 2 ? g[2] : g[3]));
+    return int((w >> (32 * (i & 1))) & 0xfffffffull) * 8;
   }
 };
 
@@ -50,21 +51,33 @@ struct Item {
   __device__ __forceinline__ int h() const { return int((shape & 7u) + 1u) * 8; }
   __device__ __forceinline__ int n0() const { return int((shape >> 3) & 7u) * 8; }
   __device__ __forceinline__ int nw() const { return 8 << int((shape >> 6) & 3u); }
+  __device__ __forceinline__ int groups() const { return int(shape >> 8); }
+  // groups of the item's stage i (0 <= i < n), with G groups per full stage (stage_groups(h, rhs))
+  __device__ __forceinline__ int stage_groups(int i, int G) const {
+    const int r = groups() - i * G;
+    return r < G ? r : G;
+  }
 };
 
 // Every `stride`-th stage descriptor from `first` on (count of them), seen through a window of 32
 // (lane i holds element wbase + i) and the following window, loaded one window ahead; reading a
-// word is two shuffles. All lanes keep identical pos / wbase.
+// stage is ten shuffles. All lanes keep identical pos / wbase.
 struct StageWin {
-  ulonglong4 cur, next;
+  Stage cur, next;
   const StageDesc* base;
   int pos, wbase, count, stride;
 
-  __device__ __forceinline__ ulonglong4 load(int i) const {
-    if (i >= count) return make_ulonglong4(0, 0, 0, 0);
+  __device__ __forceinline__ Stage load(int i) const {
+    Stage st{};
+    if (i >= count) return st;
     const ulonglong2* q = reinterpret_cast<const ulonglong2*>(base + (long long)i * stride);
-    const ulonglong2 a = __ldg(q), b = __ldg(q + 1);
-    return make_ulonglong4(a.x, a.y, b.x, b.y);
+    const ulonglong2 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 2);
+    st.w0 = a.x;
+    st.g[0] = b.x;
+    st.g[1] = b.y;
+    st.g[2] = c.x;
+    st.g[3] = c.y;
+    return st;
   }
   __device__ __forceinline__ void init(const StageDesc* s, int first, int stride_, int n, int lane) {
     base = s + first;
@@ -75,20 +88,19 @@ struct StageWin {
     cur = load(lane);
     next = load(32 + lane);
   }
-  template <int I>
-  __device__ __forceinline__ u64 word() const {
+  __device__ __forceinline__ Stage get() const {
     const int src = (pos - wbase) & 31;
-    const u64 v = I == 0 ? cur.x : (I == 1 ? cur.y : (I == 2 ? cur.z : cur.w));
-    return __shfl_sync(0xffffffffu, v, src);
+    Stage st;
+    st.w0 = __shfl_sync(0xffffffffu, cur.w0, src);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st.g[i] = __shfl_sync(0xffffffffu, cur.g[i], src);
+    return st;
   }
-  // Word I of the descriptor d < 32 positions ahead (from this window or the next).
-  template <int I>
-  __device__ __forceinline__ u64 word_ahead(int d) const {
+  // Word 0 of the descriptor d < 32 positions ahead (from this window or the next).
+  __device__ __forceinline__ u64 word0_ahead(int d) const {
     const int idx = pos - wbase + d;
     const int src = idx & 31;
-    const u64 a = I == 0 ? cur.x : (I == 1 ? cur.y : (I == 2 ? cur.z : cur.w));
-    const u64 b = I == 0 ? next.x : (I == 1 ? next.y : (I == 2 ? next.z : next.w));
-    const u64 va = __shfl_sync(0xffffffffu, a, src), vb = __shfl_sync(0xffffffffu, b, src);
+    const u64 va = __shfl_sync(0xffffffffu, cur.w0, src), vb = __shfl_sync(0xffffffffu, next.w0, src);
     return idx < 32 ? va : vb;
   }
   __device__ __forceinline__ bool has_ahead(int d) const { return pos + d < count; }

@@ -61,16 +61,19 @@ constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this m
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
-// 8-column groups per stage: 4 (32 block columns) for rhs <= 32, 3 for rhs = 64, so that a slot
-// is 24 KB either way and eight slots fit in shared memory.
-__host__ __device__ constexpr int stage_groups(int rhs) { return rhs > 32 ? 3 : 4; }
-// Slot layout (floats), G = groups per stage: group g's N-side operand at 1024 g (h rows of raw A,
-// 8 floats each, followed by the h rows of A_lo), then the operand stacks of the groups (M x 8
-// each) from 1024 G.
-__host__ __device__ constexpr int slot_stack(int G) { return 1024 * G; }
-__host__ __device__ constexpr int slot_floats(int rhs) {
-  return slot_stack(stage_groups(rhs)) + stage_groups(rhs) * stack_m(rhs) * 8;
+// A slot (26 KB) holds one stage: for each of its groups g the N-side operand (h rows of raw A, 8
+// floats each, then the h rows of A_lo) at byte 64 h g, then the groups' operand stacks S (M rows
+// of 32 bytes each) from byte 64 h G (G = the stage's groups). A stage takes as many consecutive
+// groups of its item as fit, at most 8: G = stage_groups(h, rhs).
+constexpr int kSlotBytes = 26 * 1024;
+constexpr int kMaxStageGroups = 8;
+__host__ __device__ constexpr int slot_floats(int rhs) { return (void)rhs, kSlotBytes / 4; }
+__host__ __device__ constexpr int stage_groups(int h, int rhs) {
+  return kSlotBytes / (64 * h + 32 * stack_m(rhs)) < kMaxStageGroups
+             ? kSlotBytes / (64 * h + 32 * stack_m(rhs))
+             : kMaxStageGroups;
 }
+__host__ __device__ constexpr int slot_stack_bytes(int h, int groups) { return 64 * h * groups; }
 // TMEM: 2 accumulator buffers (items alternate) x 4 partials (one per MMA warp) x 64 columns.
 constexpr int kTmemAlloc = 512;
 
@@ -185,7 +188,7 @@ struct CtaBars {
 template <bool CHECK>
 __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
                           const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
-  const int D = task.stages, SF = task.stage_floats, G = task.stage_cols >> 3;
+  const int D = task.stages, SF = task.stage_floats;
   const int nst = task.stage_end - task.stage_off;
   StageWin win;
   win.init(p.stages + task.stage_off, f, kTcFeeders, nst, lane);
@@ -195,28 +198,25 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
   VBSR_PROF_T0(t_all);
   for (int kk = f; kk < nst; kk += kTcFeeders) {
-    Stage st;
-    st.w0 = win.word<0>();
-    st.w2 = win.word<2>();
-    st.w3 = win.word<3>();
+    const Stage st = win.get();
     if (kPrefetchAhead > 0 && win.has_ahead(kPrefetchAhead) &&
         !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES)) {
       // the A values of this feeder's stage kPrefetchAhead turns later, into L2 (one TMA op)
       Stage pf;
-      pf.w0 = win.word_ahead<0>(kPrefetchAhead);
-      if (lane == 0) bulk_prefetch_l2(p.values + pf.a_start(), uint32_t(pf.h() * 4 * pf.cols()));
+      pf.w0 = win.word0_ahead(kPrefetchAhead);
+      if (lane == 0) bulk_prefetch_l2(p.values + pf.a_start(), uint32_t(32 * pf.h() * pf.groups()));
     }
     win.advance(lane);
     const uint32_t full_bar = cb.full0 + 8u * s;
     VBSR_PROF_T0(t_w);
     if (!wait_phase(cb.empty0 + 8u * s, ph ^ 1u, p, abort_flag, lane)) break;
     VBSR_PROF_ADD(p, 7, t_w);
-    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.cols() >> 3;
+    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.groups();
     const long long a0 = st.a_start();
     bool ok = true;
     if (CHECK) {
       ok = a0 + 8ll * h * groups <= p.nvalues && n0 == 0 && nw == p.rhs &&
-           8 * groups <= task.stage_cols;
+           groups <= stage_groups(h, p.rhs);
       for (int g = 0; g < groups; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
     }
     if (kk == p.drop_stage) {
@@ -233,12 +233,12 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
       __syncwarp();
       if (lane < groups) {
         // group `lane`: h rows x 8 floats, contiguous in the device format
-        bulk_g2s(sp + 4096u * lane, p.values + a0 + 8ll * h * lane, uint32_t(32 * h), full_bar,
+        bulk_g2s(sp + 64u * h * lane, p.values + a0 + 8ll * h * lane, uint32_t(32 * h), full_bar,
                  pol_a);
       } else if (lane < 2 * groups) {
         // group g's stack: M rows x 32 bytes of the pre-pass output for 8-column group col/8
         const int g = lane - groups;
-        bulk_g2s(sp + 4u * uint32_t(slot_stack(G) + g * M * 8),
+        bulk_g2s(sp + uint32_t(slot_stack_bytes(h, groups) + 32 * M * g),
                  p.bstack + (long long)(st.group_col(g) >> 3) * (M * 8), uint32_t(M * 32), full_bar,
                  pol_b);
       }
@@ -317,14 +317,14 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   return true;
 }
 
-// A_lo of a whole stage at shared address sp: group g's A (2h float4s) at byte 4096 g, its A_lo
+// A_lo of a whole stage at shared address sp: group g's A (2h float4s) at byte 64 h g, its A_lo
 // right after it. Lane l handles float4s l, l + 32, ... of each group; a group's four loads are in
 // flight before its stores.
 __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane) {
   const int run = 2 * h;  // <= 128 float4s per group: at most 4 per lane
   const uint32_t base = sp + 16u * lane, lo_off = 32u * h;
   for (int g = 0; g < groups; ++g) {
-    const uint32_t a = base + 4096u * g;
+    const uint32_t a = base + 64u * h * g;
     float4 x[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
@@ -343,11 +343,8 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
   const int D = task.stages, SF = task.stage_floats;
-  const int nst = task.stage_end - task.stage_off;
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
-  StageWin sw;
-  sw.init(p.stages + task.stage_off, w, kTcSplitWarps, nst, lane);
   int kk = w;      // this warp's next stage
   int ms = w;      // its slot (this warp's slots are w, w + 8, ...)
   uint32_t mph = 0;
@@ -360,10 +357,9 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   while (ok && !iw.done()) {
     const Item it = iw.get();
     iw.advance(lane);
-    const int h = it.h(), nw = it.nw();
+    const int h = it.h(), G = stage_groups(h, p.rhs);
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcSplitWarps) {
-      const int cols = int(((sw.word<0>() >> 28) & 3u) + 1u) * 8;
-      sw.advance(lane);
+      const int groups = it.stage_groups(kk - int(it.k0), G);
       const int s = ms;
       const uint32_t par = mph;
       if ((ms += kTcSplitWarps) >= D) {
@@ -378,7 +374,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       VBSR_PROF_ADD(p, 1, t_w);
       VBSR_PROF_T0(t_s);
       if (math) {
-        split_stage(slots + 4u * uint32_t(s * SF), cols >> 3, h, lane);
+        split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
         fence_proxy_async_smem();
       }
       __syncwarp();
@@ -413,14 +409,11 @@ template <bool CHECK>
 __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
                             const CtaBars& cb, uint32_t tmem_base, int i, int lane,
                             volatile int* abort_flag) {
-  const int D = task.stages, SF = task.stage_floats, G = task.stage_cols >> 3;
-  const int nst = task.stage_end - task.stage_off;
+  const int D = task.stages, SF = task.stage_floats;
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
-  StageWin sw;
-  sw.init(p.stages + task.stage_off, i, kTcMmaWarps, nst, lane);
   int kk = i;      // this warp's next stage
-  int ms = i;      // its slot (this warp's slots are i, i + 2, ...)
+  int ms = i;      // its slot (this warp's slots are i, i + 4, ...)
   uint32_t mph = 0;
   int j = 0;       // items started
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
@@ -437,14 +430,13 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
       break;
     VBSR_PROF_ADD(p, 5, t_f);
     tc_fence_after();
-    const int M = stack_m(it.nw());
+    const int M = stack_m(it.nw()), h = it.h(), G = stage_groups(h, p.rhs);
     const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 64 * i);
-    const uint32_t idesc = tf32_idesc(M, it.h());
-    const uint32_t lo_off = 32u * uint32_t(it.h());  // A_lo follows A (h rows of 32 bytes)
+    const uint32_t idesc = tf32_idesc(M, h);
+    const uint32_t lo_off = 32u * uint32_t(h);  // A_lo follows A (h rows of 32 bytes)
     uint32_t started = 0;
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
-      const int groups = int((sw.word<0>() >> 28) & 3u) + 1;
-      sw.advance(lane);
+      const int groups = it.stage_groups(kk - int(it.k0), G);
       const int s = ms;
       const uint32_t par = mph;
       if ((ms += kTcMmaWarps) >= D) {
@@ -462,10 +454,12 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
         if (math) {
           tc_fence_after();
           const uint32_t sa = slots + 4u * uint32_t(s * SF);
+          const uint32_t ss = sa + uint32_t(slot_stack_bytes(h, groups));
           for (int g = 0; g < groups; ++g) {
-            const uint64_t sdesc = sw32_desc(sa + 4u * uint32_t(slot_stack(G) + g * M * 8));
-            tc_mma_tf32(tmem_d, sdesc, sw32_desc(sa + 4096u * g), idesc, started);       // S x A
-            tc_mma_tf32(tmem_d, sdesc, sw32_desc(sa + 4096u * g + lo_off), idesc, 1u);  // S x A_lo
+            const uint64_t sdesc = sw32_desc(ss + 32u * M * g);
+            const uint32_t ag = sa + 64u * h * g;
+            tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag), idesc, started);          // S x A
+            tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag + lo_off), idesc, 1u);      // S x A_lo
             started = 1u;
           }
         }
@@ -495,24 +489,44 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // 8 values of RHS column c = half*q + j (raw, i.e. hi), row 2*half*q + half + j their lo parts,
 // and the two 16-byte halves of row r are exchanged when bit 2 of r is set (32-byte swizzle).
 // Rows of columns >= rhs (only for rhs < 32, where M = 64 exceeds 2 rhs) stay as the plan wrote
-// them once (zero). One thread per (group, column): it reads the column's 32-byte sector and writes
-// the column's hi row and lo row; a warp covers whole tiles.
-__global__ void bstack_kernel(const float* __restrict__ B, long long K, int rhs, float* __restrict__ out) {
+// them once (zero). A block transposes kBsGroups consecutive groups through shared memory: it reads
+// each RHS column's 8 * kBsGroups consecutive values (coalesced), then writes the kBsGroups tiles
+// (contiguous) with 16-byte stores.
+constexpr int kBsGroups = 16;
+__global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
+                                                     int rhs, float* __restrict__ out) {
+  __shared__ float4 buf[64 * kBsGroups * 2];  // [c][kg][2 x float4]: up to 32 KB
   const int M = stack_m(rhs), half = M / 8;
-  const int lg_rhs = __ffs(rhs) - 1, lg_half = __ffs(half) - 1;
-  const int total = int(K >> 3) << lg_rhs;  // (K / 8) groups x rhs columns
-  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
-    const int kg = t >> lg_rhs, c = t & (rhs - 1);
-    const float4* src = reinterpret_cast<const float4*>(B + (long long)c * K + 8ll * kg);
-    const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-    const int hi = ((c >> lg_half) << (lg_half + 1)) + (c & (half - 1)), lo = hi + half;
-    float4* tile = reinterpret_cast<float4*>(out) + (long long)kg * (2 * M);
-    const int sw = (hi >> 2) & 1;  // the same for the lo row (half is a multiple of 8)
-    tile[2 * hi + sw] = v0;
-    tile[2 * hi + (sw ^ 1)] = v1;
-    tile[2 * lo + sw] = lo_part4(v0);
-    tile[2 * lo + (sw ^ 1)] = lo_part4(v1);
+  const int lg_half = __ffs(half) - 1, lg_rhs = __ffs(rhs) - 1;
+  const long long ngroups = K >> 3;
+  for (long long kg0 = (long long)blockIdx.x * kBsGroups; kg0 < ngroups;
+       kg0 += (long long)gridDim.x * kBsGroups) {
+    const int ng = int(ngroups - kg0 < kBsGroups ? ngroups - kg0 : kBsGroups);
+    // read: float4 i of the block -> column c = i / (2 ng'), piece within the column's run
+    const int per_col = 2 * kBsGroups;  // float4s per column run (full block)
+    for (int i = threadIdx.x; i < rhs * per_col; i += blockDim.x) {
+      const int c = i / per_col, r = i - c * per_col;
+      if (r < 2 * ng)
+        buf[i] = __ldg(reinterpret_cast<const float4*>(B + (long long)c * K + 8 * kg0) + r);
+    }
+    __syncthreads();
+    // write: tile g, row `row`, 16-byte piece `up` (2M float4s per tile)
+    float4* dst = reinterpret_cast<float4*>(out) + kg0 * (2 * M);
+    for (int i = threadIdx.x; i < ng * 2 * M; i += blockDim.x) {
+      const int g = i / (2 * M), rem = i - g * 2 * M;
+      const int row = rem >> 1, up = rem & 1;
+      const int q = row >> (lg_half + 1), jj = row & (2 * half - 1);
+      const int c = (q << lg_half) + (jj & (half - 1));
+      if (c < rhs) {
+        const int u = up ^ ((row >> 2) & 1);
+        float4 v = buf[c * per_col + 2 * g + u];
+        if (jj >= half) v = lo_part4(v);
+        dst[i] = v;
+      }
+    }
+    __syncthreads();
   }
+  (void)lg_rhs;
 }
 
 template <bool CHECK>
