@@ -51,14 +51,14 @@
 namespace vbsr_b200 {
 
 constexpr int kTcSplitWarps = 8;            // split warps (warp w reads TMEM quadrant w % 4)
-constexpr int kTcEpiWarps = 4;              // split warps storing one item (one per quadrant)
+constexpr int kTcEpiWarps = 4;              // epilogue warps (warp q: TMEM quadrant q)
 constexpr int kTcMmaWarps = 4;              // MMA-issuing warps
 constexpr int kTcFeeders = 4;               // feeder warps
 #ifndef VBSR_PREFETCH
 #define VBSR_PREFETCH 4
 #endif
 constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this many own stages ahead
-constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders;
+constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders + kTcEpiWarps;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 // A slot (26 KB) holds one stage: for each of its groups g the N-side operand (h rows of raw A, 8
@@ -335,9 +335,7 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int 
   }
 }
 
-// Split warp w (0..7): forms the lo parts of the stages k with k % 8 == w, and stores the results of
-// the items j with j % 2 == w / 4 (TMEM quadrant w % 4) one item later; buffer j % 2 is therefore
-// always read by the same four warps.
+// Split warp w (0..7): forms the lo parts of the stages k with k % 8 == w (slot w).
 template <bool CHECK>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
@@ -348,9 +346,6 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   int kk = w;      // this warp's next stage
   int ms = w;      // its slot (this warp's slots are w, w + 8, ...)
   uint32_t mph = 0;
-  int j = 0;       // items done
-  const int grp = w >> 2, q = w & 3;
-  Item prev{};
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
   bool ok = true;
   VBSR_PROF_T0(t_all);
@@ -381,26 +376,27 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       if (lane == 0) mbar_arrive(cb.split0 + 8u * s);
       VBSR_PROF_ADD(p, 2, t_s);
     }
-    if (!ok) break;
-    if (j > 0 && ((j - 1) & 1) == grp) {
-      const int pj = j - 1;
-      VBSR_PROF_T0(t_e);
-      if (!tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1),
-                              tmem_base + uint32_t(256 * (pj & 1)), q, lane, prev, abort_flag)) {
-        ok = false;
-        break;
-      }
-      VBSR_PROF_ADD(p, 8, t_e);
-    }
-    prev = it;
-    ++j;
-  }
-  if (ok && j > 0 && ((j - 1) & 1) == grp) {
-    const int pj = j - 1;
-    tc_epilogue<CHECK>(p, cb, pj & 1, uint32_t((pj >> 1) & 1), tmem_base + uint32_t(256 * (pj & 1)),
-                       q, lane, prev, abort_flag);
   }
   VBSR_PROF_ADD(p, 0, t_all);
+}
+
+// Epilogue warp q (0..3, TMEM quadrant q): stores every item's result as soon as its MMAs are done.
+template <bool CHECK>
+__device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBars& cb,
+                            uint32_t tmem_base, int q, int lane, volatile int* abort_flag) {
+  ItemWin iw;
+  iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
+  VBSR_PROF_T0(t_all);
+  for (int j = 0; !iw.done(); ++j) {
+    const Item it = iw.get();
+    iw.advance(lane);
+    VBSR_PROF_T0(t_e);
+    if (!tc_epilogue<CHECK>(p, cb, j & 1, uint32_t((j >> 1) & 1),
+                            tmem_base + uint32_t(256 * (j & 1)), q, lane, it, abort_flag))
+      break;
+    VBSR_PROF_ADD(p, 8, t_e);
+  }
+  VBSR_PROF_ADD(p, 11, t_all);
 }
 
 // MMA warp i (0..3): issues the stages k with k % 4 == i, two MMAs per group (S x A, S x A_lo) into its partial
@@ -576,8 +572,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     tc_split_warp<CHECK>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < kTcSplitWarps + kTcMmaWarps)
     tc_mma_warp<CHECK>(p, task, slots, cb, tmem_base, warp - kTcSplitWarps, lane, &abort_flag);
-  else
+  else if (warp < kTcSplitWarps + kTcMmaWarps + kTcFeeders)
     tc_feeder<CHECK>(p, task, slots, cb, warp - kTcSplitWarps - kTcMmaWarps, lane, &abort_flag);
+  else  // the epilogue warps are warps 16..19: TMEM quadrant warp % 4 = warp - 16
+    tc_epi_warp<CHECK>(p, task, cb, tmem_base, warp & 3, lane, &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
