@@ -16,7 +16,7 @@ void clear_error();
 
 // ---- work schedule ---------------------------------------------------------------------------
 // The plan compiles the matrix into, per CTA, a list of work items (one block row each: an h x nw
-// tile of C) and the list of their pipeline stages. A stage covers up to eight consecutive
+// tile of C) and the list of their pipeline stages. A stage covers up to twelve consecutive
 // 8-column groups of one item (as many as fit one shared-memory slot at the item's h), possibly
 // from several blocks. Because a block row's blocks are contiguous in
 // the value array and each block stores its groups in order (h x 8 floats each), the A values of a
@@ -24,12 +24,11 @@ void clear_error();
 // item without stages (its C rows are stored as zeros).
 // Stage descriptor, 8 x 64 bits:
 //   w0: bits  0..27 A start / 64 (offsets of blocks and groups are multiples of 64 floats)
-//       bits 28..31 groups - 1 (a stage holds 1..8 groups of 8 block columns)
+//       bits 28..31 groups - 1 (a stage holds 1..12 groups of 8 block columns)
 //       bits 32..34 h/8 - 1         bits 36..38 n0/8   bits 39..40 log2(nw/8)
 //   w1: the item's index in the CTA's item list
-//   w2..w5: the groups' scalar columns / 8, two per word (group 2i in bits 0..27 of w[2+i],
+//   w2..w7: the groups' scalar columns / 8, two per word (group 2i in bits 0..27 of w[2+i],
 //           group 2i+1 in bits 32..59)
-//   w6, w7: unused
 struct alignas(64) StageDesc {
   uint64_t w[8];
 };

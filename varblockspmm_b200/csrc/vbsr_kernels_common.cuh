@@ -33,7 +33,7 @@ struct KernelParams {
 // ---- stage descriptors -----------------------------------------------------------------------------
 
 struct Stage {
-  u64 w0, g[4];  // descriptor words 0 and 2..5
+  u64 w0, g[6];  // descriptor words 0 and 2..7
   __device__ __forceinline__ long long a_start() const { return (long long)(w0 & 0xfffffffull) * 64; }
   __device__ __forceinline__ int groups() const { return int((w0 >> 28) & 15u) + 1; }
   __device__ __forceinline__ int h() const { return int(((w0 >> 32) & 7u) + 1u) * 8; }
@@ -41,7 +41,8 @@ struct Stage {
   __device__ __forceinline__ int nw() const { return 8 << int((w0 >> 39) & 3u); }
   __device__ __forceinline__ int group_col(int i) const {  // scalar column of group i
     const int k = i >> 1;  // selected without indexing, so the words stay in registers
-    const u64 w = k == 0 ? g[0] : (k == 1 ? g[1] : (k == 2 ? g[2] : g[3]));
+    const u64 w = k == 0 ? g[0]
+                         : (k == 1 ? g[1] : (k == 2 ? g[2] : (k == 3 ? g[3] : (k == 4 ? g[4] : g[5]))));
     return int((w >> (32 * (i & 1))) & 0xfffffffull) * 8;
   }
 };
@@ -61,7 +62,7 @@ struct Item {
 
 // Every `stride`-th stage descriptor from `first` on (count of them), seen through a window of 32
 // (lane i holds element wbase + i) and the following window, loaded one window ahead; reading a
-// stage is ten shuffles. All lanes keep identical pos / wbase.
+// stage is fourteen shuffles. All lanes keep identical pos / wbase.
 struct StageWin {
   Stage cur, next;
   const StageDesc* base;
@@ -71,12 +72,14 @@ struct StageWin {
     Stage st{};
     if (i >= count) return st;
     const ulonglong2* q = reinterpret_cast<const ulonglong2*>(base + (long long)i * stride);
-    const ulonglong2 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 2);
+    const ulonglong2 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 2), d = __ldg(q + 3);
     st.w0 = a.x;
     st.g[0] = b.x;
     st.g[1] = b.y;
     st.g[2] = c.x;
     st.g[3] = c.y;
+    st.g[4] = d.x;
+    st.g[5] = d.y;
     return st;
   }
   __device__ __forceinline__ void init(const StageDesc* s, int first, int stride_, int n, int lane) {
@@ -93,7 +96,7 @@ struct StageWin {
     Stage st;
     st.w0 = __shfl_sync(0xffffffffu, cur.w0, src);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) st.g[i] = __shfl_sync(0xffffffffu, cur.g[i], src);
+    for (int i = 0; i < 6; ++i) st.g[i] = __shfl_sync(0xffffffffu, cur.g[i], src);
     return st;
   }
   // Word 0 of the descriptor d < 32 positions ahead (from this window or the next).

@@ -64,9 +64,15 @@ __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 // A slot (26 KB) holds one stage: for each of its groups g the N-side operand (h rows of raw A, 8
 // floats each, then the h rows of A_lo) at byte 64 h g, then the groups' operand stacks S (M rows
 // of 32 bytes each) from byte 64 h G (G = the stage's groups). A stage takes as many consecutive
-// groups of its item as fit, at most 8: G = stage_groups(h, rhs).
-constexpr int kSlotBytes = 26 * 1024;
-constexpr int kMaxStageGroups = 8;
+// groups of its item as fit, at most kMaxStageGroups: G = stage_groups(h, rhs).
+#ifndef VBSR_SLOT_KB
+#define VBSR_SLOT_KB 26
+#endif
+#ifndef VBSR_MAX_GROUPS
+#define VBSR_MAX_GROUPS 8
+#endif
+constexpr int kSlotBytes = VBSR_SLOT_KB * 1024;
+constexpr int kMaxStageGroups = VBSR_MAX_GROUPS;
 __host__ __device__ constexpr int slot_floats(int rhs) { return (void)rhs, kSlotBytes / 4; }
 __host__ __device__ constexpr int stage_groups(int h, int rhs) {
   return kSlotBytes / (64 * h + 32 * stack_m(rhs)) < kMaxStageGroups
