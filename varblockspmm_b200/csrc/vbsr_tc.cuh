@@ -21,15 +21,16 @@
 // row r lives in lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of
 // quadrant q, so a warp adds them with one shuffle.
 //
-// CTA = sixteen warps, one CTA per SM:
+// CTA = twenty warps, one CTA per SM:
 //   warps 0..7  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 8, which
 //               forms A_lo next to each group's A, fences the writes for the async proxy and hands
-//               the slot to the MMA warp; warps 0..3 store the results of even items, warps 4..7
-//               those of odd items, one item later (warp w reads TMEM quadrant w % 4);
+//               the slot to the MMA warp;
 //   warps 8..11 MMA warps: stage k is issued by MMA warp k % 4, two MMAs per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
 //   warps 12..15 feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
-//               group (the group's A and its stack S).
+//               group (the group's A and its stack S);
+//   warps 16..19 epilogue warps: warp q reads TMEM quadrant q of every item's accumulators as soon
+//               as its MMAs are done and stores the item's C rows.
 // A single wait-and-release round on an mbarrier costs a warp ~150-200 cycles even when the
 // barrier has already completed (and a wait next to MMA issue as much), which is why every role
 // is spread over several warps. The ring has D
@@ -61,7 +62,7 @@ constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this m
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders + kTcEpiWarps;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
-// A slot (26 KB) holds one stage: for each of its groups g the N-side operand (h rows of raw A, 8
+// A slot (26 KB by default) holds one stage: for each of its groups g the N-side operand (h rows of raw A, 8
 // floats each, then the h rows of A_lo) at byte 64 h g, then the groups' operand stacks S (M rows
 // of 32 bytes each) from byte 64 h G (G = the stage's groups). A stage takes as many consecutive
 // groups of its item as fit, at most kMaxStageGroups: G = stage_groups(h, rhs).
