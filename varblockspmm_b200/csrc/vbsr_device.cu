@@ -543,10 +543,22 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
     const int64_t blocks = std::min<int64_t>(chunks, 148 * 8);
     bstack_kernel<<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, kp.rhs, p->d_bstack);
   }
+  // programmatic dependent launch: the SpMM's prologue overlaps the pre-pass (its feeders wait
+  // for the pre-pass with griddepcontrol.wait before the first copy)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(p->num_tasks));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = size_t(p->smem_bytes);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (p->flags & VBSR_PLAN_BOUNDS_CHECK)
-    spmm_tc_kernel<true><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
+    cudaLaunchKernelEx(&cfg, spmm_tc_kernel<true>, kp);
   else
-    spmm_tc_kernel<false><<<p->num_tasks, kTcThreads, p->smem_bytes, stream>>>(kp);
+    cudaLaunchKernelEx(&cfg, spmm_tc_kernel<false>, kp);
 }
 
 // Launch parameters of one execute: the plan's schedule and the caller's B and C.

@@ -203,6 +203,9 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   uint32_t ph = 0;
   uint32_t filled = 0, lastpar = 0;
   const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
+  // The SpMM is launched as a programmatic dependent of the B pre-pass, so that its prologue
+  // overlaps the pre-pass; the feeders are the only warps that read the pre-pass output.
+  griddep_wait();
   VBSR_PROF_T0(t_all);
   for (int kk = f; kk < nst; kk += kTcFeeders) {
     const Stage st = win.get();
@@ -499,6 +502,7 @@ constexpr int kBsGroups = 16;
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
                                                      int rhs, float* __restrict__ out) {
   __shared__ float4 buf[64 * kBsGroups * 2];  // [c][kg][2 x float4]: up to 32 KB
+  griddep_launch_dependents();  // the SpMM may start its prologue now (it waits before reading)
   const int M = stack_m(rhs), half = M / 8;
   const int lg_half = __ffs(half) - 1, lg_rhs = __ffs(rhs) - 1;
   const long long ngroups = K >> 3;
