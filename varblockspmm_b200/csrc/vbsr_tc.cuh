@@ -499,32 +499,33 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // each RHS column's 8 * kBsGroups consecutive values (coalesced), then writes the kBsGroups tiles
 // (contiguous) with 16-byte stores.
 constexpr int kBsGroups = 16;
+template <int RHS>
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
-                                                     int rhs, float* __restrict__ out) {
-  __shared__ float4 buf[64 * kBsGroups * 2];  // [c][kg][2 x float4]: up to 32 KB
+                                                     float* __restrict__ out) {
+  constexpr int M = stack_m(RHS), half = M / 8, per_col = 2 * kBsGroups;  // float4s per column run
+  __shared__ float4 buf[RHS * per_col];  // [c][kg][2 x float4]: up to 32 KB
   griddep_launch_dependents();  // the SpMM may start its prologue now (it waits before reading)
-  const int M = stack_m(rhs), half = M / 8;
-  const int lg_half = __ffs(half) - 1, lg_rhs = __ffs(rhs) - 1;
   const long long ngroups = K >> 3;
   for (long long kg0 = (long long)blockIdx.x * kBsGroups; kg0 < ngroups;
        kg0 += (long long)gridDim.x * kBsGroups) {
     const int ng = int(ngroups - kg0 < kBsGroups ? ngroups - kg0 : kBsGroups);
-    // read: float4 i of the block -> column c = i / (2 ng'), piece within the column's run
-    const int per_col = 2 * kBsGroups;  // float4s per column run (full block)
-    for (int i = threadIdx.x; i < rhs * per_col; i += blockDim.x) {
-      const int c = i / per_col, r = i - c * per_col;
-      if (r < 2 * ng)
-        buf[i] = __ldg(reinterpret_cast<const float4*>(B + (long long)c * K + 8 * kg0) + r);
+    // read: each RHS column's run of 8 * kBsGroups values (coalesced)
+    const float* src = B + 8 * kg0;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < RHS * per_col; i += blockDim.x) {
+      const int c = i / per_col, r = i % per_col;  // powers of two: shifts
+      if (r < 2 * ng) buf[i] = __ldg(reinterpret_cast<const float4*>(src + (long long)c * K) + r);
     }
     __syncthreads();
-    // write: tile g, row `row`, 16-byte piece `up` (2M float4s per tile)
+    // write: tile g, row `row`, 16-byte piece `up` (2M float4s per tile, contiguous)
     float4* dst = reinterpret_cast<float4*>(out) + kg0 * (2 * M);
+#pragma unroll 4
     for (int i = threadIdx.x; i < ng * 2 * M; i += blockDim.x) {
-      const int g = i / (2 * M), rem = i - g * 2 * M;
+      const int g = i / (2 * M), rem = i % (2 * M);
       const int row = rem >> 1, up = rem & 1;
-      const int q = row >> (lg_half + 1), jj = row & (2 * half - 1);
-      const int c = (q << lg_half) + (jj & (half - 1));
-      if (c < rhs) {
+      const int q = row / (2 * half), jj = row % (2 * half);
+      const int c = q * half + jj % half;
+      if (c < RHS) {
         const int u = up ^ ((row >> 2) & 1);
         float4 v = buf[c * per_col + 2 * g + u];
         if (jj >= half) v = lo_part4(v);
@@ -533,7 +534,6 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
     }
     __syncthreads();
   }
-  (void)lg_rhs;
 }
 
 template <bool CHECK>
