@@ -540,7 +540,7 @@ void free_plan(vbsr_plan* p) {
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
   const int64_t chunks = (kp.K / 8 + kBsGroups - 1) / kBsGroups;  // kBsGroups groups per block
   if (chunks > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
-    const int64_t blocks = std::min<int64_t>(chunks, 148 * 8);
+    const int64_t blocks = std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM);
     switch (kp.rhs) {
       case 8: bstack_kernel<8><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
       case 16: bstack_kernel<16><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;

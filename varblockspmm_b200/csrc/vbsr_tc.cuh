@@ -498,7 +498,13 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // them once (zero). A block transposes kBsGroups consecutive groups through shared memory: it reads
 // each RHS column's 8 * kBsGroups consecutive values (coalesced), then writes the kBsGroups tiles
 // (contiguous) with 16-byte stores.
-constexpr int kBsGroups = 16;
+#ifndef VBSR_BS_GROUPS
+#define VBSR_BS_GROUPS 8
+#endif
+#ifndef VBSR_BS_BLOCKS_PER_SM
+#define VBSR_BS_BLOCKS_PER_SM 8
+#endif
+constexpr int kBsGroups = VBSR_BS_GROUPS;
 template <int RHS>
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
                                                      float* __restrict__ out) {
