@@ -27,8 +27,8 @@
 //               the slot to the MMA warp;
 //   warps 8..11 MMA warps: stage k is issued by MMA warp k % 4, two MMAs per group into the warp's
 //               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 12..15 feeders: stage k is copied by feeder k % 4 with two cp.async.bulk copies per
-//               group (the group's A and its stack S);
+//   warps 12..15 feeders: stage k is copied by feeder k % 4 with cp.async.bulk: the stage's A in
+//               one copy, the stacks S in one copy per run of consecutive groups of a block;
 //   warps 16..19 epilogue warps: warp q reads TMEM quadrant q of every item's accumulators as soon
 //               as its MMAs are done and stores the item's C rows.
 // A single wait-and-release round on an mbarrier costs a warp ~150-200 cycles even when the
@@ -62,9 +62,9 @@ constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this m
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders + kTcEpiWarps;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
-// A slot (26 KB by default) holds one stage: for each of its groups g the N-side operand (h rows of raw A, 8
-// floats each, then the h rows of A_lo) at byte 64 h g, then the groups' operand stacks S (M rows
-// of 32 bytes each) from byte 64 h G (G = the stage's groups). A stage takes as many consecutive
+// A slot (26 KB by default) holds one stage of G groups: their raw A (h rows of 8 floats per group,
+// group after group) at byte 0, their A_lo at byte 32 h G, then their operand stacks S (M rows of
+// 32 bytes each) from byte 64 h G. A stage takes as many consecutive
 // groups of its item as fit, at most kMaxStageGroups: G = stage_groups(h, rhs).
 #ifndef VBSR_SLOT_KB
 #define VBSR_SLOT_KB 26
@@ -239,18 +239,24 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     } else {
       const uint32_t sp = slots + 4u * uint32_t(s * SF);
       const int M = stack_m(nw);
-      if (lane == 0) mbar_arrive_expect_tx(full_bar, uint32_t(groups * 32 * (h + M)));
+      // A: the stage's groups are contiguous in the device format: one copy. S: consecutive groups
+      // of one block have consecutive pre-pass tiles, so each run of them is one copy (the lane of
+      // a run's first group issues it).
+      const int col = lane < groups ? st.group_col(lane) : 0;
+      const int prev = __shfl_up_sync(0xffffffffu, col, 1);
+      const bool start = lane < groups && (lane == 0 || col != prev + 8);
+      const uint32_t starts = __ballot_sync(0xffffffffu, start);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full_bar, uint32_t(groups * 32 * (h + M)));
+        bulk_g2s(sp, p.values + a0, uint32_t(32 * h * groups), full_bar, pol_a);
+      }
       __syncwarp();
-      if (lane < groups) {
-        // group `lane`: h rows x 8 floats, contiguous in the device format
-        bulk_g2s(sp + 64u * h * lane, p.values + a0 + 8ll * h * lane, uint32_t(32 * h), full_bar,
-                 pol_a);
-      } else if (lane < 2 * groups) {
-        // group g's stack: M rows x 32 bytes of the pre-pass output for 8-column group col/8
-        const int g = lane - groups;
-        bulk_g2s(sp + uint32_t(slot_stack_bytes(h, groups) + 32 * M * g),
-                 p.bstack + (long long)(st.group_col(g) >> 3) * (M * 8), uint32_t(M * 32), full_bar,
-                 pol_b);
+      if (start) {
+        const uint32_t later = starts & ~((2u << lane) - 1u);
+        const int end = later ? __ffs(later) - 1 : groups;
+        bulk_g2s(sp + uint32_t(slot_stack_bytes(h, groups) + 32 * M * lane),
+                 p.bstack + (long long)(col >> 3) * (M * 8), uint32_t(M * 32 * (end - lane)),
+                 full_bar, pol_b);
       }
       filled |= 1u << s;
       lastpar = (lastpar & ~(1u << s)) | (ph << s);
@@ -327,21 +333,24 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   return true;
 }
 
-// A_lo of a whole stage at shared address sp: group g's A (2h float4s) at byte 64 h g, its A_lo
-// right after it. Lane l handles float4s l, l + 32, ... of each group; a group's four loads are in
-// flight before its stores.
+// A_lo of a whole stage at shared address sp: the stage's A (2h float4s per group, groups one after
+// another) at sp, its A_lo at the same offsets 32 h G bytes further. Eight loads per lane are in
+// flight before their stores.
 __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane) {
-  const int run = 2 * h;  // <= 128 float4s per group: at most 4 per lane
-  const uint32_t base = sp + 16u * lane, lo_off = 32u * h;
-  for (int g = 0; g < groups; ++g) {
-    const uint32_t a = base + 64u * h * g;
-    float4 x[4];
+  const int n = 2 * h * groups;  // float4s
+  const uint32_t lo = uint32_t(32 * h * groups);
+  for (int i0 = 0; i0 < n; i0 += 256) {
+    float4 x[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (32 * u + lane < run) x[u] = lds128(a + 512u * u);
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + 32 * u + lane;
+      if (i < n) x[u] = lds128(sp + 16u * i);
+    }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (32 * u + lane < run) sts128(a + lo_off + 512u * u, lo_part4(x[u]));
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + 32 * u + lane;
+      if (i < n) sts128(sp + lo + 16u * i, lo_part4(x[u]));
+    }
   }
 }
 
@@ -439,7 +448,6 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
     const int M = stack_m(it.nw()), h = it.h(), G = stage_groups(h, p.rhs);
     const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 64 * i);
     const uint32_t idesc = tf32_idesc(M, h);
-    const uint32_t lo_off = 32u * uint32_t(h);  // A_lo follows A (h rows of 32 bytes)
     uint32_t started = 0;
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
       const int groups = it.stage_groups(kk - int(it.k0), G);
@@ -463,7 +471,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
           const uint32_t ss = sa + uint32_t(slot_stack_bytes(h, groups));
           for (int g = 0; g < groups; ++g) {
             const uint64_t sdesc = sw32_desc(ss + 32u * M * g);
-            const uint32_t ag = sa + 64u * h * g;
+            const uint32_t ag = sa + 32u * h * g, lo_off = 32u * h * groups;  // A_lo region
             tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag), idesc, started);          // S x A
             tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag + lo_off), idesc, 1u);      // S x A_lo
             started = 1u;
