@@ -56,7 +56,7 @@ constexpr int kTcEpiWarps = 4;              // epilogue warps (warp q: TMEM quad
 constexpr int kTcMmaWarps = 4;              // MMA-issuing warps
 constexpr int kTcFeeders = 4;               // feeder warps
 #ifndef VBSR_PREFETCH
-#define VBSR_PREFETCH 4
+#define VBSR_PREFETCH 2
 #endif
 constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this many own stages ahead
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders + kTcEpiWarps;
