@@ -358,12 +358,19 @@ double item_cost(int h, int nw, int64_t sum_w, int nstages) {
 }
 
 cudaError_t set_kernel_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(spmm_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kSmemBudget + 1024);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(spmm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSmemBudget + 1024);
+  const int bytes = kSmemBudget + 1024;
+  cudaError_t e = cudaFuncSetAttribute(spmm_tc_kernel<false, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(spmm_tc_kernel<true, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(spmm_tc_kernel<false, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(spmm_tc_kernel<true, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  return e;
 }
 
 // Schedule for spmm_tc_kernel: one item per block row, one CTA per SM; items assigned to CTAs by
@@ -414,12 +421,12 @@ vbsr_status build_schedule(vbsr_plan* p) {
   items.reserve(size_t(R));
   std::vector<Task> h_tasks;
   const int slot = slot_floats(rhs);
-  // A multiple of kTcSplitWarps (and so of kTcMmaWarps and kTcFeeders): every slot then has one
-  // feeder, one split warp and one MMA warp, which pass through its uses in order, so a wait never
-  // meets a phase of another use.
+  // A multiple of every role's warp count: every slot then has one feeder, one split warp and one
+  // MMA warp, which pass through its uses in order, so a wait never meets a phase of another use.
   const int stages =
-      std::min(kMaxStages, kSmemBudget / (slot * 4)) / kTcSplitWarps * kTcSplitWarps;
-  if (stages < kTcSplitWarps) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
+      std::min(kMaxStages, (kSmemBudget - kSmemTailPad) / (slot * 4)) / kTcRingMultiple *
+      kTcRingMultiple;
+  if (stages < kTcRingMultiple) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
   const uint64_t nwc = uint64_t(stage::nw_code(rhs));
   for (int t = 0; t < ctas; ++t) {
     Task task{};
@@ -487,7 +494,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   }
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
-  p->smem_bytes = stages * slot * 4 + 1024;
+  p->smem_bytes = stages * slot * 4 + kSmemTailPad + 1024;  // + alignment of the ring
   p->num_tasks = int(h_tasks.size());
   p->stream_entries = int64_t(stream.size());
 
@@ -502,7 +509,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
   // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
-  p->bstack_floats = (d.K / 8) * int64_t(stack_m(rhs)) * 8;
+  p->bstack_floats = (d.K / 8) * int64_t(stack_rows(rhs)) * 8;
   if ((d.K / 8) * rhs >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "B too large for the pre-pass index range");
   VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
@@ -560,10 +567,11 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (p->flags & VBSR_PLAN_BOUNDS_CHECK)
-    cudaLaunchKernelEx(&cfg, spmm_tc_kernel<true>, kp);
+  const bool check = (p->flags & VBSR_PLAN_BOUNDS_CHECK) != 0;
+  if (row_stacked(kp.rhs))
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, true> : spmm_tc_kernel<false, true>, kp);
   else
-    cudaLaunchKernelEx(&cfg, spmm_tc_kernel<false>, kp);
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false> : spmm_tc_kernel<false, false>, kp);
 }
 
 // Launch parameters of one execute: the plan's schedule and the caller's B and C.
@@ -931,4 +939,12 @@ vbsr_status vbsr_fill_uniform_device(uint64_t seed, uint64_t stream, uint64_t fi
   return VBSR_OK;
 }
 
+#ifdef VBSR_TRACE
+// development builds only
+vbsr_status vbsr_debug_trace(long long* stages, long long* items) {
+  VBSR_CUDA(cudaMemcpyFromSymbol(stages, g_trace, sizeof(g_trace)));
+  VBSR_CUDA(cudaMemcpyFromSymbol(items, g_trace_items, sizeof(g_trace_items)));
+  return VBSR_OK;
+}
+#endif
 }  // extern "C"

@@ -162,6 +162,9 @@ __device__ __forceinline__ void record_status(int* status, int code, int info) {
 // mbarrier.try_wait suspends the warp in hardware while the phase is pending, so waiting warps do
 // not take issue slots from the warps that compute. Returns false if the CTA aborted or the wait
 // exceeded p.wait_limit SM clocks.
+#ifndef VBSR_WAIT_HINT_NS
+#define VBSR_WAIT_HINT_NS 20000u
+#endif
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const KernelParams& p,
                                            volatile int* abort_flag, int lane) {
 #ifdef VBSR_WAIT_LANE0
@@ -178,7 +181,13 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const 
   const long long t0 = clock64();
   while (true) {
     // suspended in hardware for up to ~20 us per probe, so a waiting warp issues few instructions
-    if (__all_sync(0xffffffffu, mbar_try_hint(bar, parity, 20000u))) return true;
+#if defined(VBSR_WAIT_TEST)
+    if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
+#elif defined(VBSR_WAIT_NOHINT)
+    if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
+#else
+    if (__all_sync(0xffffffffu, mbar_try_hint(bar, parity, VBSR_WAIT_HINT_NS))) return true;
+#endif
     int stop = 0;
     if (lane == 0) {
       if (*abort_flag) {

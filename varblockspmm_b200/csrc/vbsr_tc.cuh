@@ -51,10 +51,28 @@
 
 namespace vbsr_b200 {
 
-constexpr int kTcSplitWarps = 8;            // split warps (warp w reads TMEM quadrant w % 4)
-constexpr int kTcEpiWarps = 4;              // epilogue warps (warp q: TMEM quadrant q)
-constexpr int kTcMmaWarps = 4;              // MMA-issuing warps
-constexpr int kTcFeeders = 4;               // feeder warps
+#ifndef VBSR_EPI_SETS
+#define VBSR_EPI_SETS 2
+#endif
+#ifndef VBSR_SPLIT_WARPS
+#define VBSR_SPLIT_WARPS (VBSR_EPI_SETS == 2 ? 4 : 8)
+#endif
+#ifndef VBSR_FEEDERS
+#define VBSR_FEEDERS 4
+#endif
+constexpr int kTcSplitWarps = VBSR_SPLIT_WARPS;  // split warps
+// Epilogue warps: kEpiSets sets of four (warp q of a set reads TMEM quadrant q); set e stores the
+// items j with j % kEpiSets == e.
+constexpr int kEpiSets = VBSR_EPI_SETS;
+constexpr int kTcEpiWarps = 4 * kEpiSets;
+constexpr int kTcMmaWarps = 4;                   // MMA-issuing warps
+constexpr int kTcFeeders = VBSR_FEEDERS;         // feeder warps
+// The epilogue warps follow the others and must start at a multiple of 4 (a warp reaches the TMEM
+// lanes 32 (warp % 4) ... only); every slot count is a multiple of each role's warp count.
+static_assert((kTcSplitWarps + kTcMmaWarps + kTcFeeders) % 4 == 0, "epilogue warps misplaced");
+constexpr int kTcRingMultiple = kTcSplitWarps > kTcFeeders ? kTcSplitWarps : kTcFeeders;
+static_assert(kTcRingMultiple % kTcSplitWarps == 0 && kTcRingMultiple % kTcFeeders == 0 &&
+                  kTcRingMultiple % kTcMmaWarps == 0, "role warp counts must divide the ring");
 #ifndef VBSR_PREFETCH
 #define VBSR_PREFETCH 2
 #endif
@@ -62,9 +80,16 @@ constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this m
 constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders + kTcEpiWarps;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
-// A slot (26 KB by default) holds one stage of G groups: their raw A (h rows of 8 floats per group,
-// group after group) at byte 0, their A_lo at byte 32 h G, then their operand stacks S (M rows of
-// 32 bytes each) from byte 64 h G. A stage takes as many consecutive
+// RHS widths up to 32 use the row-stacked form (one MMA per group, the operand stack S on the N
+// side); width 64 the column-stacked form (two MMAs per group, S on the M side). S has
+// stack_rows(rhs) rows of 32 bytes per 8-column group.
+__host__ __device__ constexpr bool row_stacked(int rhs) { return rhs <= 32; }
+__host__ __device__ constexpr int stack_rows(int rhs) { return row_stacked(rhs) ? 2 * rhs : stack_m(rhs); }
+__host__ __device__ constexpr int stack_tile_bytes(int rhs) { return 32 * stack_rows(rhs); }
+// A slot (26 KB by default) holds one stage of G groups: their A values and A_lo parts in the first
+// 64 h G bytes (column-stacked form: raw A of group after group, then the A_lo parts at byte
+// 32 h G; row-stacked form: per group, 8-row blocks of raw A and of A_lo alternating), then their
+// operand stacks S (stack_tile_bytes each) from byte 64 h G. A stage takes as many consecutive
 // groups of its item as fit, at most kMaxStageGroups: G = stage_groups(h, rhs).
 #ifndef VBSR_SLOT_KB
 #define VBSR_SLOT_KB 26
@@ -76,11 +101,18 @@ constexpr int kSlotBytes = VBSR_SLOT_KB * 1024;
 constexpr int kMaxStageGroups = VBSR_MAX_GROUPS;
 __host__ __device__ constexpr int slot_floats(int rhs) { return (void)rhs, kSlotBytes / 4; }
 __host__ __device__ constexpr int stage_groups(int h, int rhs) {
-  return kSlotBytes / (64 * h + 32 * stack_m(rhs)) < kMaxStageGroups
-             ? kSlotBytes / (64 * h + 32 * stack_m(rhs))
+  return kSlotBytes / (64 * h + stack_tile_bytes(rhs)) < kMaxStageGroups
+             ? kSlotBytes / (64 * h + stack_tile_bytes(rhs))
              : kMaxStageGroups;
 }
 __host__ __device__ constexpr int slot_stack_bytes(int h, int groups) { return 64 * h * groups; }
+// The row-stacked MMA reads M = 64 or 128 rows from a group's first byte, up to 1.5 KB beyond the
+// group's 64 h bytes (rows it does not use); the shared memory allocation ends with this pad.
+constexpr int kSmemTailPad = 2048;
+#ifndef VBSR_TR_M64_MAX_H
+#define VBSR_TR_M64_MAX_H 32
+#endif
+constexpr int kTrM64MaxH = VBSR_TR_M64_MAX_H;  // row-stacked items with h <= this use M = 64
 // TMEM: 2 accumulator buffers (items alternate) x 4 partials (one per MMA warp) x 64 columns.
 constexpr int kTmemAlloc = 512;
 
@@ -189,6 +221,24 @@ struct CtaBars {
 #define VBSR_PROF_T0(v)
 #define VBSR_PROF_ADD(p, slot, t0) do { } while (0)
 #endif
+#ifdef VBSR_TRACE
+// development builds only: per-stage / per-item timestamps of one CTA
+__device__ long long g_trace[4096 * 8];
+__device__ long long g_trace_items[1024 * 4];
+#define VBSR_TRACE_ST(k, e)                                                                      \
+  do {                                                                                           \
+    if (blockIdx.x == VBSR_TRACE && (threadIdx.x & 31) == 0 && (k) < 4096)                       \
+      g_trace[(k) * 8 + (e)] = clock64();                                                        \
+  } while (0)
+#define VBSR_TRACE_IT(j, e)                                                                      \
+  do {                                                                                           \
+    if (blockIdx.x == VBSR_TRACE && (threadIdx.x & 31) == 0 && (j) < 1024)                       \
+      g_trace_items[(j) * 4 + (e)] = clock64();                                                  \
+  } while (0)
+#else
+#define VBSR_TRACE_ST(k, e) do { } while (0)
+#define VBSR_TRACE_IT(j, e) do { } while (0)
+#endif
 
 // Feeder warp f: fills the slots of the stages k with k % kTcFeeders == f, each once the MMAs of
 // the slot's previous stage have completed.
@@ -218,11 +268,30 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     }
     win.advance(lane);
     const uint32_t full_bar = cb.full0 + 8u * s;
+    // Everything the copies need is worked out before the wait, so that only their issue is on the
+    // slot's critical path. A: the stage's groups are contiguous in the device format: one copy.
+    // S: consecutive groups of one block have consecutive pre-pass tiles, so each run of them is
+    // one copy, issued by the lane of the run's first group.
+    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.groups();
+    const long long a0 = st.a_start();
+    const uint32_t sp = slots + 4u * uint32_t(s * SF);
+    const int T = stack_tile_bytes(p.rhs);
+    const int col = lane < groups ? st.group_col(lane) : 0;
+    const int prev = __shfl_up_sync(0xffffffffu, col, 1);
+    const bool start = lane < groups && (lane == 0 || col != prev + 8);
+    const uint32_t starts = __ballot_sync(0xffffffffu, start);
+    const uint32_t later = starts & ~((2u << lane) - 1u);
+    const int end = later ? __ffs(later) - 1 : groups;
+    const uint32_t s_dst = sp + uint32_t(slot_stack_bytes(h, groups) + T * lane);
+    const float* s_src = p.bstack + (long long)(col >> 3) * (T / 4);
+    const uint32_t s_bytes = uint32_t(T * (end - lane));
+    const uint32_t tx = uint32_t(groups * (32 * h + T)), a_bytes = uint32_t(32 * h * groups);
+    const float* a_src = p.values + a0;
+    asm volatile("" ::"r"(s_dst), "l"(s_src), "r"(s_bytes), "r"(tx), "r"(a_bytes), "l"(a_src));
     VBSR_PROF_T0(t_w);
     if (!wait_phase(cb.empty0 + 8u * s, ph ^ 1u, p, abort_flag, lane)) break;
     VBSR_PROF_ADD(p, 7, t_w);
-    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.groups();
-    const long long a0 = st.a_start();
+    VBSR_TRACE_ST(kk, 0);
     bool ok = true;
     if (CHECK) {
       ok = a0 + 8ll * h * groups <= p.nvalues && n0 == 0 && nw == p.rhs &&
@@ -237,28 +306,15 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
         mbar_arrive(full_bar);  // release the split warp without touching memory
       }
     } else {
-      const uint32_t sp = slots + 4u * uint32_t(s * SF);
-      const int M = stack_m(nw);
-      // A: the stage's groups are contiguous in the device format: one copy. S: consecutive groups
-      // of one block have consecutive pre-pass tiles, so each run of them is one copy (the lane of
-      // a run's first group issues it).
-      const int col = lane < groups ? st.group_col(lane) : 0;
-      const int prev = __shfl_up_sync(0xffffffffu, col, 1);
-      const bool start = lane < groups && (lane == 0 || col != prev + 8);
-      const uint32_t starts = __ballot_sync(0xffffffffu, start);
+      VBSR_TRACE_ST(kk, 7);
       if (lane == 0) {
-        mbar_arrive_expect_tx(full_bar, uint32_t(groups * 32 * (h + M)));
-        bulk_g2s(sp, p.values + a0, uint32_t(32 * h * groups), full_bar, pol_a);
+        mbar_arrive_expect_tx(full_bar, tx);
+        bulk_g2s(sp, a_src, a_bytes, full_bar, pol_a);
       }
       __syncwarp();
-      if (start) {
-        const uint32_t later = starts & ~((2u << lane) - 1u);
-        const int end = later ? __ffs(later) - 1 : groups;
-        bulk_g2s(sp + uint32_t(slot_stack_bytes(h, groups) + 32 * M * lane),
-                 p.bstack + (long long)(col >> 3) * (M * 8), uint32_t(M * 32 * (end - lane)),
-                 full_bar, pol_b);
-      }
+      if (start) bulk_g2s(s_dst, s_src, s_bytes, full_bar, pol_b);
       filled |= 1u << s;
+      VBSR_TRACE_ST(kk, 1);
       lastpar = (lastpar & ~(1u << s)) | (ph << s);
     }
     if ((s += kTcFeeders) >= D) {
@@ -280,7 +336,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   }
 }
 
-// Epilogue of one item: D -> C, by split warp w (TMEM quadrant w). Partial i (64 columns after
+// Epilogue of one item: D -> C, by epilogue warp w (TMEM quadrant w). Partial i (64 columns after
 // partial 0) holds the stages issued by MMA warp i; only partials that received a stage are read.
 // Within a partial, column r is row r of the tile. Lane j < half of quadrant w holds hi of RHS
 // column n0 + half*w + j, lane half + j its lo.
@@ -333,9 +389,108 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   return true;
 }
 
-// A_lo of a whole stage at shared address sp: the stage's A (2h float4s per group, groups one after
-// another) at sp, its A_lo at the same offsets 32 h G bytes further. Eight loads per lane are in
-// flight before their stores.
+// Row-stacked epilogue of one item, by epilogue warp w (TMEM quadrant w). Partial i (64 columns
+// after partial 0) holds the stages issued by MMA warp i; only partials that received a stage are
+// read. Accumulator row r is row r of the groups' interleaved [A | A_lo] operand, column c < rhs its
+// product with raw B of RHS column c and column rhs + c with that column's lo part. Quadrant w
+// holds, for M = 64 (h <= 32), tile rows 8w + j in lanes j (A) and 8 + j (A_lo); for M = 128, tile
+// rows 16w + j and 16w + 8 + j in lanes j, 16 + j (A) and 8 + j, 24 + j (A_lo). A lane adds its
+// hi and lo columns, then the A_lo lane's sum with one shuffle, and stores its row of C.
+template <bool CHECK>
+__device__ __forceinline__ bool tc_epilogue_rows(const KernelParams& p, const CtaBars& cb, int buf,
+                                                 uint32_t parity, uint32_t tmem_buf, int w,
+                                                 int lane, const Item& it,
+                                                 volatile int* abort_flag) {
+  VBSR_PROF_T0(t_w);
+  if (!wait_phase(cb.acc0 + 8u * buf, parity, p, abort_flag, lane)) return false;
+  VBSR_PROF_ADD(p, 4, t_w);
+  tc_fence_after();
+  const int h = it.h(), R = p.rhs;
+  uint32_t use = 0;  // bit i: partial i received a stage of the item
+  if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH))
+    for (uint32_t i = 0; i < kTcMmaWarps && i < it.n; ++i) use |= 1u << ((it.k0 + i) & 3u);
+  const bool m64 = h <= kTrM64MaxH;
+  const int row0 = m64 ? 8 * w : 16 * w;  // the quadrant's first tile row
+  if (row0 < h) {
+    const bool bad = CHECK && ((long long)it.c_row + h > p.M || it.n0() + it.nw() > p.rhs);
+    if (CHECK && w == 0 && lane == 0 && bad) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(it.c_row));
+    const int n = row0 + (lane & 7) + (m64 ? 0 : 8 * (lane >> 4));
+    const bool store = (lane & 8) == 0 && (!m64 || lane < 16) && n < h && !bad;
+    float* dst = p.C + (long long)it.c_row + n;  // RHS column c at dst + c * M
+    const uint32_t taddr = tmem_buf + (uint32_t(32 * w) << 16);
+    for (int c0 = 0; c0 < R; c0 += 8) {
+      float v[4][8], a[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (use & (1u << i)) tc_ld8_nowait(taddr + uint32_t(64 * i + c0), v[i]);
+      tc_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        a[e] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (use & (1u << i)) a[e] += v[i][e];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (use & (1u << i)) tc_ld8_nowait(taddr + uint32_t(64 * i + R + c0), v[i]);
+      tc_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (use & (1u << i)) a[e] += v[i][e];
+        a[e] += __shfl_xor_sync(0xffffffffu, a[e], 8);
+      }
+      if (store) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dst[(long long)(c0 + e) * p.M] = a[e];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(cb.accfree0 + 8u * buf);  // this warp is done with the buffer
+  return true;
+}
+
+#ifndef VBSR_SPLIT_PASS
+#define VBSR_SPLIT_PASS 16
+#endif
+// Row-stacked form: the stage's A arrives as U = h G / 8 blocks of 8 rows (256 bytes), block u at
+// byte 256 u; it is spread in place so that block u sits at byte 512 u followed by its A_lo block.
+// Block u's destination covers the sources of blocks 2u and 2u + 1 only, so passes over the
+// blocks from the last one down, each loading all its blocks before storing any, never overwrite a
+// block that is still to be read. Block 0 stays where it is. The 32-byte swizzle is a function of
+// the address bits below 256, which the move preserves.
+__device__ __forceinline__ void split_stage_rows(uint32_t sp, int groups, int h, int lane) {
+  const int units = (h >> 3) * groups;
+  constexpr int kPassUnits = VBSR_SPLIT_PASS;  // blocks per pass: kPassUnits / 2 float4s per lane
+  for (int top = units; top > 0; top -= kPassUnits) {
+    const int u0 = top > kPassUnits ? top - kPassUnits : 0;
+    float4 x[kPassUnits / 2];
+#pragma unroll
+    for (int v = 0; v < kPassUnits / 2; ++v) {
+      const int i = 32 * v + lane;  // float4 i of the pass: block u0 + i / 16, piece i % 16
+      if (u0 + (i >> 4) < top) x[v] = lds128(sp + 256u * uint32_t(u0) + 16u * uint32_t(i));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int v = 0; v < kPassUnits / 2; ++v) {
+      const int i = 32 * v + lane, u = u0 + (i >> 4);
+      if (u < top) {
+        const uint32_t d = sp + 512u * uint32_t(u) + 16u * uint32_t(i & 15);
+        if (u > 0) sts128(d, x[v]);
+        sts128(d + 256u, lo_part4(x[v]));
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Column-stacked form: A_lo of a whole stage at shared address sp: the stage's A (2h float4s per
+// group, groups one after another) at sp, its A_lo at the same offsets 32 h G bytes further. Eight
+// loads per lane are in flight before their stores.
 __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane) {
   const int n = 2 * h * groups;  // float4s
   const uint32_t lo = uint32_t(32 * h * groups);
@@ -354,8 +509,9 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int 
   }
 }
 
-// Split warp w (0..7): forms the lo parts of the stages k with k % 8 == w (slot w).
-template <bool CHECK>
+// Split warp w: forms the lo parts of the stages k with k % kTcSplitWarps == w (slots w, w +
+// kTcSplitWarps, ...).
+template <bool CHECK, bool TR>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
@@ -386,13 +542,19 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
         break;
       }
       VBSR_PROF_ADD(p, 1, t_w);
+      VBSR_TRACE_ST(kk, 2);
       VBSR_PROF_T0(t_s);
       if (math) {
-        split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
+        if (TR)
+          split_stage_rows(slots + 4u * uint32_t(s * SF), groups, h, lane);
+        else
+          split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
+        VBSR_TRACE_ST(kk, 6);
         fence_proxy_async_smem();
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(cb.split0 + 8u * s);
+      VBSR_TRACE_ST(kk, 3);
       VBSR_PROF_ADD(p, 2, t_s);
     }
   }
@@ -400,27 +562,32 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
 }
 
 // Epilogue warp q (0..3, TMEM quadrant q): stores every item's result as soon as its MMAs are done.
-template <bool CHECK>
+template <bool CHECK, bool TR>
 __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBars& cb,
-                            uint32_t tmem_base, int q, int lane, volatile int* abort_flag) {
+                            uint32_t tmem_base, int q, int set, int lane,
+                            volatile int* abort_flag) {
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
   VBSR_PROF_T0(t_all);
   for (int j = 0; !iw.done(); ++j) {
     const Item it = iw.get();
     iw.advance(lane);
+    if (kEpiSets > 1 && j % kEpiSets != set) continue;  // another set's item
     VBSR_PROF_T0(t_e);
-    if (!tc_epilogue<CHECK>(p, cb, j & 1, uint32_t((j >> 1) & 1),
-                            tmem_base + uint32_t(256 * (j & 1)), q, lane, it, abort_flag))
+    if (q == 0) VBSR_TRACE_IT(j, 0);
+    const uint32_t par = uint32_t((j >> 1) & 1), tbuf = tmem_base + uint32_t(256 * (j & 1));
+    if (!(TR ? tc_epilogue_rows<CHECK>(p, cb, j & 1, par, tbuf, q, lane, it, abort_flag)
+             : tc_epilogue<CHECK>(p, cb, j & 1, par, tbuf, q, lane, it, abort_flag)))
       break;
     VBSR_PROF_ADD(p, 8, t_e);
+    if (q == 0) VBSR_TRACE_IT(j, 1);
   }
   VBSR_PROF_ADD(p, 11, t_all);
 }
 
 // MMA warp i (0..3): issues the stages k with k % 4 == i, two MMAs per group (S x A, S x A_lo) into its partial
 // accumulator (TMEM columns 256 * buffer + 64 * i).
-template <bool CHECK>
+template <bool CHECK, bool TR>
 __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
                             const CtaBars& cb, uint32_t tmem_base, int i, int lane,
                             volatile int* abort_flag) {
@@ -444,10 +611,14 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
                               abort_flag, lane))
       break;
     VBSR_PROF_ADD(p, 5, t_f);
+    if (i == 0) VBSR_TRACE_IT(j, 2);
     tc_fence_after();
     const int M = stack_m(it.nw()), h = it.h(), G = stage_groups(h, p.rhs);
+    const uint32_t T = uint32_t(stack_tile_bytes(p.rhs));
     const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 64 * i);
-    const uint32_t idesc = tf32_idesc(M, h);
+    // row-stacked: M = the group's interleaved A / A_lo rows (64 covers h <= 32), N = S's 2 rhs
+    // rows; column-stacked: M = S's rows, N = the group's h rows of A (then of A_lo)
+    const uint32_t idesc = TR ? tf32_idesc(h <= kTrM64MaxH ? 64 : 128, 2 * p.rhs) : tf32_idesc(M, h);
     uint32_t started = 0;
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
       const int groups = it.stage_groups(kk - int(it.k0), G);
@@ -463,24 +634,34 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
         break;
       }
       VBSR_PROF_ADD(p, 3, t_w);
+      VBSR_TRACE_ST(kk, 4);
       VBSR_PROF_T0(t_i);
       if (lane == 0) {
         if (math) {
           tc_fence_after();
           const uint32_t sa = slots + 4u * uint32_t(s * SF);
           const uint32_t ss = sa + uint32_t(slot_stack_bytes(h, groups));
-          for (int g = 0; g < groups; ++g) {
-            const uint64_t sdesc = sw32_desc(ss + 32u * M * g);
-            const uint32_t ag = sa + 32u * h * g, lo_off = 32u * h * groups;  // A_lo region
-            tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag), idesc, started);          // S x A
-            tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag + lo_off), idesc, 1u);      // S x A_lo
-            started = 1u;
+          if (TR) {
+            for (int g = 0; g < groups; ++g) {  // [A | A_lo] x S^T
+              tc_mma_tf32(tmem_d, sw32_desc(sa + 64u * h * g), sw32_desc(ss + T * g), idesc,
+                          started);
+              started = 1u;
+            }
+          } else {
+            for (int g = 0; g < groups; ++g) {
+              const uint64_t sdesc = sw32_desc(ss + T * g);
+              const uint32_t ag = sa + 32u * h * g, lo_off = 32u * h * groups;  // A_lo region
+              tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag), idesc, started);          // S x A
+              tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag + lo_off), idesc, 1u);      // S x A_lo
+              started = 1u;
+            }
           }
         }
         tc_commit(cb.empty0 + 8u * s);  // the slot is free once these MMAs have read it
       }
       __syncwarp();
       VBSR_PROF_ADD(p, 10, t_i);
+      VBSR_TRACE_ST(kk, 5);
     }
     if (!ok) break;
     if (lane == 0) tc_commit(cb.acc0 + 8u * buf);  // this warp's part of the item is issued
@@ -499,13 +680,13 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 }
 
 // Pre-pass: the operand stacks S of all 8-column groups of B (K x rhs, column-major), one tile of
-// M rows x 8 floats per group (kg = k / 8) in the layout the MMA reads: row 2*half*q + j holds the
-// 8 values of RHS column c = half*q + j (raw, i.e. hi), row 2*half*q + half + j their lo parts,
-// and the two 16-byte halves of row r are exchanged when bit 2 of r is set (32-byte swizzle).
-// Rows of columns >= rhs (only for rhs < 32, where M = 64 exceeds 2 rhs) stay as the plan wrote
-// them once (zero). A block transposes kBsGroups consecutive groups through shared memory: it reads
-// each RHS column's 8 * kBsGroups consecutive values (coalesced), then writes the kBsGroups tiles
-// (contiguous) with 16-byte stores.
+// stack_rows(rhs) rows x 8 floats per group (kg = k / 8) in the layout the MMA reads. Row-stacked
+// form (rhs <= 32): row c holds the 8 values of RHS column c (raw, i.e. hi), row rhs + c their lo
+// parts. Column-stacked form (rhs = 64, M = 128, half = 16): row 2*half*q + j holds column
+// c = half*q + j, row 2*half*q + half + j its lo parts. The two 16-byte halves of row r are
+// exchanged when bit 2 of r is set (32-byte swizzle). A block transposes kBsGroups consecutive
+// groups through shared memory: it reads each RHS column's 8 * kBsGroups consecutive values
+// (coalesced), then writes the kBsGroups tiles (contiguous) with 16-byte stores.
 #ifndef VBSR_BS_GROUPS
 #define VBSR_BS_GROUPS 8
 #endif
@@ -516,7 +697,8 @@ constexpr int kBsGroups = VBSR_BS_GROUPS;
 template <int RHS>
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
                                                      float* __restrict__ out) {
-  constexpr int M = stack_m(RHS), half = M / 8, per_col = 2 * kBsGroups;  // float4s per column run
+  constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS);
+  constexpr int per_col = 2 * kBsGroups;  // float4s per column run
   __shared__ float4 buf[RHS * per_col];  // [c][kg][2 x float4]: up to 32 KB
   griddep_launch_dependents();  // the SpMM may start its prologue now (it waits before reading)
   const long long ngroups = K >> 3;
@@ -532,17 +714,25 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
     }
     __syncthreads();
     // write: tile g, row `row`, 16-byte piece `up` (2M float4s per tile, contiguous)
-    float4* dst = reinterpret_cast<float4*>(out) + kg0 * (2 * M);
+    float4* dst = reinterpret_cast<float4*>(out) + kg0 * (2 * rows);
 #pragma unroll 4
-    for (int i = threadIdx.x; i < ng * 2 * M; i += blockDim.x) {
-      const int g = i / (2 * M), rem = i % (2 * M);
+    for (int i = threadIdx.x; i < ng * 2 * rows; i += blockDim.x) {
+      const int g = i / (2 * rows), rem = i % (2 * rows);
       const int row = rem >> 1, up = rem & 1;
-      const int q = row / (2 * half), jj = row % (2 * half);
-      const int c = q * half + jj % half;
+      int c;
+      bool lo;
+      if (row_stacked(RHS)) {  // rows c: raw B of column c; rows RHS + c: its lo part
+        c = row % RHS;
+        lo = row >= RHS;
+      } else {  // per quadrant q: rows of hi, then rows of lo, of columns half*q ...
+        const int q = row / (2 * half), jj = row % (2 * half);
+        c = q * half + jj % half;
+        lo = jj >= half;
+      }
       if (c < RHS) {
         const int u = up ^ ((row >> 2) & 1);
         float4 v = buf[c * per_col + 2 * g + u];
-        if (jj >= half) v = lo_part4(v);
+        if (lo) v = lo_part4(v);
         dst[i] = v;
       }
     }
@@ -550,7 +740,7 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
   }
 }
 
-template <bool CHECK>
+template <bool CHECK, bool TR>
 __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t slots = (smem_addr(smem_raw) + 1023u) & ~1023u;  // 1024-aligned ring
@@ -574,7 +764,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_addr(&accbars[0][b]), uint32_t(kTcMmaWarps));
-      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcEpiWarps));
+      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcEpiWarps / kEpiSets));
     }
     for (int i = 0; i < kTcMmaWarps; ++i) mbar_init(smem_addr(&drainbars[i]), 1u);
 
@@ -594,13 +784,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   cb.drain0 = smem_addr(&drainbars[0]);
 
   if (warp < kTcSplitWarps)
-    tc_split_warp<CHECK>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
+    tc_split_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < kTcSplitWarps + kTcMmaWarps)
-    tc_mma_warp<CHECK>(p, task, slots, cb, tmem_base, warp - kTcSplitWarps, lane, &abort_flag);
+    tc_mma_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp - kTcSplitWarps, lane, &abort_flag);
   else if (warp < kTcSplitWarps + kTcMmaWarps + kTcFeeders)
     tc_feeder<CHECK>(p, task, slots, cb, warp - kTcSplitWarps - kTcMmaWarps, lane, &abort_flag);
-  else  // the epilogue warps are warps 16..19: TMEM quadrant warp % 4 = warp - 16
-    tc_epi_warp<CHECK>(p, task, cb, tmem_base, warp & 3, lane, &abort_flag);
+  else  // the epilogue warps: TMEM quadrant warp % 4
+    tc_epi_warp<CHECK, TR>(p, task, cb, tmem_base, warp & 3,
+                           (warp - kTcSplitWarps - kTcMmaWarps - kTcFeeders) >> 2, lane, &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
