@@ -1,6 +1,6 @@
 """bench.py — VBSR SpMM benchmark on B200 (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload large|headline|wide|small]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload large|headline|wide|small|large16k]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1, NCCL)
     python bench.py --impl reference ...                  (the reference's CPU path, rank 0 only)
 
@@ -44,6 +44,9 @@ WORKLOADS = {
     "wide": (1024, 16, 3, False, 64,
              "BASELINE config 2: 1024 block rows/cols, bimodal 8/64, degree 16, random, RHS 64, "
              "seed 1"),
+    "large16k": (16384, 16, 2, False, 64,
+                 "profiling case: BASELINE config 5's generator settings (high-variance, degree 16, "
+                 "random, RHS 64, seed 1) at 16384 block rows, A 1.4 GB, B 151 MB (above L2)"),
     "small": (256, 4, 0, True, 8,
               "BASELINE config 1: 256 block rows/cols, uniform {8..64}, degree 4, local, RHS 8, "
               "seed 1"),

@@ -1,44 +1,48 @@
 // vbsr_tc.cuh — the sm_100a SpMM kernel on 5th-generation tensor cores (tcgen05, TMEM).
 //
-// Per work item (one block row i: an h x nw tile of C) the kernel computes the transposed product
-//     D (M x h) = sum over the row's 8-column groups g of  S_g (M x 8) * (A_g + A_g,lo)^T
-// with tcgen05.mma kind::tf32 (K = 8) and an fp32 accumulator in tensor memory.
+// Per work item (one block row i: an h x nw tile of C) the kernel sums over the row's 8-column
+// groups g with tcgen05.mma kind::tf32 (K = 8) into fp32 accumulators in tensor memory, in one of
+// two forms (template parameter TR):
+//   row-stacked (rhs <= 32):    D (M x 2 rhs) = sum_g [A_g ; A_g,lo] (M x 8) * S_g^T, one MMA per
+//                               group, M = 64 for h <= 32 and 128 otherwise;
+//   column-stacked (rhs = 64):  D (128 x h) = sum_g S_g (128 x 8) * (A_g + A_g,lo)^T, two MMAs per
+//                               group (raw A, then A_lo, on the N side).
+// S_g is the operand stack of group g of B: rows of raw B (hi) and of their lo parts.
 //
-// FP32 accuracy (3xTF32 in two MMAs per group). The tensor core reads an fp32 operand as tf32 by
-// ignoring its low 13 mantissa bits (truncation), so for x = hi + lo with hi = trunc_tf32(x) the
-// raw value already acts as hi and only lo = x - hi has to be formed (exactly, in fp32). The M side
-// of the MMA is the operand stack S: for every RHS column c the raw B value (hi) and its lo part
-// sit in two rows of S. The N side is the group's h rows of raw A, then (second MMA, same
-// accumulator) its h rows of A_lo. The two MMAs produce all four products B_hi*A_hi, B_lo*A_hi,
-// B_hi*A_lo, B_lo*A_lo (the last one is below the tolerance but harmless), and the epilogue adds,
-// for every C element, the two S rows of its column. M = 64 for nw <= 32 and M = 128 for nw = 64.
+// FP32 accuracy (3xTF32). The tensor core reads an fp32 operand as tf32 by ignoring its low 13
+// mantissa bits (truncation), so for x = hi + lo with hi = trunc_tf32(x) the raw value already
+// acts as hi and only lo = x - hi has to be formed (exactly, in fp32). Both forms produce the four
+// products A_hi*B_hi, A_hi*B_lo, A_lo*B_hi and A_lo*B_lo (the last one below the tolerance but
+// harmless), and the epilogue adds, for every C element, the accumulator entries that hold them.
 //
 // The stacks of all 8-column groups of B are formed once per execute by a small pre-pass
 // (bstack_kernel) in global memory, already in the MMA's K-major, 32-byte-swizzled layout, so a
-// group's S arrives with one contiguous bulk copy. S is built per quadrant q (32 TMEM lanes, the
-// part of the accumulator one warp may read): with half = M / 8 columns per quadrant, S rows
-// 2*half*q + j and 2*half*q + half + j hold hi and lo of column c = half*q + j, and in TMEM (M = 64:
-// row r lives in lane r % 16 + 32 * (r / 16); M = 128: lane r) they land in lanes j and half + j of
-// quadrant q, so a warp adds them with one shuffle.
+// run of a block's groups arrives with one contiguous bulk copy. In the row-stacked form the A and
+// A_lo rows of a group alternate in 8-row blocks, so a C row's A and A_lo accumulator rows sit in
+// one TMEM quadrant, 8 lanes apart. In the column-stacked form S is built per quadrant q (32 TMEM
+// lanes): with half = 16 columns per quadrant, S rows 32q + j and 32q + 16 + j hold hi and lo of
+// column 16q + j, so they land in lanes j and 16 + j of quadrant q. Either way a warp adds the
+// pair with one shuffle.
 //
 // CTA = twenty warps, one CTA per SM:
-//   warps 0..7  split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 8, which
-//               forms A_lo next to each group's A, fences the writes for the async proxy and hands
-//               the slot to the MMA warp;
-//   warps 8..11 MMA warps: stage k is issued by MMA warp k % 4, two MMAs per group into the warp's
-//               own accumulator, and the slot is released with tcgen05.commit;
-//   warps 12..15 feeders: stage k is copied by feeder k % 4 with cp.async.bulk: the stage's A in
-//               one copy, the stacks S in one copy per run of consecutive groups of a block;
-//   warps 16..19 epilogue warps: warp q reads TMEM quadrant q of every item's accumulators as soon
-//               as its MMAs are done and stores the item's C rows.
+//   warps 0..3   split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4,
+//                which forms A_lo (row-stacked: spreads the stage's A in place into alternating
+//                A / A_lo blocks), fences the writes for the async proxy and hands the slot on;
+//   warps 4..7   MMA warps: stage k is issued by MMA warp k % 4 into the warp's own accumulator,
+//                and the slot is released with tcgen05.commit;
+//   warps 8..11  feeders: stage k is copied by feeder k % 4 with cp.async.bulk: the stage's A in
+//                one copy, the stacks S in one copy per run of consecutive groups of a block;
+//   warps 12..19 epilogue warps, two sets of four: set e stores the items j with j % 2 == e
+//                (TMEM buffer e); warp q of a set reads TMEM quadrant q as soon as the item's
+//                MMAs are done and stores its C rows.
 // A single wait-and-release round on an mbarrier costs a warp ~150-200 cycles even when the
 // barrier has already completed (and a wait next to MMA issue as much), which is why every role
-// is spread over several warps. The ring has D
-// slots, D a multiple of 8, stage k uses slot k % D: each slot then has one feeder, one split
-// warp and one MMA warp, all passing through its uses in order. Every warp walks the CTA's list of
-// stage descriptors (compiled by the planner; vbsr_internal.h). Every wait is bounded (see
-// wait_phase); after an abort the feeders wait for their copies and the MMA warps for their MMAs
-// before the CTA releases its tensor memory.
+// is spread over several warps. The ring has D slots, D a multiple of every role's warp count,
+// stage k uses slot k % D: each slot then has one feeder, one split warp and one MMA warp, all
+// passing through its uses in order. Every warp walks the CTA's list of stage descriptors
+// (compiled by the planner; vbsr_internal.h). Every wait is bounded (see wait_phase); after an
+// abort the feeders wait for their copies and the MMA warps for their MMAs before the CTA releases
+// its tensor memory.
 #pragma once
 #include <cuda.h>
 
@@ -561,7 +565,8 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   VBSR_PROF_ADD(p, 0, t_all);
 }
 
-// Epilogue warp q (0..3, TMEM quadrant q): stores every item's result as soon as its MMAs are done.
+// Epilogue warp q (TMEM quadrant q) of epilogue set `set`: stores the results of the set's items as
+// soon as their MMAs are done.
 template <bool CHECK, bool TR>
 __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBars& cb,
                             uint32_t tmem_base, int q, int set, int lane,
@@ -585,8 +590,9 @@ __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBa
   VBSR_PROF_ADD(p, 11, t_all);
 }
 
-// MMA warp i (0..3): issues the stages k with k % 4 == i, two MMAs per group (S x A, S x A_lo) into its partial
-// accumulator (TMEM columns 256 * buffer + 64 * i).
+// MMA warp i (0..3): issues the stages k with k % 4 == i into its partial accumulator (TMEM columns
+// 256 * buffer + 64 * i): one MMA per group in the row-stacked form, two (S x A, S x A_lo) in the
+// column-stacked form.
 template <bool CHECK, bool TR>
 __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
                             const CtaBars& cb, uint32_t tmem_base, int i, int lane,
