@@ -545,7 +545,8 @@ void free_plan(vbsr_plan* p) {
 
 // One execute: the B pre-pass, then the SpMM kernel, both on `stream`.
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
-  const int64_t chunks = (kp.K / 8 + kBsGroups - 1) / kBsGroups;  // kBsGroups groups per block
+  const int64_t bsg = bs_groups(kp.rhs);
+  const int64_t chunks = (kp.K / 8 + bsg - 1) / bsg;  // bs_groups(rhs) groups per block iteration
   if (chunks > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
     const int64_t blocks = std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM);
     switch (kp.rhs) {

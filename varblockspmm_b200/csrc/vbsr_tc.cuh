@@ -699,11 +699,20 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 #ifndef VBSR_BS_BLOCKS_PER_SM
 #define VBSR_BS_BLOCKS_PER_SM 8
 #endif
-constexpr int kBsGroups = VBSR_BS_GROUPS;
+#ifndef VBSR_BS_GROUPS_NARROW
+#define VBSR_BS_GROUPS_NARROW 32
+#endif
+// Groups per block iteration: for rhs <= 32 (B in L2 after the first touch at the headline's size,
+// the pre-pass latency-bound) more, so that each thread has more loads in flight; for rhs = 64 (at
+// DRAM bandwidth) 8.
+__host__ __device__ constexpr int bs_groups(int rhs) {
+  return rhs <= 32 ? VBSR_BS_GROUPS_NARROW : VBSR_BS_GROUPS;
+}
 template <int RHS>
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
                                                      float* __restrict__ out) {
   constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS);
+  constexpr int kBsGroups = bs_groups(RHS);
   constexpr int per_col = 2 * kBsGroups;  // float4s per column run
   __shared__ float4 buf[RHS * per_col];  // [c][kg][2 x float4]: up to 32 KB
   griddep_launch_dependents();  // the SpMM may start its prologue now (it waits before reading)
@@ -713,7 +722,7 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
     const int ng = int(ngroups - kg0 < kBsGroups ? ngroups - kg0 : kBsGroups);
     // read: each RHS column's run of 8 * kBsGroups values (coalesced)
     const float* src = B + 8 * kg0;
-#pragma unroll 4
+#pragma unroll 8
     for (int i = threadIdx.x; i < RHS * per_col; i += blockDim.x) {
       const int c = i / per_col, r = i % per_col;  // powers of two: shifts
       if (r < 2 * ng) buf[i] = __ldg(reinterpret_cast<const float4*>(src + (long long)c * K) + r);
