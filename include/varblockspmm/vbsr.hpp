@@ -109,6 +109,26 @@ class Plan {
   PlanOptions options_{};
 };
 
+/** Multi-GPU plan (no reference counterpart; the reference is single-GPU): the block rows split
+ * into balanced shards, one per entry of `devices` (entries may repeat), each with its own plan,
+ * B replica, C block and stream. replicate_B copies B (K x rhs) peer to peer along a doubling
+ * tree (src_device < 0: B is host memory); execute runs every shard with no collective;
+ * synchronize waits and returns the longest shard time in ms; gather_C assembles the M x rhs
+ * column-major result (dst_device < 0: host memory). */
+class MultiPlan {
+ public:
+  MultiPlan(const HostMatrix&, const std::vector<int>& devices, PlanOptions);
+  void replicate_B(const float* B, int src_device = -1);
+  void execute();
+  float synchronize();
+  void gather_C(float* C, int dst_device = -1);
+  int size() const;
+  const vbsr_multi_plan* handle() const { return p_.get(); }
+
+ private:
+  std::shared_ptr<vbsr_multi_plan> p_;
+};
+
 void launch_row_owned(DeviceMatrix, const int32_t* row_shape_order, int small_row_count,
                       int large_row_count, const float*, float*, int rhs, cudaStream_t);
 void launch_row_owned_scalar(DeviceMatrix, const float*, float*, int rhs, cudaStream_t);

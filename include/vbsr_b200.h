@@ -24,8 +24,8 @@
  *   vbsr_launch_row_owned_scalar launch_row_owned_scalar    vbsr.hpp:161, row_owned.cu:376-395
  *   vbsr_generate               generate(GeneratorOptions)  vbsr.hpp:69-80,
  *                                                           src/format/generator.cpp:7-88
- * Entry points with no single reference counterpart (the multi-GPU block-row partition, the
- * on-device value generator, plan diagnostics) say so in their comments.
+ * Entry points with no single reference counterpart (the multi-GPU block-row partition and
+ * multi-GPU plan, the on-device value generator, plan diagnostics) say so in their comments.
  */
 #ifndef VBSR_B200_H
 #define VBSR_B200_H
@@ -292,6 +292,53 @@ vbsr_status vbsr_fill_mt19937(uint32_t seed, uint64_t count, float* out);
  * boundaries (bounds[0] = 0, bounds[parts] = block_rows). */
 vbsr_status vbsr_partition_rows(const vbsr_host_matrix_view* host, int parts, int rhs,
                                 int32_t* bounds);
+
+/* ---- Multi-GPU plan (one process, several GPUs) ------------------------------------------- */
+
+/* No reference counterpart (the reference is single-GPU). A multi-GPU plan partitions the block
+ * rows of a host matrix into `ngpus` contiguous ranges of balanced cost (vbsr_partition_rows),
+ * builds each range's shard matrix and plan on devices[r] (devices may repeat), and owns per
+ * shard a full K x rhs replica of B, a C block of the shard's c_rows x rhs (ld c_rows) and a
+ * stream. Execute runs every shard's plan on its own stream: no reduction, no exchange, no NCCL.
+ * kernel and flags are those of vbsr_plan_create_ex. */
+typedef struct vbsr_multi_plan vbsr_multi_plan;
+typedef struct vbsr_multi_shard {
+  int32_t device;
+  int32_t row_begin, row_end; /* block rows of the shard                                   */
+  int64_t c_row0, c_rows;     /* its rows of C: [c_row0, c_row0 + c_rows) of the M rows     */
+  float* B;                   /* device pointer: the shard's B replica (K x rhs, ld K)      */
+  float* C;                   /* device pointer: the shard's C block (c_rows x rhs, ld c_rows) */
+  vbsr_plan* plan;            /* the shard's plan (owned by the multi-plan)                 */
+  vbsr_stream_t stream;       /* the shard's stream (owned by the multi-plan)               */
+} vbsr_multi_shard;
+
+vbsr_status vbsr_multi_plan_create(const vbsr_host_matrix_view* host, int ngpus,
+                                   const int* devices, int rhs, int kernel, uint32_t flags,
+                                   vbsr_multi_plan** out);
+/* Like vbsr_multi_plan_create, with the values generated on each device from `seed` (as in
+ * vbsr_matrix_create_rows_generated); host->values may be NULL. */
+vbsr_status vbsr_multi_plan_create_generated(const vbsr_host_matrix_view* host, int ngpus,
+                                             const int* devices, int rhs, int kernel,
+                                             uint32_t flags, uint64_t seed,
+                                             vbsr_multi_plan** out);
+vbsr_status vbsr_multi_plan_destroy(vbsr_multi_plan* mp);
+vbsr_status vbsr_multi_plan_count(const vbsr_multi_plan* mp, int* ngpus);
+vbsr_status vbsr_multi_plan_shard(const vbsr_multi_plan* mp, int rank, vbsr_multi_shard* out);
+/* Copies B (K x rhs, column-major) into every shard's replica: first into shard 0 from `B`
+ * (host memory if src_device < 0, else device memory on src_device), then peer to peer along a
+ * doubling tree (in round t shards [0, 2^t) each copy their replica to shard i + 2^t), so N
+ * replicas take ceil(log2 N) rounds over NVLink. Asynchronous on the shards' streams: `B` must
+ * be complete when the call is made and stay valid until the next synchronize. */
+vbsr_status vbsr_multi_plan_replicate_B(vbsr_multi_plan* mp, const float* B, int src_device);
+/* Enqueues every shard's execute on its stream (replica B, shard C), bracketed by events. */
+vbsr_status vbsr_multi_plan_execute(vbsr_multi_plan* mp);
+/* Waits for every shard, checks each plan's status word, and gives the longest shard time of
+ * the last execute in ms (device events; max over shards). max_ms may be NULL. */
+vbsr_status vbsr_multi_plan_synchronize(vbsr_multi_plan* mp, float* max_ms);
+/* Assembles C (M x rhs, column-major, ld M) from the shards: host memory if dst_device < 0,
+ * else device memory on dst_device (shards on other devices copy peer to peer). Returns when
+ * the copies are done. */
+vbsr_status vbsr_multi_plan_gather_C(vbsr_multi_plan* mp, float* C, int dst_device);
 
 /* Byte counts of the benchmark's roofline: the compulsory bytes of the reference VBSR format,
  * 4*sum(h*w) + 4*nnzb + 8*(nnzb+1) + 4*(R+1) + 4*R + 8*(R+1) + 4*S + 8*(S+1) + 4*K*N + 4*M*N,

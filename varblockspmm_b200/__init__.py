@@ -2,7 +2,8 @@
 
 Mirrors the host API of King-Clawthorne/VarBlockSpMM (include/varblockspmm/vbsr.hpp) over the
 engine's C ABI (include/vbsr_b200.h, libvbsr_b200.so): HostMatrix, Matrix, Plan, PlanOptions,
-Kernel, Distribution, GeneratorOptions, generate, launch_row_owned, launch_row_owned_scalar.
+Kernel, Distribution, GeneratorOptions, generate, launch_row_owned, launch_row_owned_scalar, and
+the multi-GPU MultiPlan (no reference counterpart).
 Errors follow the reference's exception types: malformed input raises InvalidArgument (a
 ValueError, the analogue of std::invalid_argument), CUDA failures raise CudaError (a
 RuntimeError, the analogue of std::runtime_error).
@@ -122,6 +123,12 @@ class GenOpts(C.Structure):
 
 
 _vp = C.c_void_p
+class MultiShard(C.Structure):
+    _fields_ = [("device", C.c_int32), ("row_begin", C.c_int32), ("row_end", C.c_int32),
+                ("c_row0", C.c_int64), ("c_rows", C.c_int64), ("B", _vp), ("C", _vp),
+                ("plan", _vp), ("stream", _vp)]
+
+
 _sig = {
     "vbsr_host_validate": [C.POINTER(HostView)],
     "vbsr_matrix_create": [C.POINTER(HostView), C.c_int, C.POINTER(_vp)],
@@ -154,6 +161,17 @@ _sig = {
     "vbsr_partition_rows": [C.POINTER(HostView), C.c_int, C.c_int, _p32],
     "vbsr_compulsory_bytes": [C.POINTER(HostView), C.c_int32, C.c_int32, C.c_int,
                               C.POINTER(C.c_double), C.POINTER(C.c_double)],
+    "vbsr_multi_plan_create": [C.POINTER(HostView), C.c_int, _p32, C.c_int, C.c_int, C.c_uint32,
+                               C.POINTER(_vp)],
+    "vbsr_multi_plan_create_generated": [C.POINTER(HostView), C.c_int, _p32, C.c_int, C.c_int,
+                                         C.c_uint32, C.c_uint64, C.POINTER(_vp)],
+    "vbsr_multi_plan_destroy": [_vp],
+    "vbsr_multi_plan_count": [_vp, C.POINTER(C.c_int)],
+    "vbsr_multi_plan_shard": [_vp, C.c_int, C.POINTER(MultiShard)],
+    "vbsr_multi_plan_replicate_B": [_vp, _vp, C.c_int],
+    "vbsr_multi_plan_execute": [_vp],
+    "vbsr_multi_plan_synchronize": [_vp, C.POINTER(C.c_float)],
+    "vbsr_multi_plan_gather_C": [_vp, _vp, C.c_int],
 }
 for _name, _args in _sig.items():
     _f = getattr(_lib, _name)
@@ -511,6 +529,99 @@ class Plan:
     def close(self):
         if self._h:
             _lib.vbsr_plan_destroy(self._h)
+            self._h = _vp()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class MultiPlan:
+    """Multi-GPU plan: the block rows of `host` split into len(devices) balanced shards, one per
+    entry of `devices` (entries may repeat), each with its own plan, B replica, C block and
+    stream (vbsr_multi_plan_*). No reference counterpart: the reference is single-GPU.
+
+        mp = MultiPlan(host, [0, 1, 2, 3], PlanOptions(64))
+        mp.replicate_B(B)          # host numpy array or CUDA tensor; peer-to-peer doubling tree
+        mp.execute()               # every shard on its own stream
+        ms = mp.synchronize()      # max over shards of the device time of that execute
+        C = mp.gather_C()          # M x rhs column-major result (host numpy array)
+    """
+
+    def __init__(self, host: HostMatrix, devices, options: PlanOptions | int = PlanOptions(),
+                 flags: int = 0, generated_seed=None):
+        if isinstance(options, int):
+            options = PlanOptions(options)
+        self.options = options
+        self.rhs = int(options.rhs_width)
+        devs = np.ascontiguousarray(np.asarray(devices, dtype=np.int32))
+        self._h = _vp()
+        v = host.view()
+        if generated_seed is None:
+            _check(_lib.vbsr_multi_plan_create(C.byref(v), len(devs), _ptr(devs, C.c_int32),
+                                               self.rhs, int(options.kernel), flags,
+                                               C.byref(self._h)))
+        else:
+            _check(_lib.vbsr_multi_plan_create_generated(C.byref(v), len(devs),
+                                                         _ptr(devs, C.c_int32), self.rhs,
+                                                         int(options.kernel), flags,
+                                                         generated_seed, C.byref(self._h)))
+        self.M = int(host.scalar_rows())
+        self.K = int(host.scalar_cols())
+
+    def __len__(self) -> int:
+        n = C.c_int()
+        _check(_lib.vbsr_multi_plan_count(self._h, C.byref(n)))
+        return n.value
+
+    def shard(self, rank: int) -> MultiShard:
+        sh = MultiShard()
+        _check(_lib.vbsr_multi_plan_shard(self._h, rank, C.byref(sh)))
+        return sh
+
+    def replicate_B(self, B, src_device: int | None = None):
+        """Copies B (K x rhs, column-major) into every shard's replica. B is a host numpy float32
+        array, or a CUDA tensor / device pointer on src_device."""
+        if isinstance(B, np.ndarray):
+            if B.dtype != np.float32 or B.size != self.K * self.rhs:
+                raise InvalidArgument("B must be float32 with K * rhs elements")
+            Bc = np.ascontiguousarray(B)
+            _check(_lib.vbsr_multi_plan_replicate_B(self._h, Bc.ctypes.data, -1))
+            self.synchronize()  # the host buffer may be released after the call
+            return
+        dev = src_device if src_device is not None else B.device.index
+        if hasattr(B, "device"):
+            import torch
+            torch.cuda.synchronize(B.device)  # the copies run on the shards' streams
+        _check(_lib.vbsr_multi_plan_replicate_B(self._h, _dev_ptr(B), int(dev)))
+
+    def execute(self):
+        _check(_lib.vbsr_multi_plan_execute(self._h))
+
+    def synchronize(self) -> float:
+        ms = C.c_float()
+        _check(_lib.vbsr_multi_plan_synchronize(self._h, C.byref(ms)))
+        return ms.value
+
+    def gather_C(self, out=None, dst_device: int | None = None):
+        """The M x rhs column-major result: into a new host array (default), a given host array,
+        or a CUDA tensor on dst_device."""
+        if out is None:
+            out = np.empty(self.M * self.rhs, dtype=np.float32)
+        if isinstance(out, np.ndarray):
+            if out.dtype != np.float32 or out.size != self.M * self.rhs:
+                raise InvalidArgument("out must be float32 with M * rhs elements")
+            _check(_lib.vbsr_multi_plan_gather_C(self._h, out.ctypes.data, -1))
+            return out
+        dev = dst_device if dst_device is not None else out.device.index
+        _check(_lib.vbsr_multi_plan_gather_C(self._h, _dev_ptr(out), int(dev)))
+        return out
+
+    def close(self):
+        if self._h:
+            _lib.vbsr_multi_plan_destroy(self._h)
             self._h = _vp()
 
     def __del__(self):

@@ -24,7 +24,7 @@ COMMON = [*os.environ.get("VBSR_EXTRA_FLAGS", "").split(),
           "-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
           "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 
-SOURCES = ["vbsr_host.cpp", "vbsr_device.cu"]
+SOURCES = ["vbsr_host.cpp", "vbsr_device.cu", "vbsr_multi.cpp"]
 
 
 def _run(cmd):

@@ -120,6 +120,37 @@ void Plan::execute(const float* B, float* C, cudaStream_t stream) const {
   check(vbsr_plan_execute(p_.get(), B, C, reinterpret_cast<vbsr_stream_t>(stream)));
 }
 
+MultiPlan::MultiPlan(const HostMatrix& host, const std::vector<int>& devices,
+                     PlanOptions options) {
+  const vbsr_host_matrix_view v = detail::view_of(host);
+  vbsr_multi_plan* p = nullptr;
+  check(vbsr_multi_plan_create(&v, int(devices.size()), devices.data(), options.rhs_width,
+                               int(options.kernel), 0u, &p));
+  p_ = std::shared_ptr<vbsr_multi_plan>(p, [](vbsr_multi_plan* q) { vbsr_multi_plan_destroy(q); });
+}
+
+void MultiPlan::replicate_B(const float* B, int src_device) {
+  check(vbsr_multi_plan_replicate_B(p_.get(), B, src_device));
+}
+
+void MultiPlan::execute() { check(vbsr_multi_plan_execute(p_.get())); }
+
+float MultiPlan::synchronize() {
+  float ms = 0.0f;
+  check(vbsr_multi_plan_synchronize(p_.get(), &ms));
+  return ms;
+}
+
+void MultiPlan::gather_C(float* C, int dst_device) {
+  check(vbsr_multi_plan_gather_C(p_.get(), C, dst_device));
+}
+
+int MultiPlan::size() const {
+  int n = 0;
+  check(vbsr_multi_plan_count(p_.get(), &n));
+  return n;
+}
+
 int Plan::launch_count() const {
   int n = 0;
   check(vbsr_plan_launch_count(p_.get(), &n));
