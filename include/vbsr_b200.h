@@ -72,9 +72,10 @@ typedef struct vbsr_host_matrix_view {
 
 /* Non-owning device view in the reference's own layout (DeviceMatrix, vbsr.hpp:32-38). The
  * pointers are device pointers owned by the vbsr_matrix they came from. `values` is in the
- * engine's re-laid-out block format (each h x w block stored as h/8 row panels, each panel
- * 8 x w column-major), not the reference's column-major block layout; the launchers below
- * accept views produced by this library only. */
+ * engine's re-laid-out block format, not the reference's column-major block layout: each h x w
+ * block keeps its offset and size but is stored as w/8 consecutive 8-column groups, each h rows
+ * x 8 floats (32 bytes per row) with the two 16-byte halves of row r exchanged when bit 2 of r
+ * is set. The launchers below accept views produced by this library only. */
 typedef struct vbsr_device_matrix {
   int32_t block_rows, block_cols, nnzb;
   int64_t scalar_rows, scalar_cols;
@@ -112,8 +113,8 @@ vbsr_status vbsr_host_validate(const vbsr_host_matrix_view* host);
 
 /* Matrix::Matrix (vbsr.cpp:84-113): validates `host`, then builds the device format on
  * `device` (-1 = the current device): the reference-layout metadata arrays, per-block and
- * per-row descriptors used by the kernels, and the values re-laid-out into row panels by an
- * on-device kernel. Uploads are synchronous; the call returns when the matrix is usable from
+ * per-row descriptors used by the kernels, and the values re-laid-out into 8-column groups by
+ * an on-device kernel. Uploads are synchronous; the call returns when the matrix is usable from
  * any stream. */
 vbsr_status vbsr_matrix_create(const vbsr_host_matrix_view* host, int device, vbsr_matrix** out);
 
