@@ -12,7 +12,7 @@
 //     reference's generate() bit for bit; Profile::Spec gives the benchmark specification's
 //     block-size distributions).
 //   * Plan owns its device-side schedule (built once in the constructor); copies share it.
-//   * DeviceMatrix::values points at the engine's re-laid-out value array (row panels), so a
+//   * DeviceMatrix::values points at the engine's re-laid-out value array (8-column groups), so a
 //     DeviceMatrix is only meaningful to this library's launchers.
 //   * cpu_reference is the CPU oracle: it is defined in the test-infrastructure library
 //     oracle/_build/libvbsr_oracle.so, not in the engine library.
