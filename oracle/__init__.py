@@ -5,7 +5,9 @@ Python bindings for
     double-accumulating cpu_reference (src/format/vbsr.cpp:167-201), bit-identical to it, plus the
     per-element bound S = sum |a||b|;
   * _ref/libvbsr_ref.so (when present): the reference's own src/format/{vbsr,generator}.cpp
-    compiled unchanged by oracle/Makefile, with the C shim ref_shim.cpp.
+    compiled unchanged by oracle/Makefile, with the C shim ref_shim.cpp;
+  * _ref/libvbsr_ref_gpu.so (when present): the reference's own GPU path (Matrix, Plan and the
+    row-owned CUDA kernels) compiled unchanged for sm_100a, with the C shim ref_gpu_shim.cpp.
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import this package.
 """
 from __future__ import annotations
@@ -19,6 +21,7 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(_HERE, "_build", "libvbsr_oracle.so")
 REF_LIB = os.path.join(_HERE, "_ref", "libvbsr_ref.so")
+REF_GPU_LIB = os.path.join(_HERE, "_ref", "libvbsr_ref_gpu.so")
 
 
 def build(ref_dir: str = "/root/reference") -> None:
@@ -55,6 +58,62 @@ if os.path.exists(REF_LIB):
 
 def ref_available() -> bool:
     return _rlib is not None
+
+
+_glib = None
+
+
+def ref_gpu_available() -> bool:
+    """True when the reference's GPU library is built (loaded lazily: it needs a CUDA driver)."""
+    return os.path.exists(REF_GPU_LIB)
+
+
+def _ref_gpu_lib():
+    global _glib
+    if _glib is None:
+        _glib = C.CDLL(REF_GPU_LIB)
+        _glib.ref_gpu_last_error.restype = C.c_char_p
+        _glib.ref_gpu_create.restype = C.c_void_p
+        _glib.ref_gpu_create.argtypes = [C.c_void_p] * 10 + [C.c_int]
+        _glib.ref_gpu_execute.restype = C.c_int
+        _glib.ref_gpu_execute.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        _glib.ref_gpu_launch_count.restype = C.c_int
+        _glib.ref_gpu_launch_count.argtypes = [C.c_void_p]
+        _glib.ref_gpu_destroy.argtypes = [C.c_void_p]
+    return _glib
+
+
+class RefGpuPlan:
+    """The reference's own Matrix + Plan (row-owned kernels) on the current CUDA device, for
+    tests that run the reference's GPU path next to the engine's. execute() takes device
+    pointers (ints) and a raw stream handle (0 = the legacy default stream)."""
+
+    def __init__(self, host, rhs: int):
+        lib = _ref_gpu_lib()
+        args, keep = _ref_view_args(host)
+        self._h = lib.ref_gpu_create(*args, rhs)
+        del keep
+        if not self._h:
+            raise RuntimeError("reference Matrix/Plan: " + lib.ref_gpu_last_error().decode())
+
+    def execute(self, B_ptr: int, C_ptr: int, stream: int = 0):
+        lib = _ref_gpu_lib()
+        if lib.ref_gpu_execute(self._h, B_ptr, C_ptr, stream or None) != 0:
+            raise RuntimeError("reference Plan::execute: " + lib.ref_gpu_last_error().decode())
+
+    def launch_count(self) -> int:
+        return _ref_gpu_lib().ref_gpu_launch_count(self._h)
+
+    def close(self):
+        if self._h:
+            _ref_gpu_lib().ref_gpu_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _f32(a):
