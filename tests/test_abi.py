@@ -30,7 +30,9 @@ def test_cxx_dropin_library_links():
     out = subprocess.run(["nm", "-D", "--defined-only", "-C", path], capture_output=True,
                          text=True).stdout
     for name in ("vbsr::Plan::execute", "vbsr::Matrix::Matrix", "vbsr::HostMatrix::validate",
-                 "vbsr::generate", "vbsr::launch_row_owned", "vbsr::launch_row_owned_scalar"):
+                 "vbsr::generate", "vbsr::launch_row_owned", "vbsr::launch_row_owned_scalar",
+                 "vbsr::MultiPlan::MultiPlan", "vbsr::MultiPlan::replicate_B",
+                 "vbsr::MultiPlan::execute", "vbsr::MultiPlan::gather_C"):
         assert name in out, name
 
 
