@@ -251,6 +251,50 @@ def sampled_parity(host, rhs, row_range, dC, B_host, n_rows=12):
     return worst, bad
 
 
+def gathered_parity(host, rhs, bounds, rank, world, dC, B_host, per_shard=4):
+    """Verification only, outside the timed region: every rank's C block goes to rank 0 over NCCL
+    (point-to-point sends acting as an allgatherv), rank 0 reassembles the column-major M x N
+    result on the host, and checks block rows of every shard (its first and last rows and a few
+    in between) against the oracle. Returns None on ranks > 0."""
+    import oracle
+    import torch
+    import torch.distributed as dist
+    M = int(host.scalar_rows())
+    t0 = time.perf_counter()
+    if rank != 0:
+        dist.send(dC, dst=0)
+        return None
+    full = np.empty((rhs, M), dtype=np.float32)  # column-major M x rhs: row c holds column c
+    for r in range(world):
+        a, b = int(bounds[r]), int(bounds[r + 1])
+        c0, c1 = int(host.row_scalar_off[a]), int(host.row_scalar_off[b])
+        if r == 0:
+            blk = dC
+        else:
+            blk = torch.empty(max(1, (c1 - c0) * rhs), device=dC.device)
+            dist.recv(blk, src=r)
+        if c1 > c0:
+            full[:, c0:c1] = blk[:(c1 - c0) * rhs].view(rhs, c1 - c0).cpu().numpy()
+    gather_ms = (time.perf_counter() - t0) * 1e3
+    rng = np.random.default_rng(4321)
+    worst, bad, rows = 0.0, 0, 0
+    for r in range(world):
+        a, b = int(bounds[r]), int(bounds[r + 1])
+        if b <= a:
+            continue
+        picks = sorted(set([a, b - 1] + list(rng.integers(a, b, per_shard))))
+        for i in picks:
+            sub = host.row_slice(i, i + 1, values_seed=SEED)
+            g0 = int(host.row_scalar_off[i])
+            got = full[:, g0:g0 + int(host.row_size[i])].reshape(-1).copy()
+            ratio, _, nb = oracle.compare(sub, B_host, rhs, got, threads=1)
+            worst, bad, rows = max(worst, ratio), bad + nb, rows + 1
+    return {"rows_checked": rows, "max_err_over_bound": worst, "violations": bad,
+            "gather_ms": gather_ms,
+            "how": "NCCL send/recv of every rank's C block to rank 0, host reassembly of the "
+                   "M x N column-major result, oracle check of rows of every shard"}
+
+
 def cta_time_stats(plan, B, C, stream):
     """One extra execution with per-CTA timing: spread of CTA durations (load-balance check)."""
     plan.enable_cta_timing(True)
@@ -450,8 +494,10 @@ def run_gpu_arm(args):
     # ---- parity at full size on a sample of rows -------------------------------------------------
     ratio, bad = sampled_parity(host, rhs, (r0, r1), dC, B_host)
     pr = torch.tensor([ratio, float(bad)], dtype=torch.float64, device="cuda")
+    gathered = None
     if world > 1:
         dist.all_reduce(pr, op=dist.ReduceOp.MAX)
+        gathered = gathered_parity(host, rhs, bounds, rank, world, dC, B_host)
 
     headline = None
     cpu = None
@@ -501,6 +547,8 @@ def run_gpu_arm(args):
                        "violations": int(pr[1].item())},
             "setup_s": setup_s, "replicate_ms": replicate_ms, "cta_time": cta_stats,
         }
+        if gathered:
+            line["gathered_parity"] = gathered
         if headline:
             line["headline"] = headline
         if cpu:
