@@ -55,41 +55,48 @@
 
 namespace vbsr_b200 {
 
-#ifndef VBSR_EPI_SETS
-#define VBSR_EPI_SETS 2
-#endif
-#ifndef VBSR_SPLIT_WARPS
-#define VBSR_SPLIT_WARPS (VBSR_EPI_SETS == 2 ? 4 : 8)
-#endif
-#ifndef VBSR_FEEDERS
-#define VBSR_FEEDERS 4
-#endif
-constexpr int kTcSplitWarps = VBSR_SPLIT_WARPS;  // split warps
-// Epilogue warps: kEpiSets sets of four (warp q of a set reads TMEM quadrant q); set e stores the
-// items j with j % kEpiSets == e.
-constexpr int kEpiSets = VBSR_EPI_SETS;
-constexpr int kTcEpiWarps = 4 * kEpiSets;
-constexpr int kTcMmaWarps = 4;                   // MMA-issuing warps
-constexpr int kTcFeeders = VBSR_FEEDERS;         // feeder warps
-// The epilogue warps follow the others and must start at a multiple of 4 (a warp reaches the TMEM
-// lanes 32 (warp % 4) ... only); every slot count is a multiple of each role's warp count.
-static_assert((kTcSplitWarps + kTcMmaWarps + kTcFeeders) % 4 == 0, "epilogue warps misplaced");
-constexpr int kTcRingMultiple = kTcSplitWarps > kTcFeeders ? kTcSplitWarps : kTcFeeders;
-static_assert(kTcRingMultiple % kTcSplitWarps == 0 && kTcRingMultiple % kTcFeeders == 0 &&
-                  kTcRingMultiple % kTcMmaWarps == 0, "role warp counts must divide the ring");
+// Warp roles (20 warps, one CTA per SM), per form (template parameter TR of the kernel):
+//                     split   MMA   feeders   epilogue
+//   row-stacked         4      4       4       8 (two sets)
+//   column-stacked      8      4       4       4 (one set; its split warps also form B_lo)
+// Epilogue warps come last and start at a multiple of 4 (a warp reaches the TMEM lanes
+// 32 (warp % 4) ... only); epilogue set e stores the items j with j % sets == e. Every slot
+// count is a multiple of each role's warp count (kTcRingMultiple).
+template <bool TR>
+struct Roles {
+  static constexpr int split = TR ? 4 : 8;
+  static constexpr int epi_sets = TR ? 2 : 1;
+  static constexpr int mma0 = split, feeder0 = split + 4, epi0 = split + 8;
+  static_assert(epi0 % 4 == 0 && epi0 + 4 * epi_sets == 20, "role layout");
+};
+constexpr int kTcMmaWarps = 4;  // MMA-issuing warps
+constexpr int kTcFeeders = 4;   // feeder warps
+constexpr int kTcRingMultiple = 8;
 #ifndef VBSR_PREFETCH
 #define VBSR_PREFETCH 2
 #endif
 constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this many own stages ahead
-constexpr int kTcWarps = kTcSplitWarps + kTcMmaWarps + kTcFeeders + kTcEpiWarps;
+constexpr int kTcWarps = 20;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 // RHS widths up to 32 use the row-stacked form (one MMA per group, the operand stack S on the N
 // side); width 64 the column-stacked form (two MMAs per group, S on the M side). S has
 // stack_rows(rhs) rows of 32 bytes per 8-column group.
 __host__ __device__ constexpr bool row_stacked(int rhs) { return rhs <= 32; }
-__host__ __device__ constexpr int stack_rows(int rhs) { return row_stacked(rhs) ? 2 * rhs : stack_m(rhs); }
+#ifndef VBSR_RAW_B
+#define VBSR_RAW_B 1
+#endif
+// Column-stacked form with VBSR_RAW_B: the pre-pass writes only the raw B rows (64 per group),
+// the split warps form their lo rows in shared memory, and each group takes three M = 64 MMAs.
+constexpr bool kRawB = VBSR_RAW_B != 0;
+__host__ __device__ constexpr int stack_rows(int rhs) {
+  return row_stacked(rhs) ? 2 * rhs : (kRawB ? rhs : stack_m(rhs));
+}
+// Bytes of one group's stack in global memory, and in a shared-memory slot.
 __host__ __device__ constexpr int stack_tile_bytes(int rhs) { return 32 * stack_rows(rhs); }
+__host__ __device__ constexpr int stack_slot_bytes(int rhs) {
+  return (!row_stacked(rhs) && kRawB) ? 2 * stack_tile_bytes(rhs) : stack_tile_bytes(rhs);
+}
 // A slot (26 KB by default) holds one stage of G groups: their A values and A_lo parts in the first
 // 64 h G bytes (column-stacked form: raw A of group after group, then the A_lo parts at byte
 // 32 h G; row-stacked form: per group, 8-row blocks of raw A and of A_lo alternating), then their
@@ -105,8 +112,8 @@ constexpr int kSlotBytes = VBSR_SLOT_KB * 1024;
 constexpr int kMaxStageGroups = VBSR_MAX_GROUPS;
 __host__ __device__ constexpr int slot_floats(int rhs) { return (void)rhs, kSlotBytes / 4; }
 __host__ __device__ constexpr int stage_groups(int h, int rhs) {
-  return kSlotBytes / (64 * h + stack_tile_bytes(rhs)) < kMaxStageGroups
-             ? kSlotBytes / (64 * h + stack_tile_bytes(rhs))
+  return kSlotBytes / (64 * h + stack_slot_bytes(rhs)) < kMaxStageGroups
+             ? kSlotBytes / (64 * h + stack_slot_bytes(rhs))
              : kMaxStageGroups;
 }
 __host__ __device__ constexpr int slot_stack_bytes(int h, int groups) { return 64 * h * groups; }
@@ -353,7 +360,8 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   VBSR_PROF_ADD(p, 4, t_w);
   tc_fence_after();
   const int h = it.h(), nw = it.nw(), n0 = it.n0();
-  const int half = stack_m(nw) / 8, quads = nw / half;
+  // raw-B: 16 columns per quadrant (M = 64 layout: lanes 0..15), hi and lo already summed
+  const int half = kRawB ? 16 : stack_m(nw) / 8, quads = nw / half;
   uint32_t use = 0;  // bit i: partial i received a stage of the item
   if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH))
     for (uint32_t i = 0; i < kTcMmaWarps && i < it.n; ++i) use |= 1u << ((it.k0 + i) & 3u);
@@ -379,7 +387,7 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           if (use & (1u << i)) a += v[i][e];
-        r[e] = a + __shfl_down_sync(0xffffffffu, a, half);
+        r[e] = kRawB ? a : a + __shfl_down_sync(0xffffffffu, a, half);
       }
       if (store) {
         dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
@@ -492,6 +500,23 @@ __device__ __forceinline__ void split_stage_rows(uint32_t sp, int groups, int h,
   }
 }
 
+// lo parts of n float4s at shared address sp, written lo_off bytes further.
+__device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, int lane) {
+  for (int i0 = 0; i0 < n; i0 += 128) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + 32 * u + lane;
+      if (i < n) x[u] = lds128(sp + 16u * i);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + 32 * u + lane;
+      if (i < n) sts128(sp + lo_off + 16u * i, lo_part4(x[u]));
+    }
+  }
+}
+
 // Column-stacked form: A_lo of a whole stage at shared address sp: the stage's A (2h float4s per
 // group, groups one after another) at sp, its A_lo at the same offsets 32 h G bytes further. Eight
 // loads per lane are in flight before their stores.
@@ -513,12 +538,13 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int 
   }
 }
 
-// Split warp w: forms the lo parts of the stages k with k % kTcSplitWarps == w (slots w, w +
-// kTcSplitWarps, ...).
+// Split warp w: forms the lo parts of the stages k with k % Roles<TR>::split == w (slots w,
+// w + Roles<TR>::split, ...).
 template <bool CHECK, bool TR>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
+  constexpr int kTcSplitWarps = Roles<TR>::split;
   const int D = task.stages, SF = task.stage_floats;
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
@@ -549,10 +575,16 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       VBSR_TRACE_ST(kk, 2);
       VBSR_PROF_T0(t_s);
       if (math) {
-        if (TR)
+        if (TR) {
           split_stage_rows(slots + 4u * uint32_t(s * SF), groups, h, lane);
-        else
+        } else {
           split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
+          if (kRawB) {  // the stacks' lo rows: the raw rows (T per group) are followed by theirs
+            const int T = stack_tile_bytes(p.rhs);
+            split_flat(slots + 4u * uint32_t(s * SF) + uint32_t(slot_stack_bytes(h, groups)),
+                       T * groups / 16, uint32_t(T * groups), lane);
+          }
+        }
         VBSR_TRACE_ST(kk, 6);
         fence_proxy_async_smem();
       }
@@ -577,6 +609,7 @@ __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBa
   for (int j = 0; !iw.done(); ++j) {
     const Item it = iw.get();
     iw.advance(lane);
+    constexpr int kEpiSets = Roles<TR>::epi_sets;
     if (kEpiSets > 1 && j % kEpiSets != set) continue;  // another set's item
     VBSR_PROF_T0(t_e);
     if (q == 0) VBSR_TRACE_IT(j, 0);
@@ -624,7 +657,8 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
     const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 64 * i);
     // row-stacked: M = the group's interleaved A / A_lo rows (64 covers h <= 32), N = S's 2 rhs
     // rows; column-stacked: M = S's rows, N = the group's h rows of A (then of A_lo)
-    const uint32_t idesc = TR ? tf32_idesc(h <= kTrM64MaxH ? 64 : 128, 2 * p.rhs) : tf32_idesc(M, h);
+    const uint32_t idesc = TR ? tf32_idesc(h <= kTrM64MaxH ? 64 : 128, 2 * p.rhs)
+                              : tf32_idesc(kRawB ? p.rhs : M, h);
     uint32_t started = 0;
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
       const int groups = it.stage_groups(kk - int(it.k0), G);
@@ -659,6 +693,8 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
               const uint32_t ag = sa + 32u * h * g, lo_off = 32u * h * groups;  // A_lo region
               tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag), idesc, started);          // S x A
               tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag + lo_off), idesc, 1u);      // S x A_lo
+              if (kRawB)  // B_lo x A, into the same rows: S's lo rows follow all groups' raw rows
+                tc_mma_tf32(tmem_d, sw32_desc(ss + T * (groups + g)), sw32_desc(ag), idesc, 1u);
               started = 1u;
             }
           }
@@ -739,6 +775,9 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
       if (row_stacked(RHS)) {  // rows c: raw B of column c; rows RHS + c: its lo part
         c = row % RHS;
         lo = row >= RHS;
+      } else if (kRawB) {  // raw rows only: row c is column c
+        c = row;
+        lo = false;
       } else {  // per quadrant q: rows of hi, then rows of lo, of columns half*q ...
         const int q = row / (2 * half), jj = row % (2 * half);
         c = q * half + jj % half;
@@ -779,7 +818,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_addr(&accbars[0][b]), uint32_t(kTcMmaWarps));
-      mbar_init(smem_addr(&accbars[1][b]), uint32_t(kTcEpiWarps / kEpiSets));
+      mbar_init(smem_addr(&accbars[1][b]), 4u);  // the four warps of the buffer's epilogue set
     }
     for (int i = 0; i < kTcMmaWarps; ++i) mbar_init(smem_addr(&drainbars[i]), 1u);
 
@@ -798,15 +837,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   cb.accfree0 = smem_addr(&accbars[1][0]);
   cb.drain0 = smem_addr(&drainbars[0]);
 
-  if (warp < kTcSplitWarps)
+  using RL = Roles<TR>;
+  if (warp < RL::mma0)
     tc_split_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
-  else if (warp < kTcSplitWarps + kTcMmaWarps)
-    tc_mma_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp - kTcSplitWarps, lane, &abort_flag);
-  else if (warp < kTcSplitWarps + kTcMmaWarps + kTcFeeders)
-    tc_feeder<CHECK>(p, task, slots, cb, warp - kTcSplitWarps - kTcMmaWarps, lane, &abort_flag);
+  else if (warp < RL::feeder0)
+    tc_mma_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane, &abort_flag);
+  else if (warp < RL::epi0)
+    tc_feeder<CHECK>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
   else  // the epilogue warps: TMEM quadrant warp % 4
-    tc_epi_warp<CHECK, TR>(p, task, cb, tmem_base, warp & 3,
-                           (warp - kTcSplitWarps - kTcMmaWarps - kTcFeeders) >> 2, lane, &abort_flag);
+    tc_epi_warp<CHECK, TR>(p, task, cb, tmem_base, warp & 3, (warp - RL::epi0) >> 2, lane,
+                           &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
