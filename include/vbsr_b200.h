@@ -149,6 +149,12 @@ enum {
   VBSR_PLAN_BOUNDS_CHECK = 1u << 0, /* use the bounds-checked kernel build                  */
   VBSR_PLAN_NO_SPLIT = 1u << 1,     /* accepted for compatibility; no effect (no row splits) */
   VBSR_PLAN_NARROW_STAGES = 1u << 2, /* accepted for compatibility; no effect               */
+  /* RHS 64 only, results identical either way: force the raw-B operand stacks (the pre-pass
+   * writes raw B rows, the kernel forms their lo parts) or the pre-split ones (hi and lo rows
+   * from the pre-pass). By default the plan picks raw-B when the pre-split stacks, K x 512
+   * bytes, exceed 64 MB and would not stay in L2. */
+  VBSR_PLAN_STACKS_RAW = 1u << 3,
+  VBSR_PLAN_STACKS_PRESPLIT = 1u << 4,
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
   VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9,   /* consumers wait for the data but compute nothing     */

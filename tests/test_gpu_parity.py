@@ -105,6 +105,31 @@ def test_bounds_checked_build_and_no_split(cuda, rhs):
     assert_within_bound(host, B, rhs, d)
 
 
+STACKS = [("raw", vb.PLAN_STACKS_RAW), ("presplit", vb.PLAN_STACKS_PRESPLIT)]
+
+
+@pytest.mark.parametrize("stacks", STACKS, ids=lambda s: s[0])
+@pytest.mark.parametrize("case", [(1024, 16, 3, False, 1), (512, 4, 0, True, 9),
+                                  (700, 8, 2, False, 4), (256, 1, 1, False, 13)],
+                         ids=lambda c: "r%dd%d" % (c[0], c[1]))
+def test_rhs64_stack_layouts(cuda, stacks, case):
+    """RHS 64 with each operand-stack layout forced: raw-B stacks (lo rows formed in the kernel,
+    three MMAs per group) and pre-split stacks (two MMAs per group). Both meet the bound; the
+    plan names the layout it uses."""
+    rows, deg, dist, local, seed = case
+    rhs = 64
+    host = spec_case(rows, deg, dist, local, seed)
+    B = vb.fill_uniform(seed, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(rhs), stacks[1])
+    assert ("raw-b" in p.describe()) == (stacks[0] == "raw")
+    got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
+    assert_within_bound(host, B, rhs, got)
+    # the bounds-checked build agrees bit for bit
+    chk = run_plan(cuda, host, B, rhs, flags=stacks[1] | vb.PLAN_BOUNDS_CHECK)
+    assert np.array_equal(got.view(np.uint32), chk.view(np.uint32))
+
+
 def _handmade(heights, widths, rows_cols, seed=0):
     """A matrix from explicit per-row block column lists (possibly empty rows)."""
     rng = np.random.default_rng(seed)

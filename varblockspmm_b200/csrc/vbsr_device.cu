@@ -335,6 +335,7 @@ struct vbsr_plan {
   StageDesc* d_stream = nullptr;
   ItemDesc* d_items = nullptr;
   float* d_bstack = nullptr;     // B's operand stacks, rewritten by every execute
+  bool raw_b = false;            // column-stacked form: raw-B stacks (see stack_rows)
   int64_t bstack_floats = 0;
   Task* d_tasks = nullptr;
   int* d_status = nullptr;
@@ -359,18 +360,18 @@ double item_cost(int h, int nw, int64_t sum_w, int nstages) {
 
 cudaError_t set_kernel_attrs() {
   const int bytes = kSmemBudget + 1024;
-  cudaError_t e = cudaFuncSetAttribute(spmm_tc_kernel<false, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(spmm_tc_kernel<true, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(spmm_tc_kernel<false, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(spmm_tc_kernel<true, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  return e;
+  const void* kernels[] = {
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, true>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, true>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, true, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, true, false>)};
+  for (const void* k : kernels) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 // Schedule for spmm_tc_kernel: one item per block row, one CTA per SM; items assigned to CTAs by
@@ -384,11 +385,24 @@ vbsr_status build_schedule(vbsr_plan* p) {
   if (d.nvalues >= stage::kMaxVal || d.K >= stage::kMaxCol || d.M >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "matrix exceeds the schedule's index range");
 
+  // Column-stacked form: raw-B stacks when the pre-split stacks (K x 512 bytes) would not stay in
+  // L2 (a stack read then comes from DRAM, and raw halves those bytes); pre-split stacks below
+  // that, where the reads hit L2 and the extra split work of raw would only cost time.
+#ifndef VBSR_RAW_B
+#define VBSR_RAW_B -1  // -1: by size; 0 / 1: forced (development)
+#endif
+  constexpr int64_t kRawStackBytes = 64ll << 20;
+  const bool big = (d.K / 8) * int64_t(stack_tile_bytes(rhs, false)) > kRawStackBytes;
+  p->raw_b = !row_stacked(rhs) &&
+             ((p->flags & VBSR_PLAN_STACKS_RAW)        ? true
+              : (p->flags & VBSR_PLAN_STACKS_PRESPLIT) ? false
+              : VBSR_RAW_B >= 0                        ? VBSR_RAW_B != 0
+                                                       : big);
   const int R = d.block_rows;
   std::vector<int> row_stages(R);
   std::vector<double> cost(R);
   for (int i = 0; i < R; ++i) {
-    const int G = stage_groups(d.h_row_size[i], rhs);  // 8-column groups per stage
+    const int G = stage_groups(d.h_row_size[i], rhs, p->raw_b);  // 8-column groups per stage
     int64_t groups = 0;
     for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b)
       groups += int64_t((d.h_blk_desc[b] & 7u) + 1u);
@@ -446,7 +460,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
       // format group g of a block starts 8*h*g floats after the block's values and a block row's
       // blocks are consecutive, so a stage's A values are one contiguous range.
       int64_t val = d.h_val_off_row[i];
-      const int G = stage_groups(h, rhs);
+      const int G = stage_groups(h, rhs, p->raw_b);
       int used = 0;  // columns in the current stage
       StageDesc cur{};
       for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) {
@@ -501,15 +515,17 @@ vbsr_status build_schedule(vbsr_plan* p) {
   char buf[512];
   std::snprintf(buf, sizeof buf,
                 "rhs=%d items=%d pipeline_stages=%zu tasks=%d teams=%d ring=%d smem=%d sms=%d "
-                "kernel=tcgen05-3xtf32-stacked",
-                rhs, R, stream.size(), p->num_tasks, teams, stages, p->smem_bytes, num_sm);
+                "kernel=tcgen05-3xtf32-%s",
+                rhs, R, stream.size(), p->num_tasks, teams, stages, p->smem_bytes, num_sm,
+                row_stacked(rhs) ? "row-stacked" : (p->raw_b ? "column-stacked-raw-b"
+                                                              : "column-stacked-pre-split"));
   p->summary = buf;
 
   DeviceGuard guard(d.device);
   VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
   // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
-  p->bstack_floats = (d.K / 8) * int64_t(stack_rows(rhs)) * 8;
+  p->bstack_floats = (d.K / 8) * int64_t(stack_rows(rhs, p->raw_b)) * 8;
   if ((d.K / 8) * rhs >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "B too large for the pre-pass index range");
   VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
@@ -550,10 +566,15 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   if (chunks > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
     const int64_t blocks = std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM);
     switch (kp.rhs) {
-      case 8: bstack_kernel<8><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
-      case 16: bstack_kernel<16><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
-      case 32: bstack_kernel<32><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
-      default: bstack_kernel<64><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
+      case 8: bstack_kernel<8, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
+      case 16: bstack_kernel<16, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
+      case 32: bstack_kernel<32, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
+      default:
+        if (p->raw_b)
+          bstack_kernel<64, true><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack);
+        else
+          bstack_kernel<64, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack);
+        break;
     }
   }
   // programmatic dependent launch: the SpMM's prologue overlaps the pre-pass (its feeders wait
@@ -570,9 +591,14 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   cfg.numAttrs = 1;
   const bool check = (p->flags & VBSR_PLAN_BOUNDS_CHECK) != 0;
   if (row_stacked(kp.rhs))
-    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, true> : spmm_tc_kernel<false, true>, kp);
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, true, false>
+                                   : spmm_tc_kernel<false, true, false>, kp);
+  else if (p->raw_b)
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, true>
+                                   : spmm_tc_kernel<false, false, true>, kp);
   else
-    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false> : spmm_tc_kernel<false, false>, kp);
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, false>
+                                   : spmm_tc_kernel<false, false, false>, kp);
 }
 
 // Launch parameters of one execute: the plan's schedule and the caller's B and C.

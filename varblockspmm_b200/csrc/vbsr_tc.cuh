@@ -83,19 +83,20 @@ __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 // side); width 64 the column-stacked form (two MMAs per group, S on the M side). S has
 // stack_rows(rhs) rows of 32 bytes per 8-column group.
 __host__ __device__ constexpr bool row_stacked(int rhs) { return rhs <= 32; }
-#ifndef VBSR_RAW_B
-#define VBSR_RAW_B 1
-#endif
-// Column-stacked form with VBSR_RAW_B: the pre-pass writes only the raw B rows (64 per group),
-// the split warps form their lo rows in shared memory, and each group takes three M = 64 MMAs.
-constexpr bool kRawB = VBSR_RAW_B != 0;
-__host__ __device__ constexpr int stack_rows(int rhs) {
-  return row_stacked(rhs) ? 2 * rhs : (kRawB ? rhs : stack_m(rhs));
+// Column-stacked form, two stack layouts (the plan picks one; `raw` below):
+//   pre-split: the pre-pass writes hi and lo rows (M = 128 per group), two MMAs per group;
+//   raw:       the pre-pass writes only the raw B rows (64 per group), the split warps form their
+//              lo rows in shared memory, and each group takes three M = 64 MMAs.
+// Raw halves the stacks' bytes in global memory, which pays when they do not stay in L2.
+__host__ __device__ constexpr int stack_rows(int rhs, bool raw) {
+  return row_stacked(rhs) ? 2 * rhs : (raw ? rhs : stack_m(rhs));
 }
 // Bytes of one group's stack in global memory, and in a shared-memory slot.
-__host__ __device__ constexpr int stack_tile_bytes(int rhs) { return 32 * stack_rows(rhs); }
-__host__ __device__ constexpr int stack_slot_bytes(int rhs) {
-  return (!row_stacked(rhs) && kRawB) ? 2 * stack_tile_bytes(rhs) : stack_tile_bytes(rhs);
+__host__ __device__ constexpr int stack_tile_bytes(int rhs, bool raw) {
+  return 32 * stack_rows(rhs, raw);
+}
+__host__ __device__ constexpr int stack_slot_bytes(int rhs, bool raw) {
+  return (!row_stacked(rhs) && raw) ? 2 * stack_tile_bytes(rhs, raw) : stack_tile_bytes(rhs, raw);
 }
 // A slot (26 KB by default) holds one stage of G groups: their A values and A_lo parts in the first
 // 64 h G bytes (column-stacked form: raw A of group after group, then the A_lo parts at byte
@@ -111,9 +112,9 @@ __host__ __device__ constexpr int stack_slot_bytes(int rhs) {
 constexpr int kSlotBytes = VBSR_SLOT_KB * 1024;
 constexpr int kMaxStageGroups = VBSR_MAX_GROUPS;
 __host__ __device__ constexpr int slot_floats(int rhs) { return (void)rhs, kSlotBytes / 4; }
-__host__ __device__ constexpr int stage_groups(int h, int rhs) {
-  return kSlotBytes / (64 * h + stack_slot_bytes(rhs)) < kMaxStageGroups
-             ? kSlotBytes / (64 * h + stack_slot_bytes(rhs))
+__host__ __device__ constexpr int stage_groups(int h, int rhs, bool raw) {
+  return kSlotBytes / (64 * h + stack_slot_bytes(rhs, raw)) < kMaxStageGroups
+             ? kSlotBytes / (64 * h + stack_slot_bytes(rhs, raw))
              : kMaxStageGroups;
 }
 __host__ __device__ constexpr int slot_stack_bytes(int h, int groups) { return 64 * h * groups; }
@@ -253,7 +254,7 @@ __device__ long long g_trace_items[1024 * 4];
 
 // Feeder warp f: fills the slots of the stages k with k % kTcFeeders == f, each once the MMAs of
 // the slot's previous stage have completed.
-template <bool CHECK>
+template <bool CHECK, bool RAW>
 __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
                           const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
   const int D = task.stages, SF = task.stage_floats;
@@ -286,7 +287,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.groups();
     const long long a0 = st.a_start();
     const uint32_t sp = slots + 4u * uint32_t(s * SF);
-    const int T = stack_tile_bytes(p.rhs);
+    const int T = stack_tile_bytes(p.rhs, RAW);
     const int col = lane < groups ? st.group_col(lane) : 0;
     const int prev = __shfl_up_sync(0xffffffffu, col, 1);
     const bool start = lane < groups && (lane == 0 || col != prev + 8);
@@ -306,7 +307,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     bool ok = true;
     if (CHECK) {
       ok = a0 + 8ll * h * groups <= p.nvalues && n0 == 0 && nw == p.rhs &&
-           groups <= stage_groups(h, p.rhs);
+           groups <= stage_groups(h, p.rhs, RAW);
       for (int g = 0; g < groups; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
     }
     if (kk == p.drop_stage) {
@@ -351,7 +352,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
 // partial 0) holds the stages issued by MMA warp i; only partials that received a stage are read.
 // Within a partial, column r is row r of the tile. Lane j < half of quadrant w holds hi of RHS
 // column n0 + half*w + j, lane half + j its lo.
-template <bool CHECK>
+template <bool CHECK, bool RAW>
 __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars& cb, int buf,
                                             uint32_t parity, uint32_t tmem_buf, int w, int lane,
                                             const Item& it, volatile int* abort_flag) {
@@ -361,7 +362,7 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
   tc_fence_after();
   const int h = it.h(), nw = it.nw(), n0 = it.n0();
   // raw-B: 16 columns per quadrant (M = 64 layout: lanes 0..15), hi and lo already summed
-  const int half = kRawB ? 16 : stack_m(nw) / 8, quads = nw / half;
+  const int half = RAW ? 16 : stack_m(nw) / 8, quads = nw / half;
   uint32_t use = 0;  // bit i: partial i received a stage of the item
   if (!(p.diag & VBSR_PLAN_DIAG_SKIP_MATH))
     for (uint32_t i = 0; i < kTcMmaWarps && i < it.n; ++i) use |= 1u << ((it.k0 + i) & 3u);
@@ -387,7 +388,7 @@ __device__ __forceinline__ bool tc_epilogue(const KernelParams& p, const CtaBars
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           if (use & (1u << i)) a += v[i][e];
-        r[e] = kRawB ? a : a + __shfl_down_sync(0xffffffffu, a, half);
+        r[e] = RAW ? a : a + __shfl_down_sync(0xffffffffu, a, half);
       }
       if (store) {
         dst[c0 / 4] = make_float4(r[0], r[1], r[2], r[3]);
@@ -540,7 +541,7 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int 
 
 // Split warp w: forms the lo parts of the stages k with k % Roles<TR>::split == w (slots w,
 // w + Roles<TR>::split, ...).
-template <bool CHECK, bool TR>
+template <bool CHECK, bool TR, bool RAW>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
@@ -557,7 +558,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
   while (ok && !iw.done()) {
     const Item it = iw.get();
     iw.advance(lane);
-    const int h = it.h(), G = stage_groups(h, p.rhs);
+    const int h = it.h(), G = stage_groups(h, p.rhs, RAW);
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcSplitWarps) {
       const int groups = it.stage_groups(kk - int(it.k0), G);
       const int s = ms;
@@ -579,8 +580,8 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
           split_stage_rows(slots + 4u * uint32_t(s * SF), groups, h, lane);
         } else {
           split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
-          if (kRawB) {  // the stacks' lo rows: the raw rows (T per group) are followed by theirs
-            const int T = stack_tile_bytes(p.rhs);
+          if (RAW) {  // the stacks' lo rows: the raw rows (T per group) are followed by theirs
+            const int T = stack_tile_bytes(p.rhs, RAW);
             split_flat(slots + 4u * uint32_t(s * SF) + uint32_t(slot_stack_bytes(h, groups)),
                        T * groups / 16, uint32_t(T * groups), lane);
           }
@@ -599,7 +600,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
 
 // Epilogue warp q (TMEM quadrant q) of epilogue set `set`: stores the results of the set's items as
 // soon as their MMAs are done.
-template <bool CHECK, bool TR>
+template <bool CHECK, bool TR, bool RAW>
 __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBars& cb,
                             uint32_t tmem_base, int q, int set, int lane,
                             volatile int* abort_flag) {
@@ -615,7 +616,7 @@ __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBa
     if (q == 0) VBSR_TRACE_IT(j, 0);
     const uint32_t par = uint32_t((j >> 1) & 1), tbuf = tmem_base + uint32_t(256 * (j & 1));
     if (!(TR ? tc_epilogue_rows<CHECK>(p, cb, j & 1, par, tbuf, q, lane, it, abort_flag)
-             : tc_epilogue<CHECK>(p, cb, j & 1, par, tbuf, q, lane, it, abort_flag)))
+             : tc_epilogue<CHECK, RAW>(p, cb, j & 1, par, tbuf, q, lane, it, abort_flag)))
       break;
     VBSR_PROF_ADD(p, 8, t_e);
     if (q == 0) VBSR_TRACE_IT(j, 1);
@@ -626,7 +627,7 @@ __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBa
 // MMA warp i (0..3): issues the stages k with k % 4 == i into its partial accumulator (TMEM columns
 // 256 * buffer + 64 * i): one MMA per group in the row-stacked form, two (S x A, S x A_lo) in the
 // column-stacked form.
-template <bool CHECK, bool TR>
+template <bool CHECK, bool TR, bool RAW>
 __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
                             const CtaBars& cb, uint32_t tmem_base, int i, int lane,
                             volatile int* abort_flag) {
@@ -652,13 +653,13 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
     VBSR_PROF_ADD(p, 5, t_f);
     if (i == 0) VBSR_TRACE_IT(j, 2);
     tc_fence_after();
-    const int M = stack_m(it.nw()), h = it.h(), G = stage_groups(h, p.rhs);
-    const uint32_t T = uint32_t(stack_tile_bytes(p.rhs));
+    const int M = stack_m(it.nw()), h = it.h(), G = stage_groups(h, p.rhs, RAW);
+    const uint32_t T = uint32_t(stack_tile_bytes(p.rhs, RAW));
     const uint32_t tmem_d = tmem_base + uint32_t(256 * buf + 64 * i);
     // row-stacked: M = the group's interleaved A / A_lo rows (64 covers h <= 32), N = S's 2 rhs
     // rows; column-stacked: M = S's rows, N = the group's h rows of A (then of A_lo)
     const uint32_t idesc = TR ? tf32_idesc(h <= kTrM64MaxH ? 64 : 128, 2 * p.rhs)
-                              : tf32_idesc(kRawB ? p.rhs : M, h);
+                              : tf32_idesc(RAW ? p.rhs : M, h);
     uint32_t started = 0;
     for (const int kend = int(it.k0 + it.n); kk < kend; kk += kTcMmaWarps) {
       const int groups = it.stage_groups(kk - int(it.k0), G);
@@ -693,7 +694,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
               const uint32_t ag = sa + 32u * h * g, lo_off = 32u * h * groups;  // A_lo region
               tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag), idesc, started);          // S x A
               tc_mma_tf32(tmem_d, sdesc, sw32_desc(ag + lo_off), idesc, 1u);      // S x A_lo
-              if (kRawB)  // B_lo x A, into the same rows: S's lo rows follow all groups' raw rows
+              if (RAW)  // B_lo x A, into the same rows: S's lo rows follow all groups' raw rows
                 tc_mma_tf32(tmem_d, sw32_desc(ss + T * (groups + g)), sw32_desc(ag), idesc, 1u);
               started = 1u;
             }
@@ -744,10 +745,10 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 __host__ __device__ constexpr int bs_groups(int rhs) {
   return rhs <= 32 ? VBSR_BS_GROUPS_NARROW : VBSR_BS_GROUPS;
 }
-template <int RHS>
+template <int RHS, bool RAW>
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
                                                      float* __restrict__ out) {
-  constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS);
+  constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS, RAW);
   constexpr int kBsGroups = bs_groups(RHS);
   constexpr int per_col = 2 * kBsGroups;  // float4s per column run
   __shared__ float4 buf[RHS * per_col];  // [c][kg][2 x float4]: up to 32 KB
@@ -775,7 +776,7 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
       if (row_stacked(RHS)) {  // rows c: raw B of column c; rows RHS + c: its lo part
         c = row % RHS;
         lo = row >= RHS;
-      } else if (kRawB) {  // raw rows only: row c is column c
+      } else if (RAW) {  // raw rows only: row c is column c
         c = row;
         lo = false;
       } else {  // per quadrant q: rows of hi, then rows of lo, of columns half*q ...
@@ -794,7 +795,8 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
   }
 }
 
-template <bool CHECK, bool TR>
+// TR: row-stacked form (rhs <= 32); RAW: column-stacked form with raw-B stacks.
+template <bool CHECK, bool TR, bool RAW>
 __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t slots = (smem_addr(smem_raw) + 1023u) & ~1023u;  // 1024-aligned ring
@@ -839,14 +841,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
 
   using RL = Roles<TR>;
   if (warp < RL::mma0)
-    tc_split_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
+    tc_split_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < RL::feeder0)
-    tc_mma_warp<CHECK, TR>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane, &abort_flag);
+    tc_mma_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane,
+                                &abort_flag);
   else if (warp < RL::epi0)
-    tc_feeder<CHECK>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
+    tc_feeder<CHECK, RAW>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
   else  // the epilogue warps: TMEM quadrant warp % 4
-    tc_epi_warp<CHECK, TR>(p, task, cb, tmem_base, warp & 3, (warp - RL::epi0) >> 2, lane,
-                           &abort_flag);
+    tc_epi_warp<CHECK, TR, RAW>(p, task, cb, tmem_base, warp & 3, (warp - RL::epi0) >> 2, lane,
+                                &abort_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
