@@ -350,6 +350,9 @@ struct vbsr_plan {
 
 namespace {
 
+#ifndef VBSR_RAW_B
+#define VBSR_RAW_B -1  // raw-B stacks for RHS 64: -1 chosen by size; 0 / 1 forced (development)
+#endif
 constexpr int kSmemBudget = 224 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
 
 // Per-team time model of one item: the bytes its stages move (A and B) plus a fixed cost per stage
@@ -388,9 +391,6 @@ vbsr_status build_schedule(vbsr_plan* p) {
   // Column-stacked form: raw-B stacks when the pre-split stacks (K x 512 bytes) would not stay in
   // L2 (a stack read then comes from DRAM, and raw halves those bytes); pre-split stacks below
   // that, where the reads hit L2 and the extra split work of raw would only cost time.
-#ifndef VBSR_RAW_B
-#define VBSR_RAW_B -1  // -1: by size; 0 / 1: forced (development)
-#endif
   constexpr int64_t kRawStackBytes = 64ll << 20;
   const bool big = (d.K / 8) * int64_t(stack_tile_bytes(rhs, false)) > kRawStackBytes;
   p->raw_b = !row_stacked(rhs) &&
