@@ -731,7 +731,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // groups through shared memory: it reads each RHS column's 8 * kBsGroups consecutive values
 // (coalesced), then writes the kBsGroups tiles (contiguous) with 16-byte stores.
 #ifndef VBSR_BS_GROUPS
-#define VBSR_BS_GROUPS 8
+#define VBSR_BS_GROUPS 16
 #endif
 #ifndef VBSR_BS_BLOCKS_PER_SM
 #define VBSR_BS_BLOCKS_PER_SM 8
