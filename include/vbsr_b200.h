@@ -148,7 +148,6 @@ enum { VBSR_KERNEL_AUTO = 0, VBSR_KERNEL_ROW_OWNED = 1, VBSR_KERNEL_SPLIT_ROW = 
 enum {
   VBSR_PLAN_BOUNDS_CHECK = 1u << 0, /* use the bounds-checked kernel build                  */
   VBSR_PLAN_NO_SPLIT = 1u << 1,     /* accepted for compatibility; no effect (no row splits) */
-  VBSR_PLAN_NARROW_STAGES = 1u << 2, /* accepted for compatibility; no effect               */
   /* RHS 64 only, results identical either way: force the raw-B operand stacks (the pre-pass
    * writes raw B rows, the kernel forms their lo parts) or the pre-split ones (hi and lo rows
    * from the pre-pass). By default the plan picks raw-B when the pre-split stacks, K x 512
@@ -176,8 +175,11 @@ vbsr_status vbsr_plan_destroy(vbsr_plan* p);
  * into the plan's buffer, then the SpMM) and returns. B is K x rhs and C is M x rhs, column-major
  * device buffers on the matrix's device. C is fully overwritten (rows with no blocks become 0). No
  * allocation, no host synchronisation. Concurrent calls on one plan from several host threads or
- * streams are safe when they pass the same B and different C; with different B use one plan per
- * stream (the pre-pass buffer belongs to the plan). Launch failures return VBSR_CUDA_ERROR
+ * streams are safe, with any B and C: the executes of one plan share its pre-pass buffer, so each
+ * one is ordered on the GPU after the plan's previous execute, whatever stream that used (an event
+ * the plan records; the host never waits). Inside a CUDA stream capture that cross-stream ordering
+ * is not added: executes captured on one stream are ordered by it, executes captured on several
+ * streams must be ordered by the graph's own dependencies. Launch failures return VBSR_CUDA_ERROR
  * (cudaGetLastError right after the launch). */
 vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr_stream_t stream);
 
@@ -191,9 +193,14 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
  * address (cudaGetSymbolAddress); make that first call before any stream capture. Each call clears
  * the array's used part first, and all calls share it, so calls that overlap on the GPU race on it
  * (their C results are unaffected, only the reported status/timestamps). With cta_times == NULL the
- * call is asynchronous like vbsr_plan_execute; otherwise it synchronises `stream`, copies up to
- * cta_times_len timestamps ((start, end) pairs in ns, per CTA) and returns VBSR_TIMEOUT or
- * VBSR_BOUNDS_VIOLATION if the kernel recorded one. */
+ * call is asynchronous like vbsr_plan_execute and reports no kernel-side error: a VBSR_TIMEOUT or
+ * VBSR_BOUNDS_VIOLATION recorded by that launch is overwritten by the next call's clearing, so a
+ * caller that needs the kernel's status uses the reporting form. With cta_times != NULL the call
+ * synchronises `stream`, copies up to cta_times_len timestamps ((start, end) pairs in ns, per CTA)
+ * and returns VBSR_TIMEOUT, VBSR_BOUNDS_VIOLATION or (any other nonzero status word)
+ * VBSR_CUDA_ERROR if the kernel recorded one. B or C not 16-byte aligned take a plain row kernel
+ * that records neither status nor timestamps: the reporting form then waits for it and returns
+ * zeros in cta_times. */
 vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float* C,
                                       vbsr_stream_t stream, uint64_t* cta_times,
                                       int cta_times_len);
@@ -207,7 +214,8 @@ vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out);
  * enqueued since the last check. */
 vbsr_status vbsr_plan_check_status(const vbsr_plan* p, vbsr_stream_t stream);
 
-/* Human-readable schedule summary: classes, tasks, split rows, shared memory per CTA. */
+/* Human-readable schedule summary: RHS, items, pipeline stages, CTAs, ring depth, shared memory
+ * per CTA and the kernel form. */
 vbsr_status vbsr_plan_describe(const vbsr_plan* p, char* buf, size_t buf_len);
 
 /* Test hook (no reference counterpart): makes the next executions stall one pipeline stage on
@@ -220,7 +228,7 @@ vbsr_status vbsr_plan_set_debug(vbsr_plan* p, int drop_stage, int64_t wait_limit
  * executions record, for every CTA, its start and end on the GPU's global nanosecond timer.
  * If `out` is not NULL, synchronises `stream` and copies up to out_len values (start, end pairs in
  * CTA order) from the last timed execution; values past the first 2 * tasks are 16 per-CTA cycle
- * counters that only an instrumented build (VBSR_PROF) fills, zero otherwise. */
+ * counters that only an instrumented development build fills, zero otherwise. */
 vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int out_len,
                                  vbsr_stream_t stream);
 /* Per-task schedule facts (a tuning aid): team size in warps and the planner's cost estimate of

@@ -24,8 +24,10 @@ REF_LIB = os.path.join(_HERE, "_ref", "libvbsr_ref.so")
 REF_GPU_LIB = os.path.join(_HERE, "_ref", "libvbsr_ref_gpu.so")
 
 
-def build(ref_dir: str = "/root/reference") -> None:
-    """Builds the oracle (and the reference, when its sources exist) with oracle/Makefile."""
+def build(ref_dir: str | None = None) -> None:
+    """Builds the oracle (and the reference, when its checkout is given by `ref_dir` or the
+    environment variable VBSR_REFERENCE_DIR) with oracle/Makefile."""
+    ref_dir = ref_dir or os.environ.get("VBSR_REFERENCE_DIR", "")
     subprocess.run(["make", "-s", "-C", _HERE, "REF=" + ref_dir], check=True)
 
 

@@ -36,6 +36,7 @@ def test_noalloc_matches_execute_twice(cuda, rhs):
     stream = torch.cuda.Stream()
     for call in range(2):
         out = torch.full((n,), float("nan"), device="cuda")
+        stream.wait_stream(torch.cuda.current_stream())  # the NaN fill lands before the kernel
         times = p.execute_noalloc(dB, out, stream, report=True)
         got = out.cpu().numpy()
         assert_within_bound(host, B, rhs, got)
@@ -44,6 +45,7 @@ def test_noalloc_matches_execute_twice(cuda, rhs):
         assert np.all(times[:, 1] >= times[:, 0]) and np.all(times[:, 0] > 0)
     # asynchronous form (no reporting) gives the same C as well
     out = torch.full((n,), float("nan"), device="cuda")
+    stream.wait_stream(torch.cuda.current_stream())
     p.execute_noalloc(dB, out, stream)
     stream.synchronize()
     assert np.array_equal(out.cpu().numpy().view(np.uint32), ref_h.view(np.uint32))

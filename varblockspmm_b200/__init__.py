@@ -182,7 +182,6 @@ STREAM_VALUES = 0xA11CE
 STREAM_DENSE = 0xB0B
 PLAN_BOUNDS_CHECK = 1
 PLAN_NO_SPLIT = 2
-PLAN_NARROW_STAGES = 4
 PLAN_STACKS_RAW = 8        # RHS 64: force raw-B operand stacks (same results)
 PLAN_STACKS_PRESPLIT = 16  # RHS 64: force pre-split operand stacks (same results)
 PLAN_DIAG_SKIP_COPIES = 1 << 8  # diagnostics only: C is wrong
@@ -472,9 +471,10 @@ class Plan:
 
     def execute_noalloc(self, B, C_out, stream=None, report: bool = False):
         """Like execute, but allocates nothing: status words and CTA timestamps live in a fixed
-        array inside the library (see vbsr_plan_execute_noalloc). With report=True, waits for the
-        launch, raises on a recorded timeout or bounds violation, and returns the (start, end)
-        timestamps per CTA."""
+        array inside the library (see vbsr_plan_execute_noalloc). With report=False the call is
+        asynchronous and reports no kernel-side error. With report=True, waits for the launch,
+        raises on a recorded timeout or bounds violation, and returns the (start, end) timestamps
+        per CTA (zeros when B or C is not 16-byte aligned: that path records none)."""
         if not report:
             _check(_lib.vbsr_plan_execute_noalloc(self._h, _dev_ptr(B), _dev_ptr(C_out),
                                                   _stream_ptr(stream), None, 0))

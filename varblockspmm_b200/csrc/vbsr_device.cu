@@ -346,13 +346,16 @@ struct vbsr_plan {
   std::string summary;
   std::vector<int> task_warps;      // team size of every task
   std::vector<double> task_cost;    // planner's cost model: the task's most loaded team
+  // Every execute writes the operand stacks into d_bstack and the SpMM reads them, so two executes
+  // of one plan must not overlap on the GPU. Each execute waits (cudaStreamWaitEvent) for the
+  // completion event of the previous one, on whatever stream that ran, and records its own.
+  mutable std::mutex exec_mu;
+  cudaEvent_t done = nullptr;
+  mutable bool has_done = false;
 };
 
 namespace {
 
-#ifndef VBSR_RAW_B
-#define VBSR_RAW_B -1  // raw-B stacks for RHS 64: -1 chosen by size; 0 / 1 forced (development)
-#endif
 constexpr int kSmemBudget = 224 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
 
 // Per-team time model of one item: the bytes its stages move (A and B) plus a fixed cost per stage
@@ -396,7 +399,6 @@ vbsr_status build_schedule(vbsr_plan* p) {
   p->raw_b = !row_stacked(rhs) &&
              ((p->flags & VBSR_PLAN_STACKS_RAW)        ? true
               : (p->flags & VBSR_PLAN_STACKS_PRESPLIT) ? false
-              : VBSR_RAW_B >= 0                        ? VBSR_RAW_B != 0
                                                        : big);
   const int R = d.block_rows;
   std::vector<int> row_stages(R);
@@ -543,6 +545,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
     VBSR_CUDA(cudaMemcpy(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
                          cudaMemcpyHostToDevice));
   VBSR_CUDA(cudaMemset(p->d_status, 0, kStatusWords * sizeof(int)));
+  VBSR_CUDA(cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming));
   VBSR_CUDA(set_kernel_attrs());
   return VBSR_OK;
 }
@@ -556,6 +559,7 @@ void free_plan(vbsr_plan* p) {
   cudaFree(p->d_tasks);
   cudaFree(p->d_status);
   cudaFree(p->d_timing);
+  if (p->done != nullptr) cudaEventDestroy(p->done);
   delete p;
 }
 
@@ -601,6 +605,25 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
                                    : spmm_tc_kernel<false, false, false>, kp);
 }
 
+// Enqueues one execute on `stream` after the plan's previous execute (on any stream) has finished
+// with the operand-stack buffer, then records its own completion. Waiting on an event recorded
+// outside a stream capture is not allowed inside one, so a captured execute is ordered only by the
+// graph the caller builds (executes captured on one stream are ordered by that stream).
+vbsr_status enqueue_execute(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(p->exec_mu);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  VBSR_CUDA(cudaStreamIsCapturing(stream, &cs));
+  const bool capturing = cs != cudaStreamCaptureStatusNone;
+  if (!capturing && p->has_done) VBSR_CUDA(cudaStreamWaitEvent(stream, p->done, 0));
+  launch_spmm(p, kp, stream);
+  VBSR_CUDA(cudaGetLastError());
+  if (!capturing) {
+    VBSR_CUDA(cudaEventRecord(p->done, stream));
+    p->has_done = true;
+  }
+  return VBSR_OK;
+}
+
 // Launch parameters of one execute: the plan's schedule and the caller's B and C.
 vbsr_status fill_params(const vbsr_plan* p, const float* B, float* C, int* status,
                         unsigned long long* timing, KernelParams* kp) {
@@ -620,6 +643,8 @@ vbsr_status fill_params(const vbsr_plan* p, const float* B, float* C, int* statu
   kp->drop_stage = p->drop_stage;
   kp->wait_limit = p->wait_limit;
   kp->timing = timing;
+  // per-CTA cycle counters of instrumented builds follow the timestamps (plan-owned buffer only)
+  kp->prof = (timing != nullptr && timing == p->d_timing) ? timing + 2 * p->num_tasks : nullptr;
   kp->diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
   return VBSR_OK;
 }
@@ -771,9 +796,7 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
   KernelParams kp;
   vbsr_status st = fill_params(p, B, C, p->d_status, p->timing_on ? p->d_timing : nullptr, &kp);
   if (st != VBSR_OK) return st;
-  launch_spmm(p, kp, s);
-  VBSR_CUDA(cudaGetLastError());
-  return VBSR_OK;
+  return enqueue_execute(p, kp, s);
 }
 
 // ---- execute without allocating ---------------------------------------------------------------------
@@ -829,9 +852,15 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
   DeviceGuard guard(p->device);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if ((reinterpret_cast<uintptr_t>(B) & 15u) || (reinterpret_cast<uintptr_t>(C) & 15u)) {
-    vbsr_device_matrix view;  // unaligned buffers: the plain-load row kernel (no scratch)
+    // unaligned buffers: the plain-load row kernel, which uses no scratch and records no status
+    // and no timestamps; in reporting mode the call still waits and reports zero timestamps
+    vbsr_device_matrix view;
     vbsr_matrix_device_view(p->m, &view);
-    return launch_view_kernel(&view, B, C, p->rhs, s, false);
+    const vbsr_status st = launch_view_kernel(&view, B, C, p->rhs, s, false);
+    if (st != VBSR_OK || cta_times == nullptr) return st;
+    if (cta_times_len > 0) std::memset(cta_times, 0, size_t(cta_times_len) * sizeof(uint64_t));
+    VBSR_CUDA(cudaStreamSynchronize(s));
+    return VBSR_OK;
   }
   if (p->num_tasks == 0) return VBSR_OK;
   unsigned long long* scratch = nullptr;
@@ -843,9 +872,8 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
   KernelParams kp;
   st = fill_params(p, B, C, reinterpret_cast<int*>(scratch), scratch + 2, &kp);
   if (st != VBSR_OK) return st;
-  launch_spmm(p, kp, s);
-  VBSR_CUDA(cudaGetLastError());
-  if (cta_times == nullptr) return VBSR_OK;
+  st = enqueue_execute(p, kp, s);
+  if (st != VBSR_OK || cta_times == nullptr) return st;
   // Reporting mode: wait for this launch, then return its status and CTA timestamps.
   int words[kStatusWords] = {0, 0, 0, 0};
   VBSR_CUDA(cudaMemcpyAsync(words, scratch, sizeof words, cudaMemcpyDeviceToHost, s));
@@ -858,6 +886,7 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
     return set_error(VBSR_TIMEOUT, "pipeline wait timed out in CTA " + std::to_string(words[kStatusInfo]));
   if (words[kStatusCode] == VBSR_BOUNDS_VIOLATION)
     return set_error(VBSR_BOUNDS_VIOLATION, "index out of bounds (info " + std::to_string(words[kStatusInfo]) + ")");
+  if (words[kStatusCode] != 0) return set_error(VBSR_CUDA_ERROR, "unknown device status");
   return VBSR_OK;
 }
 

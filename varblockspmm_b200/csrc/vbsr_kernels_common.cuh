@@ -27,6 +27,7 @@ struct KernelParams {
   int drop_stage;       // debug: stage number (team 0 of each CTA) whose copies are withheld
   long long wait_limit; // SM clocks a single wait may take before it is declared stalled
   u64* timing;          // optional: per CTA (start, end) global timer in ns
+  u64* prof;            // instrumented builds only (VBSR_PROF): 16 cycle counters per CTA
   int diag;             // VBSR_PLAN_DIAG_* bits (performance analysis only)
 };
 
@@ -162,32 +163,14 @@ __device__ __forceinline__ void record_status(int* status, int code, int info) {
 // mbarrier.try_wait suspends the warp in hardware while the phase is pending, so waiting warps do
 // not take issue slots from the warps that compute. Returns false if the CTA aborted or the wait
 // exceeded p.wait_limit SM clocks.
-#ifndef VBSR_WAIT_HINT_NS
-#define VBSR_WAIT_HINT_NS 20000u
-#endif
+constexpr unsigned kWaitHintNs = 20000u;  // suspend-time hint of one try_wait probe
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, const KernelParams& p,
                                            volatile int* abort_flag, int lane) {
-#ifdef VBSR_WAIT_LANE0
-  {
-    int ok = 0;
-    if (lane == 0) ok = mbar_try(bar, parity);
-    if (__shfl_sync(0xffffffffu, ok, 0)) {
-      __syncwarp();
-      return true;
-    }
-  }
-#endif
   if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
   const long long t0 = clock64();
   while (true) {
     // suspended in hardware for up to ~20 us per probe, so a waiting warp issues few instructions
-#if defined(VBSR_WAIT_TEST)
-    if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
-#elif defined(VBSR_WAIT_NOHINT)
-    if (__all_sync(0xffffffffu, mbar_try(bar, parity))) return true;
-#else
-    if (__all_sync(0xffffffffu, mbar_try_hint(bar, parity, VBSR_WAIT_HINT_NS))) return true;
-#endif
+    if (__all_sync(0xffffffffu, mbar_try_hint(bar, parity, kWaitHintNs))) return true;
     int stop = 0;
     if (lane == 0) {
       if (*abort_flag) {

@@ -219,38 +219,7 @@ struct CtaBars {
   uint32_t drain0;          // per MMA warp: end-of-kernel drain of its MMAs
 };
 
-// Optional cycle counters (instrumented builds only): per CTA 16 slots after the 2 * tasks
-// start/end timestamps of the timing buffer.
-#ifdef VBSR_PROF
-#define VBSR_PROF_T0(v) const long long v = clock64()
-#define VBSR_PROF_ADD(p, slot, t0)                                                          \
-  do {                                                                                     \
-    if ((p).timing && (threadIdx.x & 31) == 0)                                             \
-      atomicAdd((p).timing + 2 * gridDim.x + 16 * blockIdx.x + (slot),                     \
-                (unsigned long long)(clock64() - (t0)));                                   \
-  } while (0)
-#else
-#define VBSR_PROF_T0(v)
-#define VBSR_PROF_ADD(p, slot, t0) do { } while (0)
-#endif
-#ifdef VBSR_TRACE
-// development builds only: per-stage / per-item timestamps of one CTA
-__device__ long long g_trace[4096 * 8];
-__device__ long long g_trace_items[1024 * 4];
-#define VBSR_TRACE_ST(k, e)                                                                      \
-  do {                                                                                           \
-    if (blockIdx.x == VBSR_TRACE && (threadIdx.x & 31) == 0 && (k) < 4096)                       \
-      g_trace[(k) * 8 + (e)] = clock64();                                                        \
-  } while (0)
-#define VBSR_TRACE_IT(j, e)                                                                      \
-  do {                                                                                           \
-    if (blockIdx.x == VBSR_TRACE && (threadIdx.x & 31) == 0 && (j) < 1024)                       \
-      g_trace_items[(j) * 4 + (e)] = clock64();                                                  \
-  } while (0)
-#else
-#define VBSR_TRACE_ST(k, e) do { } while (0)
-#define VBSR_TRACE_IT(j, e) do { } while (0)
-#endif
+#include "vbsr_dev_instrument.cuh"
 
 // Feeder warp f: fills the slots of the stages k with k % kTcFeeders == f, each once the MMAs of
 // the slot's previous stage have completed.
@@ -467,9 +436,6 @@ __device__ __forceinline__ bool tc_epilogue_rows(const KernelParams& p, const Ct
   return true;
 }
 
-#ifndef VBSR_SPLIT_PASS
-#define VBSR_SPLIT_PASS 16
-#endif
 // Row-stacked form: the stage's A arrives as U = h G / 8 blocks of 8 rows (256 bytes), block u at
 // byte 256 u; it is spread in place so that block u sits at byte 512 u followed by its A_lo block.
 // Block u's destination covers the sources of blocks 2u and 2u + 1 only, so passes over the
@@ -478,7 +444,7 @@ __device__ __forceinline__ bool tc_epilogue_rows(const KernelParams& p, const Ct
 // the address bits below 256, which the move preserves.
 __device__ __forceinline__ void split_stage_rows(uint32_t sp, int groups, int h, int lane) {
   const int units = (h >> 3) * groups;
-  constexpr int kPassUnits = VBSR_SPLIT_PASS;  // blocks per pass: kPassUnits / 2 float4s per lane
+  constexpr int kPassUnits = 16;  // blocks per pass: kPassUnits / 2 float4s per lane
   for (int top = units; top > 0; top -= kPassUnits) {
     const int u0 = top > kPassUnits ? top - kPassUnits : 0;
     float4 x[kPassUnits / 2];
