@@ -2,14 +2,17 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload large|headline|wide|small|large16k]
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1, NCCL)
-    python bench.py --impl reference ...                  (the reference's CPU path, rank 0 only)
+    python bench.py --impl reference ...                  (the reference's CPU path, rank 0 only;
+                                                           loads the oracle library only)
 
 Workload (default `large`): 262144 x 262144 block rows/columns, high-variance
 block sizes {8,16,56,64} w.p. {.3,.2,.2,.3}, degree 16, random pattern, RHS 64, seed 1 (~22 GB of
 A). Block rows are partitioned over the ranks by balanced cost (vbsr_partition_rows); each rank
 builds its shard on its GPU (values generated on the device by the engine's counter-based
-generator, identical to the host generator), receives one replica of B from rank 0 over NCCL
-(setup, not timed) and runs Plan.execute on its shard. No collective runs inside the timed region.
+generator, identical to the host generator), receives its replica of B from rank 0 by peer copies
+over NVLink between CUDA-IPC-mapped buffers (setup, timed as `replicate`; no NCCL) and runs
+Plan.execute on its shard. No collective runs inside the timed region. After it, every block row of
+every shard is checked against the oracle on its own rank.
 
 Metric: effective HBM GB/s = compulsory bytes of the whole problem (reference VBSR format:
 A values + indices + B + C) / device time per step, max over ranks. One JSON line on rank 0, with
@@ -141,85 +144,120 @@ def make_structure(workload):
     return host, rhs
 
 
-# ---- CPU baseline ---------------------------------------------------------------------------------
-
-def cpu_sample_run(host, rhs, B, r1, threads, use_ref):
-    """One run of the CPU path over block rows [0, r1); returns (seconds, flops of the sample)."""
+def make_workload(workload):
+    """The workload's structure built by the oracle library alone (no engine library); its values
+    are regenerated per row slice."""
     import oracle
-    sub = host.row_slice(0, r1, values_seed=SEED)
-    flops = 2.0 * sub.values.size * rhs
-    t = time.perf_counter()
-    if use_ref:
-        oracle.ref_cpu_reference(sub, B, rhs, threads=threads)
-    else:
-        oracle.spmm(sub, B, rhs, threads=threads)
-    return time.perf_counter() - t, flops
+    rows, degree, dist, local, rhs, _ = WORKLOADS[workload]
+    return oracle.WorkloadMatrix(rows, rows, degree, dist, local, SEED), rhs
 
 
-def calibrate_cpu_rows(host, rhs, B, threads, use_ref, target_s):
-    """Block rows [0, r) whose CPU run takes about target_s seconds."""
-    r = min(host.block_rows, max(threads * 4, 64))
-    while True:
-        dt, _ = cpu_sample_run(host, rhs, B, r, threads, use_ref)
-        if dt >= 0.2 * target_s or r >= host.block_rows:
-            break
-        r = min(host.block_rows, r * 4)
-    return max(1, min(host.block_rows, int(r * target_s / max(dt, 1e-6))))
+def problem_bytes(host, rhs, r0=0, r1=None):
+    """Compulsory bytes of block rows [r0, r1) in the reference VBSR format (values, block_col,
+    value_off, row_ptr, row_size, row_scalar_off, col_size, col_scalar_off, B, C) and the useful
+    flops 2 * sum(h*w) * rhs; the same formula as vbsr_compulsory_bytes."""
+    r1 = host.block_rows if r1 is None else r1
+    b0, b1 = int(host.row_ptr[r0]), int(host.row_ptr[r1])
+    hw = float(host.value_off[b1] - host.value_off[b0])
+    nnzb, R, S = float(b1 - b0), float(r1 - r0), float(host.block_cols)
+    M = float(host.row_scalar_off[r1] - host.row_scalar_off[r0])
+    K = float(host.col_scalar_off[-1])
+    return (4 * hw + 4 * nnzb + 8 * (nnzb + 1) + 4 * (R + 1) + 4 * R + 8 * (R + 1) + 4 * S
+            + 8 * (S + 1) + 4 * K * rhs + 4 * M * rhs), 2 * hw * rhs
 
 
-def cpu_baseline(host, rhs, B, problem_bytes, total_flops, target_s=12.0):
+# ---- CPU reference path -----------------------------------------------------------------------
+
+class _PortRunner:
+    """The oracle's C restatement (bit-identical to the reference's cpu_reference), timed the way
+    oracle.RefTimer times the reference itself: run() returns the computation's seconds."""
+
+    def __init__(self, host, B, rhs, threads):
+        self.host, self.B, self.rhs, self.threads = host, B, rhs, threads
+
+    def run(self, C_out=None):
+        import oracle
+        t = time.perf_counter()
+        oracle.spmm(self.host, self.B, self.rhs, threads=self.threads)
+        return time.perf_counter() - t
+
+    def close(self):
+        pass
+
+
+def cpu_reference_timing(host, rhs, B, warmup, repeats, min_frac=0.05, min_run_s=1.0):
+    """The reference's own cpu_reference (oracle/_ref, compiled unchanged from the reference
+    sources; the oracle's restatement when that is absent) on all host threads, on block rows
+    [0, r) of the workload: at least `min_frac` of its flops and at least `min_run_s` per run. The
+    sample's inputs (values, the per-thread row-slice HostMatrix parts and the std::vector copy of
+    B the reference API takes) are built before timing; each timed run is only the cpu_reference
+    calls. Returns (median seconds per sample, sample flops, details)."""
     import oracle
+    threads = oracle.host_threads()
     use_ref = oracle.ref_available()
-    threads = os.cpu_count() or 1
-    r = calibrate_cpu_rows(host, rhs, B, threads, use_ref, target_s)
-    dt, flops = cpu_sample_run(host, rhs, B, r, threads, use_ref)
-    est_full = dt * total_flops / flops
-    return {"value": problem_bytes / est_full / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "reference" if use_ref else "port",
-            "sample": f"block rows [0,{r}) of the workload ({100 * flops / total_flops:.2f}% of its "
-                      f"flops) in {dt:.2f} s on {threads} threads, extrapolated to the full "
-                      f"problem by flops",
-            "sample_seconds": dt}
+    rows = host.block_rows
+    total = host.flops(rhs)
+
+    def runner_for(r):
+        sub = host.row_slice(0, r)
+        return (oracle.RefTimer(sub, B, rhs, threads) if use_ref
+                else _PortRunner(sub, B, rhs, threads))
+
+    r = min(rows, max(threads, int(np.ceil(min_frac * rows))))
+    while host.flops(rhs, 0, r) < min_frac * total and r < rows:
+        r = min(rows, r + max(1, rows // 100))
+    runner = runner_for(r)
+    dt = runner.run()
+    if dt < min_run_s and r < rows:
+        r = min(rows, int(np.ceil(r * min_run_s / max(dt, 1e-6) * 1.1)))
+        runner.close()
+        runner = runner_for(r)
+    for _ in range(warmup):
+        runner.run()
+    times = [runner.run() for _ in range(max(1, repeats))]
+    runner.close()
+    flops = host.flops(rhs, 0, r)
+    med = statistics.median(times)
+    return med, flops, {
+        "kind": "reference" if use_ref else "port", "cores": threads, "rows": r,
+        "flops_frac": flops / total, "runs": len(times), "run_s": times}
 
 
 def run_reference_arm(args):
     """--impl reference: the reference's own cpu_reference (oracle/_ref, compiled unchanged from
     the reference sources) or, if that library is absent, the bit-identical C restatement, with all
-    host threads, on bounded samples of the same workload. Rank 0 only."""
+    host threads, on samples of the same workload (every step one timed sample run, at least 5% of
+    the workload's flops), extrapolated to the whole workload by flops. Rank 0 only. The inputs come
+    from the oracle library's own generator: nothing of the engine is loaded in this arm."""
     rank, world, _ = rank_env()
     if rank != 0:
         return 0
     import oracle
-    import varblockspmm_b200 as vb
-    host, rhs = make_structure(args.workload)
-    problem_bytes, total_flops = vb.compulsory_bytes(host, rhs)
-    B = vb.fill_uniform(SEED, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
-    use_ref = oracle.ref_available()
-    threads = os.cpu_count() or 1
-    per_step = max(0.3, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
-    r = calibrate_cpu_rows(host, rhs, B, threads, use_ref, per_step)
-    for _ in range(args.warmup):
-        cpu_sample_run(host, rhs, B, r, threads, use_ref)
-    times = []
-    flops = 0.0
-    for _ in range(args.steps):
-        dt, flops = cpu_sample_run(host, rhs, B, r, threads, use_ref)
-        times.append(dt)
-    med = statistics.median(times)
+    host, rhs = make_workload(args.workload)
+    pbytes, total_flops = problem_bytes(host, rhs)
+    B = oracle.fill_uniform(SEED, oracle.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    per_step = max(0.5, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
+    med, flops, info = cpu_reference_timing(host, rhs, B, args.warmup, args.steps,
+                                            min_run_s=per_step)
     est_full_s = med * total_flops / flops
-    value = problem_bytes / est_full_s / 1e9
+    value = pbytes / est_full_s / 1e9
+    sample = (f"block rows [0,{info['rows']}) of the workload ({100 * info['flops_frac']:.1f}% of "
+              f"its flops) per step, median of {info['runs']} timed runs {med:.3f} s on "
+              f"{info['cores']} threads (cpu_reference calls only; inputs prepared before "
+              f"timing), extrapolated to the whole workload by flops")
     line = {
         "metric": "spmm_effective_hbm_GBps", "impl": "reference", "value": value, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": est_full_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)",
-        "config": {"workload": WORKLOADS[args.workload][5], "rhs": rhs,
-                   "block_rows": host.block_rows, "compulsory_bytes": problem_bytes},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads,
-                         "kind": "reference" if use_ref else "port",
-                         "sample": f"block rows [0,{r}) per step "
-                                   f"({100 * flops / total_flops:.2f}% of the flops), "
-                                   f"median {med:.3f} s, extrapolated by flops"},
+        "config": {"workload": WORKLOADS[args.workload][5], "block_rows": host.block_rows,
+                   "nnzb": host.nnzb, "rhs": rhs, "compulsory_bytes": pbytes,
+                   "useful_flops": total_flops},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": info["cores"],
+                         "kind": info["kind"], "sample": sample,
+                         "sample_seconds_median": med,
+                         "sample_seconds_min": min(info["run_s"]),
+                         "sample_seconds_max": max(info["run_s"])},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -228,27 +266,26 @@ def run_reference_arm(args):
 
 # ---- GPU arm --------------------------------------------------------------------------------------
 
-def sampled_parity(host, rhs, row_range, dC, B_host, n_rows=12):
-    """Size-independent parity at full size: a deterministic sample of this rank's block rows is
-    recomputed by the oracle (values regenerated from the counter stream) and compared under
-    |C - C_ref| <= 1e-5 * sum|a||b|. Returns (max error/limit ratio, violations)."""
+def full_parity(work, rhs, r0, r1, C_host, B_host, threads, slice_rows=4096):
+    """Every block row of [r0, r1) against the oracle, after the timed region: the rows' values are
+    regenerated by the oracle library's own generator slice by slice (host memory stays bounded)
+    and each slice of C is compared under |C - C_ref| <= 1e-5 * sum|a||b| with all `threads`.
+    C_host is the rank's C block, column-major with ld = its scalar row count."""
     import oracle
-    import torch
-    r0, r1 = row_range
-    if r1 <= r0:
-        return 0.0, 0
-    rng = np.random.default_rng(1234 + r0)
-    picks = sorted(set([r0, r1 - 1] + list(rng.integers(r0, r1, n_rows))))
-    M_r = int(host.row_scalar_off[r1] - host.row_scalar_off[r0])
-    Cv = dC.view(rhs, M_r)
+    t0 = time.perf_counter()
+    off = work.row_scalar_off
+    M_r = int(off[r1] - off[r0])
+    Cv = np.asarray(C_host)[:M_r * rhs].reshape(rhs, M_r)
     worst, bad = 0.0, 0
-    for i in picks:
-        sub = host.row_slice(i, i + 1, values_seed=SEED)
-        a = int(host.row_scalar_off[i] - host.row_scalar_off[r0])
-        got = Cv[:, a:a + int(host.row_size[i])].contiguous().cpu().numpy().reshape(-1)
-        ratio, _, nb = oracle.compare(sub, B_host, rhs, got, threads=1)
-        worst, bad = max(worst, ratio), bad + nb
-    return worst, bad
+    for a in range(r0, r1, slice_rows):
+        b = min(r1, a + slice_rows)
+        sub = work.row_slice(a, b)
+        c0, c1 = int(off[a] - off[r0]), int(off[b] - off[r0])
+        got = np.ascontiguousarray(Cv[:, c0:c1]).reshape(-1)
+        ratio, _, nb = oracle.compare(sub, B_host, rhs, got, threads=threads)
+        worst, bad = max(worst, ratio), bad + int(nb)
+    return {"rows_checked": r1 - r0, "max_err_over_bound": worst, "violations": bad,
+            "seconds": time.perf_counter() - t0, "threads": threads}
 
 
 def gathered_parity(host, rhs, bounds, rank, world, dC, B_host, per_shard=4):
@@ -315,9 +352,12 @@ def cta_time_stats(plan, B, C, stream):
 
 
 def time_headline(vb, torch, stream, peak, steps=200, warmup=10):
-    """BASELINE config 3 on this GPU: per-launch device time with L2 flushed between launches."""
+    """BASELINE config 3 on this GPU: per-launch device time with L2 flushed between launches,
+    every block row checked against the oracle afterwards."""
+    import oracle
     host, rhs = make_structure("headline")
-    problem_bytes, flops = vb.compulsory_bytes(host, rhs)
+    work, _ = make_workload("headline")
+    pbytes, flops = vb.compulsory_bytes(host, rhs)
     m = vb.Matrix(host, rows=(0, host.block_rows), generated_seed=SEED)
     p = vb.Plan(m, vb.PlanOptions(rhs))
     B = torch.empty(host.scalar_cols() * rhs, device="cuda")
@@ -335,61 +375,95 @@ def time_headline(vb, torch, stream, peak, steps=200, warmup=10):
             p.execute(B, Cd, stream)
             ev[i][1].record(stream)
     stream.synchronize()
+    p.check_status(stream)
     ts = sorted(a.elapsed_time(b) for a, b in ev)
     med = ts[len(ts) // 2]
     p95 = ts[min(len(ts) - 1, int(len(ts) * 0.95))]
-    B_host = vb.fill_uniform(SEED, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
-    ratio, bad = sampled_parity(host, rhs, (0, host.block_rows), Cd, B_host, n_rows=64)
-    gbs = problem_bytes / (med * 1e-3) / 1e9
+    B_host = oracle.fill_uniform(SEED, oracle.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    parity = full_parity(work, rhs, 0, host.block_rows, Cd.cpu().numpy(), B_host,
+                         oracle.host_threads())
+    gbs = pbytes / (med * 1e-3) / 1e9
     return {"workload": WORKLOADS["headline"][5], "median_ms": med, "p95_ms": p95,
-            "GBps": gbs, "frac_of_measured_hbm": gbs / peak, "compulsory_bytes": problem_bytes,
+            "GBps": gbs, "frac_of_measured_hbm": gbs / peak, "compulsory_bytes": pbytes,
             "useful_TFLOPs": flops / (med * 1e-3) / 1e12, "l2": "flushed before every launch",
-            "plan": p.describe(), "parity_max_ratio": ratio, "parity_violations": bad,
+            "plan": p.describe(), "parity": parity,
             "cta_time": cta_time_stats(p, B, Cd, stream)}
 
 
 def run_gpu_arm(args):
     import torch
     import torch.distributed as dist
+    import oracle
     import varblockspmm_b200 as vb
+    from varblockspmm_b200.replica import PeerReplica, copy_async
 
     rank, world, local = rank_env()
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     if world != args.gpus:
         print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
     torch.cuda.set_device(local)
+    hostgrp = None
     if world > 1:
+        # NCCL only for the max-over-ranks reductions and the verification gather of C; the
+        # data path (B replication) is peer copies ordered by barriers on a gloo group
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        hostgrp = dist.new_group(backend="gloo")
     stream = torch.cuda.Stream()
     peak, peak_kind = measured_hbm_peak()
 
     host, rhs = make_structure(args.workload)
-    problem_bytes, total_flops = vb.compulsory_bytes(host, rhs)
+    work, _ = make_workload(args.workload)
+    assert np.array_equal(work.block_col, host.block_col) and \
+        np.array_equal(work.value_off, host.value_off), "oracle and engine structures differ"
+    pbytes, total_flops = vb.compulsory_bytes(host, rhs)
     bounds = vb.partition_rows(host, world, rhs)
     r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
     rank_bytes, rank_flops = vb.compulsory_bytes(host, rhs, r0, r1)
     M_r = int(host.row_scalar_off[r1] - host.row_scalar_off[r0])
     K = host.scalar_cols()
+    nB = K * rhs
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=hostgrp)
+        torch.cuda.synchronize()
+
+    def max_over_ranks(*vals):
+        t = torch.tensor(list(vals), dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
 
     t_setup = time.perf_counter()
     m = vb.Matrix(host, device=local, rows=(r0, r1), generated_seed=SEED)
     plan = vb.Plan(m, vb.PlanOptions(rhs))
-    dB = torch.empty(K * rhs, device="cuda")
+    # two B buffers and two C buffers: buffer 0 for the device-timed steps, both for the pipelined
+    # end-to-end steps
+    rep = None
+    if world > 1:
+        rep = PeerReplica(nB, rank, world, local, hostgrp, buffers=2)
+        bptr = [rep.ptr(0), rep.ptr(1)]
+    else:
+        dBs = [torch.empty(nB, device="cuda") for _ in range(2)]
+        bptr = [t.data_ptr() for t in dBs]
     torch.cuda.synchronize()
-    t_rep0 = time.perf_counter()
+    replicate = None
     if rank == 0:
-        vb.fill_uniform_device(SEED, vb.STREAM_DENSE, 0, dB.numel(), dB, stream)
+        vb.fill_uniform_device(SEED, vb.STREAM_DENSE, 0, nB, bptr[0], stream)
         stream.synchronize()
     if world > 1:
-        dist.broadcast(dB, src=0)  # B replica over NVLink (setup; not timed as SpMM)
-    torch.cuda.synchronize()
-    replicate_ms = (time.perf_counter() - t_rep0) * 1e3
+        barrier()
+        t_rep0 = time.perf_counter()
+        got = rep.replicate_from(0, 0, stream)
+        rep_ms = (time.perf_counter() - t_rep0) * 1e3
+        rep_ms_max, = max_over_ranks(rep_ms)
+        replicate = {"ms": rep_ms_max, "bytes_per_rank": 4 * nB,
+                     "GBps_per_rank": 4 * nB / (rep_ms_max * 1e-3) / 1e9,
+                     "how": "peer copies over NVLink between CUDA-IPC-mapped replicas (scatter "
+                            "from rank 0, then every chunk from its owner), host barriers on a "
+                            "gloo group; no NCCL; host-timed including two barriers"}
     dC = torch.empty(max(1, M_r * rhs), device="cuda")
     setup_s = time.perf_counter() - t_setup
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
 
     flush = None
     if rank_bytes < 2 * L2_BYTES:
@@ -397,7 +471,7 @@ def run_gpu_arm(args):
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            plan.execute(dB, dC, stream)
+            plan.execute(bptr[0], dC, stream)
     barrier()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -410,7 +484,7 @@ def run_gpu_arm(args):
                 if flush is not None:
                     flush.fill_(float(i))
                 evs[i][0].record(stream)
-                plan.execute(dB, dC, stream)
+                plan.execute(bptr[0], dC, stream)
                 evs[i][1].record(stream)
             t1.record(stream)
         barrier()
@@ -420,84 +494,102 @@ def run_gpu_arm(args):
     p95 = launch_ms[min(len(launch_ms) - 1, int(len(launch_ms) * 0.95))]
     mean_launch = sum(launch_ms) / len(launch_ms)
     plan.check_status(stream)
-
-    stats = torch.tensor([total_ms, med, p95, mean_launch], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    total_ms, med_max, p95_max, _ = stats.tolist()
+    total_ms, med_max, p95_max = max_over_ranks(total_ms, med, p95)
     ms_per_step = total_ms / args.steps if flush is None else med_max
 
-    cta_stats = cta_time_stats(plan, dB, dC, stream)
+    cta_stats = cta_time_stats(plan, bptr[0], dC, stream)
 
     # ---- the SpMM kernel alone (roofline): a second plan that skips the B pre-pass ---------------
     kplan = vb.Plan(m, vb.PlanOptions(rhs), vb.PLAN_DIAG_SKIP_PREPASS)
+    kC = torch.empty_like(dC)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
-            kplan.execute(dB, dC, stream)
+            kplan.execute(bptr[0], kC, stream)
         for i in range(args.steps):
             if flush is not None:
                 flush.fill_(float(i))
             kev[i][0].record(stream)
-            kplan.execute(dB, dC, stream)
+            kplan.execute(bptr[0], kC, stream)
             kev[i][1].record(stream)
     stream.synchronize()
-    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
-    kt = torch.tensor([kernel_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(kt, op=dist.ReduceOp.MAX)
-    kernel_ms = float(kt.item())
-    del kplan
+    kernel_ms, = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps)
+    del kplan, kC
 
     # ---- end to end through the public API with host buffers ---------------------------------
-    # Every step uploads its B from pinned host memory, executes, and downloads its C. Steps are
-    # pipelined the way a serving loop would run them: B and C are double-buffered on the device,
-    # uploads run on one copy stream and downloads on another, so step i+1's upload overlaps step
-    # i's download (the two PCIe directions) and execute. The timed region spans the first upload
-    # to the last download.
-    B_host = vb.fill_uniform(SEED, vb.STREAM_DENSE, 0, K * rhs)
+    # Every step brings B from pinned host memory, executes, and brings this rank's C block back
+    # to pinned host memory. At N = 1 the whole of B crosses PCIe; at N > 1 each rank uploads only
+    # its own 1/N chunk of B and takes the other chunks from its peers over NVLink (peer copies,
+    # ordered by a host barrier), so PCIe traffic per rank shrinks with N. Steps are pipelined:
+    # B and C are double-buffered, uploads and downloads run on their own copy streams, and step
+    # i+1's upload overlaps step i's execute and download. The timed region spans the first
+    # upload to the last download on the device, max over ranks.
+    B_host = oracle.fill_uniform(SEED, oracle.STREAM_DENSE, 0, nB)
     hB = torch.from_numpy(B_host).pin_memory()
     hC = [torch.empty(max(1, M_r * rhs), dtype=torch.float32).pin_memory() for _ in range(2)]
-    dB2, dC2 = [dB, torch.empty_like(dB)], [dC, torch.empty_like(dC)]
+    dC2 = [dC, torch.empty_like(dC)]
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     e2e_steps = max(2, min(args.steps, 8))
-    ev = [[torch.cuda.Event() for _ in range(e2e_steps)] for _ in range(3)]  # uploaded, run, down
+    ev_up, ev_pull, ev_run, ev_down = ([torch.cuda.Event() for _ in range(e2e_steps)]
+                                       for _ in range(4))
+    h2d = d2h = nvl = 0
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s_in)
     for i in range(e2e_steps):
         b = i % 2
         if i >= 2:
-            s_in.wait_event(ev[1][i - 2])  # the execute that read dB[b] is done
-        with torch.cuda.stream(s_in):
-            dB2[b].copy_(hB, non_blocking=True)
-        ev[0][i].record(s_in)
-        stream.wait_event(ev[0][i])
+            s_in.wait_event(ev_run[i - 2])  # the execute that read B buffer b is done
+        if world > 1:
+            h2d += rep.upload_own_chunk(hB.data_ptr(), b, s_in)
+            ev_up[i].record(s_in)
+            ev_up[i].synchronize()
+            if i >= 1:
+                ev_pull[i - 1].synchronize()  # this rank's pulls of step i-1 are done
+            dist.barrier(group=hostgrp)  # every chunk of step i is in its owner's buffer
+            nvl += rep.pull_peers(b, s_in)
+        else:
+            copy_async(bptr[b], hB.data_ptr(), 4 * nB, s_in)
+            h2d += 4 * nB
+        ev_pull[i].record(s_in)
+        stream.wait_event(ev_pull[i])
         if i >= 2:
-            stream.wait_event(ev[2][i - 2])  # dC[b] of step i-2 is downloaded
-        plan.execute(dB2[b], dC2[b], stream)
-        ev[1][i].record(stream)
-        s_out.wait_event(ev[1][i])
+            stream.wait_event(ev_down[i - 2])  # C buffer b of step i-2 is downloaded
+        plan.execute(bptr[b], dC2[b], stream)
+        ev_run[i].record(stream)
+        s_out.wait_event(ev_run[i])
         with torch.cuda.stream(s_out):
             hC[b].copy_(dC2[b], non_blocking=True)
-        ev[2][i].record(s_out)
+        d2h += 4 * M_r * rhs
+        ev_down[i].record(s_out)
     e1.record(s_out)
     e1.synchronize()
     torch.cuda.synchronize()
-    del dB2, dC2
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device="cuda")
+    e2e_ms, = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
     if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_ms = float(e2e_ms.item())
+        barrier()
+    plan.check_status(stream)
 
-    # ---- parity at full size on a sample of rows -------------------------------------------------
-    ratio, bad = sampled_parity(host, rhs, (r0, r1), dC, B_host)
-    pr = torch.tensor([ratio, float(bad)], dtype=torch.float64, device="cuda")
+    # ---- parity: every block row of this rank's shard against the oracle ------------------------
+    threads = max(1, oracle.host_threads() // max(1, local_world))
+    parity = full_parity(work, rhs, r0, r1, dC.cpu().numpy(), B_host, threads)
+    pr = torch.tensor([parity["max_err_over_bound"], parity["violations"],
+                       parity["rows_checked"], parity["seconds"]], dtype=torch.float64,
+                      device="cuda")
     gathered = None
     if world > 1:
-        dist.all_reduce(pr, op=dist.ReduceOp.MAX)
+        pr_max = pr.clone()
+        dist.all_reduce(pr_max, op=dist.ReduceOp.MAX)
+        dist.all_reduce(pr, op=dist.ReduceOp.SUM)
+        pr[0], pr[3] = pr_max[0], pr_max[3]
         gathered = gathered_parity(host, rhs, bounds, rank, world, dC, B_host)
+    parity = {"rows_checked": int(pr[2].item()), "block_rows": host.block_rows,
+              "max_err_over_bound": pr[0].item(), "violations": int(pr[1].item()),
+              "seconds": pr[3].item(),
+              "how": "after the timed region, every block row of every rank's shard checked on "
+                     "its own rank against the oracle (values regenerated by the oracle library "
+                     "slice by slice), |C - C_ref| <= 1e-5 * sum|a||b| per element"}
 
     headline = None
     cpu = None
@@ -505,10 +597,20 @@ def run_gpu_arm(args):
         if args.workload != "headline":
             headline = time_headline(vb, torch, stream, peak)
         if not args.no_cpu_baseline:
-            cpu = cpu_baseline(host, rhs, B_host, problem_bytes, total_flops)
+            med_s, flops_s, info = cpu_reference_timing(work, rhs, B_host, 1, 3, min_run_s=2.0)
+            est_full = med_s * total_flops / flops_s
+            cpu = {"value": pbytes / est_full / 1e9, "unit": "GB/s", "cores": info["cores"],
+                   "kind": info["kind"],
+                   "sample": f"block rows [0,{info['rows']}) of the workload "
+                             f"({100 * info['flops_frac']:.1f}% of its flops), median of "
+                             f"{info['runs']} timed runs {med_s:.2f} s on {info['cores']} threads "
+                             f"(cpu_reference calls only), extrapolated by flops",
+                   "sample_seconds_median": med_s}
+    if rep is not None:
+        rep.close()
 
     if rank == 0:
-        value = problem_bytes / (ms_per_step * 1e-3) / 1e9
+        value = pbytes / (ms_per_step * 1e-3) / 1e9
         achieved = rank_bytes / (kernel_ms * 1e-3) / 1e9
         traffic = traffic_from_profiles(args.workload) if world == 1 else None
         line = {
@@ -519,7 +621,7 @@ def run_gpu_arm(args):
             "data": "synthetic (seeded spec generator; A values generated on device, bit-identical "
                     "to the host generator)",
             "config": {"workload": WORKLOADS[args.workload][5], "block_rows": host.block_rows,
-                       "nnzb": host.nnzb, "rhs": rhs, "compulsory_bytes": problem_bytes,
+                       "nnzb": host.nnzb, "rhs": rhs, "compulsory_bytes": pbytes,
                        "useful_flops": total_flops,
                        "parallelism": f"block-row partition over {world} GPU(s), B replicated",
                        "l2": ("inputs larger than L2 (A is %.1f GB)" % (rank_bytes / 1e9))
@@ -535,18 +637,22 @@ def run_gpu_arm(args):
                                  "SpMM kernel alone (events around executes of a plan that skips "
                                  "the B pre-pass); execute_frac covers pre-pass + kernel"},
             "useful_TFLOPs": total_flops / (ms_per_step * 1e-3) / 1e12,
-            "e2e": {"value": problem_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": K * rhs * 4,
-                    "d2h_bytes_per_step": M_r * rhs * 4, "steps": e2e_steps,
-                    "path": "pinned host B -> device, Plan.execute (C ABI), device C -> pinned "
-                            "host, every step; steps pipelined (double-buffered B and C, upload "
-                            "and download on separate copy streams)"},
+            "e2e": {"value": pbytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d // e2e_steps,
+                    "d2h_bytes_per_step": d2h // e2e_steps,
+                    "nvlink_bytes_per_step": nvl // e2e_steps, "steps": e2e_steps,
+                    "bytes_are": "per rank (rank 0)",
+                    "path": "pinned host B -> device (at N>1 the rank's own 1/N chunk; the other "
+                            "chunks by peer copies from the ranks that uploaded them), "
+                            "Plan.execute (C ABI), device C block -> pinned host, every step; "
+                            "steps pipelined (double-buffered B and C, separate copy streams)"},
             "gpu_launches": args.steps * plan.launch_count(),
             "clocks": clocks.summary(),
-            "parity": {"sampled_rows_max_err_over_bound": pr[0].item(),
-                       "violations": int(pr[1].item())},
-            "setup_s": setup_s, "replicate_ms": replicate_ms, "cta_time": cta_stats,
+            "parity": parity,
+            "setup_s": setup_s, "cta_time": cta_stats,
         }
+        if replicate:
+            line["replicate"] = replicate
         if gathered:
             line["gathered_parity"] = gathered
         if headline:

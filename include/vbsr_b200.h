@@ -355,6 +355,29 @@ vbsr_status vbsr_multi_plan_synchronize(vbsr_multi_plan* mp, float* max_ms);
  * the copies are done. */
 vbsr_status vbsr_multi_plan_gather_C(vbsr_multi_plan* mp, float* C, int dst_device);
 
+/* ---- Buffers shared between processes (one process per GPU) ------------------------------ */
+
+/* No reference counterpart (the reference is single-GPU). For the one-process-per-GPU layout: each
+ * rank allocates its B replica with vbsr_shared_buffer_create, exchanges the handle from
+ * vbsr_shared_buffer_export with the other ranks (any host channel), maps theirs with
+ * vbsr_shared_buffer_open, and fills its replica by copy-engine peer copies over NVLink
+ * (vbsr_copy_async, one cudaMemcpyAsync per chunk) with no NCCL involved. A mapped peer buffer is
+ * read-only by convention and must be closed (vbsr_shared_buffer_close) before its owner destroys
+ * it. Ordering between processes is the caller's (a host barrier after each copy phase). */
+typedef struct vbsr_shared_buffer vbsr_shared_buffer;
+typedef struct vbsr_ipc_handle {
+  unsigned char bytes[64];
+} vbsr_ipc_handle;
+vbsr_status vbsr_shared_buffer_create(int device, int64_t bytes, vbsr_shared_buffer** out);
+vbsr_status vbsr_shared_buffer_destroy(vbsr_shared_buffer* b);
+vbsr_status vbsr_shared_buffer_ptr(const vbsr_shared_buffer* b, void** ptr);
+vbsr_status vbsr_shared_buffer_export(const vbsr_shared_buffer* b, vbsr_ipc_handle* out);
+vbsr_status vbsr_shared_buffer_open(const vbsr_ipc_handle* handle, int device, void** peer_ptr);
+vbsr_status vbsr_shared_buffer_close(void* peer_ptr, int device);
+/* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream): host, device or mapped peer memory
+ * on either side. */
+vbsr_status vbsr_copy_async(void* dst, const void* src, int64_t bytes, vbsr_stream_t stream);
+
 /* Byte counts of the benchmark's roofline: the compulsory bytes of the reference VBSR format,
  * 4*sum(h*w) + 4*nnzb + 8*(nnzb+1) + 4*(R+1) + 4*R + 8*(R+1) + 4*S + 8*(S+1) + 4*K*N + 4*M*N,
  * and the useful flops 2*sum(h*w)*N, for block rows [row_begin, row_end) (the full column

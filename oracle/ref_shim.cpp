@@ -4,6 +4,7 @@
 // It lets the tests pin the CPU restatement (vbsr_oracle.c) and the engine's generator and
 // validation against the reference itself, and lets bench.py --impl reference time the
 // reference's own cpu_reference.
+#include <chrono>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -163,4 +164,82 @@ int ref_cpu_reference_rows(const int32_t* dims, const int32_t* row_ptr, const in
     return 1;
   }
 }
+
+// Timing form of ref_cpu_reference_rows for the benchmark's reference arm: ref_prepare builds,
+// outside any timed region, the per-thread row-slice HostMatrix parts and the std::vector copy of B
+// that vbsr::cpu_reference takes; ref_run then runs only the reference's cpu_reference calls (one
+// per thread, as independent calls on row slices) and reports their wall time; ref_release frees
+// the prepared state.
+struct RefPrepared {
+  std::vector<vbsr::HostMatrix> parts;
+  std::vector<int64_t> bases;  // first output row of each part within [r0, r1)
+  std::vector<float> input;
+  int rhs = 0;
+  int64_t ldc = 0;
+};
+
+void* ref_prepare(const int32_t* dims, const int32_t* row_ptr, const int32_t* block_col,
+                  const int32_t* row_size, const int32_t* col_size, const int64_t* row_off,
+                  const int64_t* col_off, const int64_t* value_off, const float* values,
+                  const int64_t* lens, const float* B, int rhs, int r0, int r1, int threads) {
+  try {
+    const vbsr::HostMatrix full = from_view(dims, row_ptr, block_col, row_size, col_size, row_off,
+                                            col_off, value_off, values, lens);
+    auto* h = new RefPrepared;
+    h->rhs = rhs;
+    h->input.assign(B, B + full.scalar_cols() * rhs);
+    h->ldc = full.row_scalar_off[r1] - full.row_scalar_off[r0];
+    const int rows = r1 - r0;
+    if (threads < 1) threads = 1;
+    if (threads > rows) threads = rows;
+    for (int t = 0; t < threads; ++t) {
+      const int a = r0 + int(int64_t(rows) * t / threads);
+      const int b = r0 + int(int64_t(rows) * (t + 1) / threads);
+      h->parts.push_back(row_slice(full, a, b));
+      h->bases.push_back(full.row_scalar_off[a] - full.row_scalar_off[r0]);
+    }
+    return h;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return nullptr;
+  }
+}
+
+int ref_run(void* handle, float* C, double* seconds) {
+  auto* h = static_cast<RefPrepared*>(handle);
+  const int threads = int(h->parts.size());
+  std::vector<std::vector<float>> outs(threads);
+  std::vector<std::string> errs(threads);
+  const auto t0 = std::chrono::steady_clock::now();
+  {
+    std::vector<std::thread> pool;
+    for (int t = 0; t < threads; ++t) {
+      pool.emplace_back([&, t] {
+        try {
+          outs[t] = vbsr::cpu_reference(h->parts[t], h->input, h->rhs);
+        } catch (const std::exception& e) {
+          errs[t] = e.what();
+        }
+      });
+    }
+    for (auto& th : pool) th.join();
+  }
+  const auto t1 = std::chrono::steady_clock::now();
+  if (seconds) *seconds = std::chrono::duration<double>(t1 - t0).count();
+  for (auto& e : errs)
+    if (!e.empty()) {
+      g_err = e;
+      return 1;
+    }
+  if (C != nullptr)
+    for (int t = 0; t < threads; ++t) {
+      const int64_t mt = h->parts[t].scalar_rows();
+      for (int n = 0; n < h->rhs; ++n)
+        std::memcpy(C + h->bases[t] + int64_t(n) * h->ldc, outs[t].data() + int64_t(n) * mt,
+                    size_t(mt) * sizeof(float));
+    }
+  return 0;
+}
+
+void ref_release(void* handle) { delete static_cast<RefPrepared*>(handle); }
 }

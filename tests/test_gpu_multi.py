@@ -110,3 +110,92 @@ def test_multi_plan_two_gpus(cuda):
     dC = torch.empty(M * rhs, device="cuda:0")
     mp.gather_C(dC)
     assert_within_bound(host, B, rhs, dC.cpu().numpy())
+
+
+def _replica_rank(rank, world, port, result_path):
+    import os
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.dirname(here))
+    sys.path.insert(0, here)
+    import json
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    import varblockspmm_b200 as vb
+    from varblockspmm_b200.replica import PeerReplica
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dev = rank % torch.cuda.device_count()
+    torch.cuda.set_device(dev)
+    rhs = 32
+    host = spec_case(700, 8, 2, False, 5)
+    K = host.scalar_cols()
+    B = vb.fill_uniform(5, vb.STREAM_DENSE, 0, K * rhs)
+    rep = PeerReplica(K * rhs, rank, world, dev, dist.group.WORLD, buffers=2)
+    out = {}
+    # setup form: the root holds B, everyone pulls
+    if rank == 0:
+        vb.fill_uniform_device(5, vb.STREAM_DENSE, 0, K * rhs, rep.ptr(0))
+        torch.cuda.synchronize()
+    rep.replicate_from(0, 0)
+    got = torch.empty(K * rhs, device="cuda")
+    from varblockspmm_b200.replica import copy_async
+    copy_async(got.data_ptr(), rep.ptr(0), 4 * K * rhs)
+    torch.cuda.synchronize()
+    out["replicate_equal"] = bool(np.array_equal(got.cpu().numpy().view(np.uint32),
+                                                 B.view(np.uint32)))
+    # per-step form: own chunk from pinned host memory, the rest from the peers
+    hB = torch.from_numpy(B).pin_memory()
+    up = rep.upload_own_chunk(hB.data_ptr(), 1)
+    torch.cuda.synchronize()
+    rep.barrier()
+    pulled = rep.pull_peers(1)
+    torch.cuda.synchronize()
+    rep.barrier()
+    out["bytes"] = up + pulled
+    copy_async(got.data_ptr(), rep.ptr(1), 4 * K * rhs)
+    torch.cuda.synchronize()
+    out["upload_pull_equal"] = bool(np.array_equal(got.cpu().numpy().view(np.uint32),
+                                                   B.view(np.uint32)))
+    # this rank's shard multiplied with the replica
+    bounds = vb.partition_rows(host, world, rhs)
+    r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
+    m = vb.Matrix(host, device=dev, rows=(r0, r1))
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    M_r = int(host.row_scalar_off[r1] - host.row_scalar_off[r0])
+    dC = torch.full((M_r * rhs,), float("nan"), device="cuda")
+    p.execute(rep.ptr(1), dC)
+    torch.cuda.synchronize()
+    p.check_status()
+    ratio, _, bad = oracle.compare(host, B, rhs, dC.cpu().numpy(), r0, r1)
+    out["violations"] = int(bad)
+    del p, m
+    rep.close()
+    with open(f"{result_path}.{rank}", "w") as f:
+        json.dump(out, f)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_peer_replica_two_processes(cuda, tmp_path):
+    """Two processes (one per GPU, or both on GPU 0 on a one-GPU box) share their B buffers
+    through CUDA IPC: replicate_from(root) and the upload-own-chunk + pull-peers form both give
+    every rank all of B bit for bit, and each rank's shard multiplied with its replica meets the
+    bound."""
+    import json
+    import socket
+    import torch.multiprocessing as tmp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    base = str(tmp_path / "rank")
+    tmp.start_processes(_replica_rank, args=(2, port, base), nprocs=2, join=True,
+                        start_method="spawn")
+    for r in range(2):
+        out = json.load(open(f"{base}.{r}"))
+        assert out["replicate_equal"] and out["upload_pull_equal"], out
+        assert out["violations"] == 0

@@ -52,3 +52,43 @@ def test_oracle_vs_live_reference_threaded():
     a = oracle.spmm(host, B, 64, threads=4)
     b = oracle.ref_cpu_reference(host, B, 64, threads=3)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("case", [(256, 256, 4, 0, True, 1), (1024, 1024, 16, 3, False, 1),
+                                  (4096, 4096, 8, 2, False, 1), (1024, 1024, 8, 1, True, 7),
+                                  (300, 40, 16, 2, False, 3)])
+def test_workload_generator_matches_engine(case):
+    """The oracle's own workload generator (used by the benchmark's reference arm, which must not
+    load the engine) gives the engine generator's spec-profile matrices bit for bit."""
+    rows, cols, degree, dist, local, seed = case
+    w = oracle.WorkloadMatrix(rows, cols, degree, dist, local, seed, with_values=True)
+    e = vb.generate(vb.GeneratorOptions(rows, cols, degree, 32, vb.Distribution(dist), local, seed,
+                                        vb.Profile.Spec))
+    for f in ("row_ptr", "block_col", "row_size", "col_size", "row_scalar_off",
+              "col_scalar_off", "value_off"):
+        assert np.array_equal(np.asarray(getattr(w, f), dtype=np.int64),
+                              np.asarray(getattr(e, f), dtype=np.int64)), f
+    assert np.array_equal(w.values.view(np.uint32), e.values.view(np.uint32))
+    s = w.row_slice(rows // 3, rows // 2)
+    t = e.row_slice(rows // 3, rows // 2)
+    assert np.array_equal(s.values.view(np.uint32), t.values.view(np.uint32))
+    assert np.array_equal(s.value_off, t.value_off)
+
+
+def test_workload_dense_stream_matches_engine():
+    a = oracle.fill_uniform(1, oracle.STREAM_DENSE, 12345, 200_000)
+    b = vb.fill_uniform(1, vb.STREAM_DENSE, 12345, 200_000)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="reference library not built")
+def test_ref_timer_matches_oracle():
+    """The prepared reference run (the benchmark's timed reference arm) computes the reference's
+    C: bit-identical to the oracle restatement."""
+    w = oracle.WorkloadMatrix(512, 512, 8, 2, False, 5, with_values=True)
+    B = oracle.fill_uniform(5, oracle.STREAM_DENSE, 0, w.scalar_cols() * 32)
+    t = oracle.RefTimer(w, B, 32, threads=3)
+    C = np.empty(w.scalar_rows() * 32, dtype=np.float32)
+    sec = t.run(C)
+    assert sec > 0
+    assert np.array_equal(C.view(np.uint32), oracle.spmm(w, B, 32).view(np.uint32))

@@ -324,4 +324,94 @@ vbsr_status vbsr_multi_plan_gather_C(vbsr_multi_plan* mp, float* C, int dst_devi
   return VBSR_OK;
 }
 
+// ---- Buffers shared between processes (one process per GPU) -------------------------------------
+//
+// A replica of B per rank, filled over NVLink by copy-engine peer copies between processes: each
+// rank allocates its buffer here (cudaMalloc, so the IPC handle covers exactly the buffer and the
+// mapping in another process starts at the buffer's first byte), exports its handle, and maps the
+// other ranks' buffers with vbsr_shared_buffer_open. The copies themselves are plain
+// cudaMemcpyAsync calls, one per chunk.
+
+struct vbsr_shared_buffer {
+  int device = 0;
+  int64_t bytes = 0;
+  void* ptr = nullptr;
+};
+
+vbsr_status vbsr_shared_buffer_create(int device, int64_t bytes, vbsr_shared_buffer** out) {
+  clear_error();
+  if (out == nullptr || bytes <= 0) return set_error(VBSR_INVALID_ARGUMENT, "bad argument");
+  *out = nullptr;
+  auto* b = new (std::nothrow) vbsr_shared_buffer;
+  if (b == nullptr) return set_error(VBSR_OUT_OF_MEMORY, "host allocation failed");
+  Guard g(device);
+  b->device = device;
+  b->bytes = bytes;
+  const cudaError_t e = cudaMalloc(&b->ptr, size_t(bytes));
+  if (e != cudaSuccess) {
+    delete b;
+    return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e));
+  }
+  *out = b;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_shared_buffer_destroy(vbsr_shared_buffer* b) {
+  clear_error();
+  if (b == nullptr) return VBSR_OK;
+  {
+    Guard g(b->device);
+    cudaFree(b->ptr);
+  }
+  delete b;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_shared_buffer_ptr(const vbsr_shared_buffer* b, void** ptr) {
+  clear_error();
+  if (b == nullptr || ptr == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  *ptr = b->ptr;
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_shared_buffer_export(const vbsr_shared_buffer* b, vbsr_ipc_handle* out) {
+  clear_error();
+  if (b == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(out->bytes), "IPC handle size");
+  Guard g(b->device);
+  cudaIpcMemHandle_t h;
+  VBSR_MCUDA(cudaIpcGetMemHandle(&h, b->ptr));
+  std::memcpy(out->bytes, &h, sizeof h);
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_shared_buffer_open(const vbsr_ipc_handle* handle, int device, void** peer_ptr) {
+  clear_error();
+  if (handle == nullptr || peer_ptr == nullptr)
+    return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  Guard g(device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof h);
+  VBSR_MCUDA(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_shared_buffer_close(void* peer_ptr, int device) {
+  clear_error();
+  if (peer_ptr == nullptr) return VBSR_OK;
+  Guard g(device);
+  VBSR_MCUDA(cudaIpcCloseMemHandle(peer_ptr));
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_copy_async(void* dst, const void* src, int64_t bytes, vbsr_stream_t stream) {
+  clear_error();
+  if (bytes < 0 || (bytes > 0 && (dst == nullptr || src == nullptr)))
+    return set_error(VBSR_INVALID_ARGUMENT, "bad copy arguments");
+  if (bytes == 0) return VBSR_OK;
+  VBSR_MCUDA(cudaMemcpyAsync(dst, src, size_t(bytes), cudaMemcpyDefault,
+                             reinterpret_cast<cudaStream_t>(stream)));
+  return VBSR_OK;
+}
+
 }  // extern "C"
