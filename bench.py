@@ -166,6 +166,20 @@ def problem_bytes(host, rhs, r0=0, r1=None):
             + 8 * (S + 1) + 4 * K * rhs + 4 * M * rhs), 2 * hw * rhs
 
 
+def flush_l2(rank_bytes):
+    """Whether the timed steps flush L2 between launches (a rank's inputs smaller than 2 x L2)."""
+    return rank_bytes < 2 * L2_BYTES
+
+
+def workload_config(workload, host, rhs, pbytes, flops, gpus, rank_bytes):
+    """The `config` object of both arms' JSON lines (identical for the same workload and N)."""
+    return {"workload": WORKLOADS[workload][5], "block_rows": host.block_rows, "nnzb": host.nnzb,
+            "rhs": rhs, "compulsory_bytes": pbytes, "useful_flops": flops,
+            "parallelism": f"block-row partition over {gpus} GPU(s), B replicated",
+            "l2": "L2 flushed before every launch" if flush_l2(rank_bytes)
+                  else "inputs larger than L2 (no flush)"}
+
+
 # ---- CPU reference path -----------------------------------------------------------------------
 
 class _PortRunner:
@@ -245,14 +259,16 @@ def run_reference_arm(args):
               f"its flops) per step, median of {info['runs']} timed runs {med:.3f} s on "
               f"{info['cores']} threads (cpu_reference calls only; inputs prepared before "
               f"timing), extrapolated to the whole workload by flops")
+    # a step is one timed sample run; value is the sample's throughput (its share of the
+    # workload's compulsory bytes, by flops, per second)
     line = {
         "metric": "spmm_effective_hbm_GBps", "impl": "reference", "value": value, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": est_full_s * 1e3, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": med * 1e3, "full_workload_ms_extrapolated": est_full_s * 1e3,
+        "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded generator)",
-        "config": {"workload": WORKLOADS[args.workload][5], "block_rows": host.block_rows,
-                   "nnzb": host.nnzb, "rhs": rhs, "compulsory_bytes": pbytes,
-                   "useful_flops": total_flops},
+        "config": workload_config(args.workload, host, rhs, pbytes, total_flops, args.gpus,
+                                  pbytes / max(1, args.gpus)),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": info["cores"],
                          "kind": info["kind"], "sample": sample,
                          "sample_seconds_median": med,
@@ -466,7 +482,7 @@ def run_gpu_arm(args):
     setup_s = time.perf_counter() - t_setup
 
     flush = None
-    if rank_bytes < 2 * L2_BYTES:
+    if flush_l2(rank_bytes):
         flush = torch.empty(2 * L2_BYTES // 4, device="cuda")
 
     with torch.cuda.stream(stream):
@@ -620,13 +636,9 @@ def run_gpu_arm(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded spec generator; A values generated on device, bit-identical "
                     "to the host generator)",
-            "config": {"workload": WORKLOADS[args.workload][5], "block_rows": host.block_rows,
-                       "nnzb": host.nnzb, "rhs": rhs, "compulsory_bytes": pbytes,
-                       "useful_flops": total_flops,
-                       "parallelism": f"block-row partition over {world} GPU(s), B replicated",
-                       "l2": ("inputs larger than L2 (A is %.1f GB)" % (rank_bytes / 1e9))
-                       if flush is None else "L2 flushed before every launch",
-                       "plan": plan.describe()},
+            "config": workload_config(args.workload, host, rhs, pbytes, total_flops, world,
+                                      rank_bytes),
+            "plan": plan.describe(),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": rank_bytes,

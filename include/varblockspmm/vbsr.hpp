@@ -5,7 +5,8 @@
 // Same names, members, signatures, exception types and stream semantics as the reference:
 //   HostMatrix (ref vbsr.hpp:16-29), DeviceMatrix (:32-38), Matrix (:41-64), Distribution (:67),
 //   GeneratorOptions (:70-76), generate (:80), cpu_reference (:87), Kernel (:91),
-//   PlanOptions (:94-97), Plan (:104-119), launch_row_owned (:158-159),
+//   PlanOptions (:94-97), Plan (:104-119), ScalarCsrPlan (:121-137), GroupedGemmPlan (:139-155),
+//   launch_row_owned (:158-159),
 //   launch_row_owned_scalar (:161).
 // Differences a user can see:
 //   * GeneratorOptions has one more member, `profile` (default Profile::Reference reproduces the
@@ -16,8 +17,9 @@
 //     DeviceMatrix is only meaningful to this library's launchers.
 //   * cpu_reference is the CPU oracle: it is defined in the test-infrastructure library
 //     oracle/_build/libvbsr_oracle.so, not in the engine library.
-//   * The library comparators ScalarCsrPlan / GroupedGemmPlan (cuSPARSE / cuBLAS baselines of
-//     the reference) are not part of this engine.
+//   * The library comparators ScalarCsrPlan / GroupedGemmPlan (ref vbsr.hpp:121-155) are this
+//     library's own cuSPARSE / grouped-cuBLAS plans (vbsr_comparators.cpp); ScalarCsrPlan switches
+//     to 64-bit CSR indices when the expanded matrix has 2^31 or more nonzeros.
 #pragma once
 #include <cuda_runtime_api.h>
 
@@ -107,6 +109,37 @@ class Plan {
  private:
   std::shared_ptr<vbsr_plan> p_;
   PlanOptions options_{};
+};
+
+/** cuSPARSE comparator: C = A*B with A expanded to scalar CSR (ref vbsr.hpp:121-137). The
+ * workspace is allocated by the first execute and kept. */
+class ScalarCsrPlan {
+ public:
+  ScalarCsrPlan(const HostMatrix&, int rhs_width);
+  ~ScalarCsrPlan();
+  ScalarCsrPlan(const ScalarCsrPlan&) = delete;
+  void execute(const float* B, float* C, cudaStream_t stream = 0);
+  size_t workspace_bytes() const;
+
+ private:
+  struct Impl;
+  std::unique_ptr<Impl> impl_;
+};
+
+/** Grouped cuBLAS comparator: per slot k (the k-th block of every block row), one grouped SGEMM
+ * over the blocks grouped by shape (ref vbsr.hpp:139-155). */
+class GroupedGemmPlan {
+ public:
+  GroupedGemmPlan(const HostMatrix&, int rhs_width);
+  ~GroupedGemmPlan();
+  GroupedGemmPlan(const GroupedGemmPlan&) = delete;
+  void execute(const float* B, float* C, cudaStream_t stream = 0);
+  int launch_count() const;
+  size_t workspace_bytes() const { return 0; }
+
+ private:
+  struct Impl;
+  std::unique_ptr<Impl> impl_;
 };
 
 /** Multi-GPU plan (no reference counterpart; the reference is single-GPU): the block rows split

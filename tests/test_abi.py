@@ -32,7 +32,9 @@ def test_cxx_dropin_library_links():
     for name in ("vbsr::Plan::execute", "vbsr::Matrix::Matrix", "vbsr::HostMatrix::validate",
                  "vbsr::generate", "vbsr::launch_row_owned", "vbsr::launch_row_owned_scalar",
                  "vbsr::MultiPlan::MultiPlan", "vbsr::MultiPlan::replicate_B",
-                 "vbsr::MultiPlan::execute", "vbsr::MultiPlan::gather_C"):
+                 "vbsr::MultiPlan::execute", "vbsr::MultiPlan::gather_C",
+                 "vbsr::ScalarCsrPlan::execute", "vbsr::GroupedGemmPlan::execute",
+                 "vbsr::GroupedGemmPlan::launch_count"):
         assert name in out, name
 
 

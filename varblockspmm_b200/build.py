@@ -18,7 +18,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libvbsr_b200.so")
 CXXLIB = os.path.join(HERE, "libvbsr_b200_cxx.so")
 
-NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+CUDA = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+NVCC = os.environ.get("NVCC", CUDA + "/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = [*os.environ.get("VBSR_EXTRA_FLAGS", "").split(),
           "-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
@@ -60,14 +61,15 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> str:
     if _stale(LIB, objs):
         log += _run([NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lpthread"])
     # C++ drop-in API (include/varblockspmm/vbsr.hpp) over the C ABI
-    cxx_src = os.path.join(CSRC, "vbsr_api.cpp")
-    if os.path.exists(cxx_src):
-        hdr = [os.path.join(ROOT, "include", "varblockspmm", "vbsr.hpp")] + headers
-        if _stale(CXXLIB, [cxx_src, LIB] + hdr):
-            log += _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared",
-                         "-I" + os.path.join(ROOT, "include"), "-I/usr/local/cuda/include",
-                         cxx_src, "-o", CXXLIB, "-L" + HERE, "-lvbsr_b200",
-                         "-Wl,-rpath,$ORIGIN"])
+    # (with the library comparator plans on cuSPARSE / cuBLAS)
+    cxx_srcs = [os.path.join(CSRC, f) for f in ("vbsr_api.cpp", "vbsr_comparators.cpp")]
+    hdr = [os.path.join(ROOT, "include", "varblockspmm", "vbsr.hpp")] + headers
+    if _stale(CXXLIB, cxx_srcs + [LIB] + hdr):
+        log += _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall",
+                     "-I" + os.path.join(ROOT, "include"), "-I" + CUDA + "/include",
+                     *cxx_srcs, "-o", CXXLIB, "-L" + HERE, "-lvbsr_b200",
+                     "-L" + CUDA + "/lib64", "-lcusparse", "-lcublas", "-lcudart",
+                     "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + CUDA + "/lib64"])
     if verbose and log:
         print(log)
     return log
