@@ -147,7 +147,10 @@ enum { VBSR_KERNEL_AUTO = 0, VBSR_KERNEL_ROW_OWNED = 1, VBSR_KERNEL_SPLIT_ROW = 
 /* Plan flags (no reference counterpart). */
 enum {
   VBSR_PLAN_BOUNDS_CHECK = 1u << 0, /* use the bounds-checked kernel build                  */
-  VBSR_PLAN_NO_SPLIT = 1u << 1,     /* accepted for compatibility; no effect (no row splits) */
+  /* Keep every block row whole. By default a block row whose cost exceeds the fair share of one
+   * SM (1/num_SMs of the matrix's) is cut into row parts of multiples of 8 rows, up to h/8 parts,
+   * each a separate work item writing its own rows of C (no atomics, no workspace). */
+  VBSR_PLAN_NO_SPLIT = 1u << 1,
   /* RHS 64 only, results identical either way: force the raw-B operand stacks (the pre-pass
    * writes raw B rows, the kernel forms their lo parts) or the pre-split ones (hi and lo rows
    * from the pre-pass). By default the plan picks raw-B when the pre-split stacks, K x 512
@@ -163,8 +166,8 @@ enum {
 };
 
 /* Plan::Plan (plan.cpp:5-18): rhs must be 8, 16, 32 or 64. The plan schedules the block rows
- * of `m` once (per-SM work lists balanced by a byte cost model, pipeline stages of 8-column
- * groups), uploads that schedule to the matrix's device and allocates the buffer the B pre-pass
+ * of `m` once (per-SM work lists balanced by a byte cost model, heavy block rows cut into row
+ * parts, pipeline stages of 8-column groups), uploads that schedule to the matrix's device and allocates the buffer the B pre-pass
  * writes (K/8 tiles of B's hi and lo rows); the matrix must outlive the plan. */
 vbsr_status vbsr_plan_create(const vbsr_matrix* m, int rhs, int kernel, vbsr_plan** out);
 vbsr_status vbsr_plan_create_ex(const vbsr_matrix* m, int rhs, int kernel, uint32_t flags,

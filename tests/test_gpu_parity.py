@@ -162,17 +162,74 @@ def test_edge_shapes(cuda, rhs):
         assert np.all(C[:, r0:r1] == 0)
 
 
-def test_heavy_rows(cuda):
-    """A few very heavy block rows (64 blocks of 64 x 64) among many light ones."""
+@pytest.mark.parametrize("rhs", [8, 16, 32, 64])
+def test_heavy_rows(cuda, rhs):
+    """A few very heavy block rows (64 blocks of 64 x 64) among many light ones: the planner cuts
+    the heavy rows into row parts; with and without the cut C meets the bound, and the
+    bounds-checked kernel on the cut schedule gives the same bits."""
     heights = [64] * 4 + [8] * 400
     widths = [64] * 64
     rows_cols = [list(range(64))] * 4 + [[i % 64] for i in range(400)]
     host = _handmade(heights, widths, rows_cols, seed=3)
-    B = np.random.default_rng(2).uniform(-1, 1, host.scalar_cols() * 64).astype(np.float32)
+    B = np.random.default_rng(2).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
     m = vb.Matrix(host)
-    p = vb.Plan(m, vb.PlanOptions(64))
-    got = run_plan(cuda, host, B, 64, matrix=m, plan=p)
-    assert_within_bound(host, B, 64, got)
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    assert "split_rows=4" in p.describe(), p.describe()
+    got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
+    assert_within_bound(host, B, rhs, got)
+    q = vb.Plan(m, vb.PlanOptions(rhs), vb.PLAN_NO_SPLIT)
+    assert "split_rows=0" in q.describe()
+    whole = run_plan(cuda, host, B, rhs, matrix=m, plan=q)
+    assert_within_bound(host, B, rhs, whole)
+    chk = run_plan(cuda, host, B, rhs, flags=vb.PLAN_BOUNDS_CHECK, matrix=m)
+    assert np.array_equal(chk.view(np.uint32), got.view(np.uint32))
+
+
+def _power_law_case(light_rows, heavy_rows, heavy_degree, S, seed):
+    """light_rows block rows of degree 8 and heavy_rows block rows of height 64 and degree
+    heavy_degree (spread through the matrix), random distinct columns, high-variance sizes."""
+    rng = np.random.default_rng(seed)
+    sizes = np.array([8, 16, 56, 64])
+    R = light_rows + heavy_rows
+    heights = rng.choice(sizes, R, p=[.3, .2, .2, .3])
+    heavy = np.linspace(R // (2 * heavy_rows), R - 1, heavy_rows).astype(int)
+    heights[heavy] = 64
+    widths = rng.choice(sizes, S, p=[.3, .2, .2, .3])
+    rows_cols = []
+    for i in range(R):
+        d = heavy_degree if i in set(heavy.tolist()) else 8
+        rows_cols.append(np.sort(rng.choice(S, d, replace=False)).tolist())
+    return _handmade(heights.tolist(), widths.tolist(), rows_cols, seed=seed), heavy
+
+
+def test_power_law_rows_split_and_balance(cuda):
+    """Two block rows of degree 1024 among 8192 rows of degree 8 (RHS 8). Whole, each heavy row
+    alone is several CTAs' fair share and sets the kernel's length; cut into row parts the CTA
+    durations even out. Parity is checked for both schedules."""
+    torch = cuda
+    rhs = 8
+    host, heavy = _power_law_case(8190, 2, 1024, 8192, seed=23)
+    B = np.random.default_rng(4).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
+    m = vb.Matrix(host)
+    spread = {}
+    for name, flags in (("split", 0), ("whole", vb.PLAN_NO_SPLIT)):
+        p = vb.Plan(m, vb.PlanOptions(rhs), flags)
+        got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
+        assert_within_bound(host, B, rhs, got)
+        dB = torch.from_numpy(B).cuda()
+        dC = torch.empty(host.scalar_rows() * rhs, device="cuda")
+        for _ in range(3):
+            p.execute(dB, dC)
+        p.enable_cta_timing(True)
+        p.execute(dB, dC)
+        t = p.cta_timing().astype(np.int64)
+        p.enable_cta_timing(False)
+        dur = (t[:, 1] - t[:, 0]).astype(np.float64)
+        spread[name] = (dur.max() / np.median(dur), dur.max(), p.describe())
+    assert "split_rows=2" in spread["split"][2]
+    # the cut shortens the longest CTA and evens the CTAs out
+    assert spread["split"][1] < 0.75 * spread["whole"][1], spread
+    assert spread["split"][0] <= 1.35, spread
 
 
 def test_unaligned_and_offset_buffers(cuda):
@@ -290,3 +347,20 @@ def test_stalled_pipeline_times_out_and_recovers(cuda):
     p.set_debug(-1, 0)
     got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
     assert_within_bound(host, B, rhs, got)
+
+
+def test_upload_across_slices_matches_device_generation(cuda):
+    """A matrix of ~85 M values (more than one 64 M-value upload slice): built from host values
+    through the pipelined upload + on-device relayout, it gives the same C, bit for bit, as the
+    same matrix generated on the device, and that C meets the bound against the oracle."""
+    torch = cuda
+    rhs = 8
+    host = spec_case(8192, 8, 2, False, 31)
+    assert host.values.size > (1 << 26)
+    B = vb.fill_uniform(31, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    up = run_plan(cuda, host, B, rhs)
+    structure = spec_case(8192, 8, 2, False, 31, with_values=False)
+    gen = vb.Matrix(structure, rows=(0, structure.block_rows), generated_seed=31)
+    got = run_plan(cuda, host, B, rhs, matrix=gen)
+    assert np.array_equal(up.view(np.uint32), got.view(np.uint32))
+    assert_within_bound(host, B, rhs, up)

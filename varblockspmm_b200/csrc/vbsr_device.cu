@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <cstdio>
 #include <cstring>
@@ -11,6 +12,7 @@
 #include <numeric>
 #include <queue>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "vbsr_internal.h"
@@ -159,13 +161,30 @@ __global__ void rowwise_direct_kernel(vbsr_device_matrix a, const float* __restr
 
 bool valid_rhs(int rhs) { return rhs == 8 || rhs == 16 || rhs == 32 || rhs == 64; }
 
+// A private non-blocking stream for the copies and kernels that build a matrix or a plan. Its work
+// is ordered only by itself, and finish() waits for exactly that work, so creation neither waits
+// for nor stalls other streams of the device (a legacy-stream cudaMemcpy from pageable memory or
+// cudaMemset may still be in flight when it returns, so creation does not use those).
+struct SetupStream {
+  cudaStream_t s = nullptr;
+  cudaError_t init() { return cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking); }
+  cudaError_t finish() { return s ? cudaStreamSynchronize(s) : cudaSuccess; }
+  ~SetupStream() {
+    if (s) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  }
+};
+
 template <class T>
-vbsr_status upload(T** dst, const T* src, size_t n, int64_t* bytes) {
+vbsr_status upload(T** dst, const T* src, size_t n, int64_t* bytes, cudaStream_t s) {
   *dst = nullptr;
   if (n == 0) return VBSR_OK;
   VBSR_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), n * sizeof(T)));
   *bytes += int64_t(n * sizeof(T));
-  if (src != nullptr) VBSR_CUDA(cudaMemcpy(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice));
+  if (src != nullptr)
+    VBSR_CUDA(cudaMemcpyAsync(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice, s));
   return VBSR_OK;
 }
 
@@ -183,6 +202,82 @@ void release(MatrixData& d) {
   d.d_row_off = d.d_col_off = d.d_value_off = nullptr;
   d.d_values = nullptr;
   d.d_blk_desc = nullptr;
+}
+
+// Uploads the packed host values of a matrix (blocks [0, nnzb), `src` = its first value, voff the
+// matrix-local value offsets) into d.d_values in the device format. Pipelined in slices of whole
+// blocks (up to kSliceFloats values): host threads copy slice s into pinned staging buffer s % 2,
+// the copy stream moves it to device staging buffer s % 2, and the relayout stream re-lays it out
+// into d_values, so the host copy of slice s+1, the PCIe transfer of slice s and the relayout of
+// slice s-1 overlap. Waits only on its own streams and events (no device-wide synchronisation).
+vbsr_status upload_values(MatrixData& d, const float* src, const std::vector<int64_t>& voff) {
+  constexpr int64_t kSliceFloats = int64_t(1) << 26;  // 256 MiB
+  const int64_t cap = std::min<int64_t>(d.nvalues, kSliceFloats);
+  float* hstage[2] = {nullptr, nullptr};
+  float* dstage[2] = {nullptr, nullptr};
+  cudaStream_t copy_s = nullptr, lay_s = nullptr;
+  cudaEvent_t copied[2] = {nullptr, nullptr}, laid[2] = {nullptr, nullptr};
+  cudaError_t e = cudaSuccess;
+  auto ok = [&](cudaError_t x) {
+    if (e == cudaSuccess) e = x;
+    return e == cudaSuccess;
+  };
+  for (int i = 0; i < 2; ++i) {
+    ok(cudaHostAlloc(reinterpret_cast<void**>(&hstage[i]), size_t(cap) * sizeof(float),
+                     cudaHostAllocDefault));
+    ok(cudaMalloc(&dstage[i], size_t(cap) * sizeof(float)));
+    ok(cudaEventCreateWithFlags(&copied[i], cudaEventDisableTiming));
+    ok(cudaEventCreateWithFlags(&laid[i], cudaEventDisableTiming));
+  }
+  ok(cudaStreamCreateWithFlags(&copy_s, cudaStreamNonBlocking));
+  ok(cudaStreamCreateWithFlags(&lay_s, cudaStreamNonBlocking));
+  const unsigned hc = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  int64_t b = 0;
+  for (int s = 0; e == cudaSuccess && b < d.nnzb; ++s) {
+    const int k = s & 1;
+    int64_t be = b;
+    while (be < d.nnzb && voff[be + 1] - voff[b] <= cap) ++be;
+    const int64_t n = voff[be] - voff[b];
+    // staging pair k was last used by slice s-2: its transfer must have read the pinned buffer
+    if (s >= 2 && !ok(cudaEventSynchronize(copied[k]))) break;
+    {
+      const float* from = src + voff[b];
+      float* to = hstage[k];
+      std::vector<std::thread> pool;
+      for (unsigned t = 1; t < hc; ++t)
+        pool.emplace_back([=] {
+          const int64_t a0 = n * t / hc, a1 = n * (t + 1) / hc;
+          std::memcpy(to + a0, from + a0, size_t(a1 - a0) * sizeof(float));
+        });
+      std::memcpy(to, from, size_t(n / hc) * sizeof(float));
+      for (auto& th : pool) th.join();
+    }
+    // ... and its relayout must have read the device staging buffer
+    if (s >= 2 && !ok(cudaStreamWaitEvent(copy_s, laid[k], 0))) break;
+    if (!ok(cudaMemcpyAsync(dstage[k], hstage[k], size_t(n) * sizeof(float),
+                            cudaMemcpyHostToDevice, copy_s)))
+      break;
+    if (!ok(cudaEventRecord(copied[k], copy_s))) break;
+    if (!ok(cudaStreamWaitEvent(lay_s, copied[k], 0))) break;
+    relayout_blocks<<<unsigned(be - b), 256, 0, lay_s>>>(d.d_row_ptr, d.block_rows, d.d_row_size,
+                                                        d.d_value_off, d.d_blk_desc, int(b),
+                                                        dstage[k], voff[b], d.d_values);
+    if (!ok(cudaGetLastError())) break;
+    if (!ok(cudaEventRecord(laid[k], lay_s))) break;
+    b = be;
+  }
+  if (copy_s) ok(cudaStreamSynchronize(copy_s));
+  if (lay_s) ok(cudaStreamSynchronize(lay_s));
+  for (int i = 0; i < 2; ++i) {
+    cudaFreeHost(hstage[i]);
+    cudaFree(dstage[i]);
+    if (copied[i]) cudaEventDestroy(copied[i]);
+    if (laid[i]) cudaEventDestroy(laid[i]);
+  }
+  if (copy_s) cudaStreamDestroy(copy_s);
+  if (lay_s) cudaStreamDestroy(lay_s);
+  if (e != cudaSuccess) return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e));
+  return VBSR_OK;
 }
 
 // Builds the device format of block rows [r0, r1). mode 0: values from host; 1: generated.
@@ -245,6 +340,11 @@ vbsr_status build_matrix(const vbsr_host_matrix_view* v, int r0, int r1, int mod
     }
 
     int64_t bytes = 0;
+    SetupStream ss;
+    if (ss.init() != cudaSuccess) {
+      delete m;
+      return set_error(VBSR_CUDA_ERROR, "stream creation failed");
+    }
 #define VBSR_TRY(x)          \
   do {                       \
     st = (x);                \
@@ -254,55 +354,31 @@ vbsr_status build_matrix(const vbsr_host_matrix_view* v, int r0, int r1, int mod
       return st;             \
     }                        \
   } while (0)
-    VBSR_TRY(upload(&d.d_row_ptr, d.h_row_ptr.data(), d.h_row_ptr.size(), &bytes));
-    VBSR_TRY(upload(&d.d_block_col, v->block_col + b0, size_t(d.nnzb), &bytes));
-    VBSR_TRY(upload(&d.d_row_size, d.h_row_size.data(), d.h_row_size.size(), &bytes));
-    VBSR_TRY(upload(&d.d_col_size, v->col_size, size_t(S), &bytes));
-    VBSR_TRY(upload(&d.d_row_off, d.h_row_off.data(), d.h_row_off.size(), &bytes));
-    VBSR_TRY(upload(&d.d_col_off, v->col_scalar_off, size_t(S) + 1, &bytes));
-    VBSR_TRY(upload(&d.d_value_off, voff.data(), voff.size(), &bytes));
-    VBSR_TRY(upload(&d.d_blk_desc, desc.data(), desc.size(), &bytes));
-    VBSR_TRY(upload<float>(&d.d_values, nullptr, size_t(d.nvalues), &bytes));
+    VBSR_TRY(upload(&d.d_row_ptr, d.h_row_ptr.data(), d.h_row_ptr.size(), &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_block_col, v->block_col + b0, size_t(d.nnzb), &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_row_size, d.h_row_size.data(), d.h_row_size.size(), &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_col_size, v->col_size, size_t(S), &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_row_off, d.h_row_off.data(), d.h_row_off.size(), &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_col_off, v->col_scalar_off, size_t(S) + 1, &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_value_off, voff.data(), voff.size(), &bytes, ss.s));
+    VBSR_TRY(upload(&d.d_blk_desc, desc.data(), desc.size(), &bytes, ss.s));
+    VBSR_TRY(upload<float>(&d.d_values, nullptr, size_t(d.nvalues), &bytes, ss.s));
 
+    VBSR_TRY(ss.finish() == cudaSuccess ? VBSR_OK
+                                        : set_error(VBSR_CUDA_ERROR, "metadata upload failed"));
     if (d.nnzb > 0 && mode == 0) {
-      // Upload in slices of whole blocks through a staging buffer and re-lay each slice.
-      const int64_t slice_cap = std::min<int64_t>(d.nvalues, int64_t(1) << 28);  // 1 GiB
-      float* staging = nullptr;
-      const cudaError_t e = cudaMalloc(&staging, size_t(slice_cap) * sizeof(float));
-      if (e != cudaSuccess) {
+      st = upload_values(d, v->values + v0, voff);
+      if (st != VBSR_OK) {
         release(d);
         delete m;
-        return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e));
+        return st;
       }
-      int64_t b = 0;
-      while (b < d.nnzb) {
-        int64_t be = b;
-        while (be < d.nnzb && voff[be + 1] - voff[b] <= slice_cap) ++be;
-        const int64_t n = voff[be] - voff[b];
-        cudaError_t e2 = cudaMemcpy(staging, v->values + v0 + voff[b], size_t(n) * sizeof(float),
-                                    cudaMemcpyHostToDevice);
-        if (e2 == cudaSuccess) {
-          relayout_blocks<<<unsigned(be - b), 256>>>(d.d_row_ptr, R, d.d_row_size, d.d_value_off,
-                                                    d.d_blk_desc, int(b), staging, voff[b],
-                                                    d.d_values);
-          e2 = cudaGetLastError();
-        }
-        if (e2 == cudaSuccess) e2 = cudaDeviceSynchronize();
-        if (e2 != cudaSuccess) {
-          cudaFree(staging);
-          release(d);
-          delete m;
-          return set_error(VBSR_CUDA_ERROR, cudaGetErrorString(e2));
-        }
-        b = be;
-      }
-      cudaFree(staging);
     } else if (d.nnzb > 0) {
-      generate_blocks<<<4096, 256>>>(d.d_row_ptr, R, d.d_row_size, d.d_value_off, d.d_blk_desc,
-                                     int(d.nnzb), rng_key(seed, VBSR_STREAM_VALUES), v0,
-                                     d.d_values);
+      generate_blocks<<<4096, 256, 0, ss.s>>>(d.d_row_ptr, R, d.d_row_size, d.d_value_off,
+                                              d.d_blk_desc, int(d.nnzb),
+                                              rng_key(seed, VBSR_STREAM_VALUES), v0, d.d_values);
       cudaError_t e2 = cudaGetLastError();
-      if (e2 == cudaSuccess) e2 = cudaDeviceSynchronize();
+      if (e2 == cudaSuccess) e2 = ss.finish();
       if (e2 != cudaSuccess) {
         release(d);
         delete m;
@@ -346,6 +422,8 @@ struct vbsr_plan {
   std::string summary;
   std::vector<int> task_warps;      // team size of every task
   std::vector<double> task_cost;    // planner's cost model: the task's most loaded team
+  int split_rows = 0;               // block rows cut into row parts
+  int work_items = 0;               // items (block rows and row parts)
   // Every execute writes the operand stacks into d_bstack and the SpMM reads them, so two executes
   // of one plan must not overlap on the GPU. Each execute waits (cudaStreamWaitEvent) for the
   // completion event of the previous one, on whatever stream that ran, and records its own.
@@ -380,9 +458,9 @@ cudaError_t set_kernel_attrs() {
   return cudaSuccess;
 }
 
-// Schedule for spmm_tc_kernel: one item per block row, one CTA per SM; items assigned to CTAs by
-// longest-processing-time-first on the cost model; each CTA's stream cuts the item's 8-column
-// groups into stages of stage_groups(h, rhs) groups.
+// Schedule for spmm_tc_kernel: one item per block row (or per row part of a heavy block row), one
+// CTA per SM; items assigned to CTAs by longest-processing-time-first on the cost model; each
+// CTA's stream cuts the item's 8-column groups into stages of stage_groups(h, rhs) groups.
 vbsr_status build_schedule(vbsr_plan* p) {
   const MatrixData& d = p->m->d;
   const int rhs = p->rhs;
@@ -401,32 +479,65 @@ vbsr_status build_schedule(vbsr_plan* p) {
               : (p->flags & VBSR_PLAN_STACKS_PRESPLIT) ? false
                                                        : big);
   const int R = d.block_rows;
-  std::vector<int> row_stages(R);
-  std::vector<double> cost(R);
+  // Work units: one per block row, or, for a block row whose cost exceeds a CTA's fair share, one
+  // per row part. A row part is rows [r0, r0 + hp) of the block row (multiples of 8) over all its
+  // blocks: parts write disjoint rows of C, so no atomics and no workspace are needed. Each part
+  // streams only its rows of A but the block row's whole B slice, so parts are made no smaller
+  // than needed: P = ceil(cost / fair share), at most H / 8.
+  struct Unit {
+    int row, r0, hp;
+    double cost;
+  };
+  auto groups_of = [&](int i) {
+    int64_t g = 0;
+    for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b) g += int64_t((d.h_blk_desc[b] & 7u) + 1u);
+    return g;
+  };
+  auto unit_cost = [&](int i, int hp) {
+    const int G = stage_groups(hp, rhs, p->raw_b);  // 8-column groups per stage
+    return item_cost(hp, rhs, d.h_sum_w[i], int((groups_of(i) + G - 1) / G));
+  };
+  std::vector<double> row_cost(R);
+  double total = 0.0;
+  for (int i = 0; i < R; ++i) total += (row_cost[i] = unit_cost(i, d.h_row_size[i]));
+  const double fair = total / double(num_sm);
+  const bool may_split = !(p->flags & VBSR_PLAN_NO_SPLIT);
+  std::vector<Unit> units;
+  units.reserve(size_t(R));
+  int split_rows = 0;
   for (int i = 0; i < R; ++i) {
-    const int G = stage_groups(d.h_row_size[i], rhs, p->raw_b);  // 8-column groups per stage
-    int64_t groups = 0;
-    for (int b = d.h_row_ptr[i]; b < d.h_row_ptr[i + 1]; ++b)
-      groups += int64_t((d.h_blk_desc[b] & 7u) + 1u);
-    const int st = int((groups + G - 1) / G);
-    row_stages[i] = st;
-    cost[i] = item_cost(d.h_row_size[i], rhs, d.h_sum_w[i], st);
+    const int H = d.h_row_size[i];
+    int parts = 1;
+    if (may_split && R > 1 && row_cost[i] > fair)
+      parts = std::min(H / 8, int(std::ceil(row_cost[i] / fair)));
+    if (parts <= 1) {
+      units.push_back({i, 0, H, row_cost[i]});
+      continue;
+    }
+    ++split_rows;
+    const int blocks8 = H / 8;
+    for (int q = 0, r8 = 0; q < parts; ++q) {
+      const int n8 = blocks8 / parts + (q < blocks8 % parts ? 1 : 0);  // 8-row blocks of part q
+      units.push_back({i, 8 * r8, 8 * n8, unit_cost(i, 8 * n8)});
+      r8 += n8;
+    }
   }
-  const int ctas = std::max(1, std::min(num_sm, R));
-  const int teams = ctas;
-  std::vector<int> order(R);
+  const int nunits = int(units.size());
+  const int teams = std::max(1, std::min(num_sm, nunits));
+  std::vector<int> order(nunits);
   std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return units[a].cost > units[b].cost; });
   using Load = std::pair<double, int>;
   std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
   for (int t = 0; t < teams; ++t) heap.push({0.0, t});
   std::vector<std::vector<int>> lists(teams);
   std::vector<double> load(teams, 0.0);
-  for (int i : order) {
+  for (int u : order) {
     Load l = heap.top();
     heap.pop();
-    lists[l.second].push_back(i);
-    l.first += cost[i];
+    lists[l.second].push_back(u);
+    l.first += units[u].cost;
     load[l.second] = l.first;
     heap.push(l);
   }
@@ -434,7 +545,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   std::vector<StageDesc> stream;
   stream.reserve(size_t(d.nnzb) * 2 + 16);
   std::vector<ItemDesc> items;
-  items.reserve(size_t(R));
+  items.reserve(size_t(nunits));
   std::vector<Task> h_tasks;
   const int slot = slot_floats(rhs);
   // A multiple of every role's warp count: every slot then has one feeder, one split warp and one
@@ -444,23 +555,25 @@ vbsr_status build_schedule(vbsr_plan* p) {
       kTcRingMultiple;
   if (stages < kTcRingMultiple) return set_error(VBSR_INVALID_ARGUMENT, "stage does not fit shared memory");
   const uint64_t nwc = uint64_t(stage::nw_code(rhs));
-  for (int t = 0; t < ctas; ++t) {
+  for (int t = 0; t < teams; ++t) {
     Task task{};
     task.item_off = int(items.size());
     task.stage_off = int(stream.size());
     std::vector<int>& l = lists[t];
-    std::sort(l.begin(), l.end());
-    for (int i : l) {
-      const int h = d.h_row_size[i];
-      const uint64_t base0 = (uint64_t(h / 8 - 1) << 32) | (nwc << 39);
+    std::sort(l.begin(), l.end());  // units are in row order, parts of a row by r0
+    for (int u : l) {
+      const int i = units[u].row, r0 = units[u].r0, h = units[u].hp, H = d.h_row_size[i];
+      const uint64_t base0 =
+          (uint64_t(h / 8 - 1) << 32) | (nwc << 39) | (uint64_t(H / 8 - 1) << 41);
       ItemDesc item{};
-      item.c_row = uint32_t(d.h_row_off[i]);
+      item.c_row = uint32_t(d.h_row_off[i] + r0);
       item.shape = uint32_t(h / 8 - 1) | (uint32_t(nwc) << 6);
       item.k0 = uint32_t(stream.size() - size_t(task.stage_off));
       const uint64_t w1 = uint64_t(items.size() - size_t(task.item_off));
       // The item's 8-column groups, block after block, in runs of G per stage. In the device
-      // format group g of a block starts 8*h*g floats after the block's values and a block row's
-      // blocks are consecutive, so a stage's A values are one contiguous range.
+      // format group g of a block starts 8*H*g floats after the block's values and a block row's
+      // blocks are consecutive, so a stage's A values are one contiguous range (a row part's rows
+      // start 8*r0 floats into each group).
       int64_t val = d.h_val_off_row[i];
       const int G = stage_groups(h, rhs, p->raw_b);
       int used = 0;  // columns in the current stage
@@ -477,14 +590,14 @@ vbsr_status build_schedule(vbsr_plan* p) {
           }
           if (used == 0) {
             cur = StageDesc{};
-            cur.w[0] = base0 | uint64_t((val + int64_t(8) * h * g) / 64);
+            cur.w[0] = base0 | uint64_t((val + int64_t(8) * H * g + int64_t(8) * r0) / 64);
             cur.w[1] = w1;
           }
           const int gg = used / 8;  // < kMaxStageGroups
           cur.w[2 + gg / 2] |= uint64_t((col + 8 * g) / 8) << (32 * (gg & 1));
           used += 8;
         }
-        val += int64_t(h) * w;
+        val += int64_t(H) * w;
       }
       if (used > 0) {
         cur.w[0] |= uint64_t(used / 8 - 1) << 28;
@@ -508,6 +621,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
     p->task_warps.push_back(kTcWarps);
     p->task_cost.push_back(load[t]);
   }
+  p->split_rows = split_rows;
+  p->work_items = nunits;
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
   p->smem_bytes = stages * slot * 4 + kSmemTailPad + 1024;  // + alignment of the ring
@@ -516,14 +631,17 @@ vbsr_status build_schedule(vbsr_plan* p) {
 
   char buf[512];
   std::snprintf(buf, sizeof buf,
-                "rhs=%d items=%d pipeline_stages=%zu tasks=%d teams=%d ring=%d smem=%d sms=%d "
-                "kernel=tcgen05-3xtf32-%s",
-                rhs, R, stream.size(), p->num_tasks, teams, stages, p->smem_bytes, num_sm,
+                "rhs=%d items=%d split_rows=%d pipeline_stages=%zu tasks=%d teams=%d ring=%d "
+                "smem=%d sms=%d kernel=tcgen05-3xtf32-%s",
+                rhs, nunits, split_rows, stream.size(), p->num_tasks, teams, stages,
+                p->smem_bytes, num_sm,
                 row_stacked(rhs) ? "row-stacked" : (p->raw_b ? "column-stacked-raw-b"
                                                               : "column-stacked-pre-split"));
   p->summary = buf;
 
   DeviceGuard guard(d.device);
+  SetupStream ss;
+  VBSR_CUDA(ss.init());
   VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
   // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
@@ -532,19 +650,21 @@ vbsr_status build_schedule(vbsr_plan* p) {
     return set_error(VBSR_INVALID_ARGUMENT, "B too large for the pre-pass index range");
   VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
   // rows of RHS columns >= rhs (rhs < 32) are never written by the pre-pass: zero them once
-  VBSR_CUDA(cudaMemset(p->d_bstack, 0, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
+  VBSR_CUDA(cudaMemsetAsync(p->d_bstack, 0,
+                            size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float), ss.s));
   if (!items.empty())
-    VBSR_CUDA(cudaMemcpy(p->d_items, items.data(), items.size() * sizeof(ItemDesc),
-                         cudaMemcpyHostToDevice));
+    VBSR_CUDA(cudaMemcpyAsync(p->d_items, items.data(), items.size() * sizeof(ItemDesc),
+                              cudaMemcpyHostToDevice, ss.s));
   VBSR_CUDA(cudaMalloc(&p->d_tasks, std::max<size_t>(1, h_tasks.size()) * sizeof(Task)));
   VBSR_CUDA(cudaMalloc(&p->d_status, kStatusWords * sizeof(int)));
   if (!stream.empty())
-    VBSR_CUDA(cudaMemcpy(p->d_stream, stream.data(), stream.size() * sizeof(StageDesc),
-                         cudaMemcpyHostToDevice));
+    VBSR_CUDA(cudaMemcpyAsync(p->d_stream, stream.data(), stream.size() * sizeof(StageDesc),
+                              cudaMemcpyHostToDevice, ss.s));
   if (!h_tasks.empty())
-    VBSR_CUDA(cudaMemcpy(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
-                         cudaMemcpyHostToDevice));
-  VBSR_CUDA(cudaMemset(p->d_status, 0, kStatusWords * sizeof(int)));
+    VBSR_CUDA(cudaMemcpyAsync(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
+                              cudaMemcpyHostToDevice, ss.s));
+  VBSR_CUDA(cudaMemsetAsync(p->d_status, 0, kStatusWords * sizeof(int), ss.s));
+  VBSR_CUDA(ss.finish());
   VBSR_CUDA(cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming));
   VBSR_CUDA(set_kernel_attrs());
   return VBSR_OK;
@@ -936,8 +1056,13 @@ vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int ou
   DeviceGuard guard(p->device);
   if (enable && p->d_timing == nullptr)
     VBSR_CUDA(cudaMalloc(&p->d_timing, std::max(1, 18 * p->num_tasks) * sizeof(uint64_t)));
-  if (enable && out == nullptr)  // switching on: start from zeroed counters
-    VBSR_CUDA(cudaMemset(p->d_timing, 0, std::max(1, 18 * p->num_tasks) * sizeof(uint64_t)));
+  if (enable && out == nullptr) {  // switching on: start from zeroed counters
+    SetupStream ss;
+    VBSR_CUDA(ss.init());
+    VBSR_CUDA(cudaMemsetAsync(p->d_timing, 0, std::max(1, 18 * p->num_tasks) * sizeof(uint64_t),
+                              ss.s));
+    VBSR_CUDA(ss.finish());
+  }
   if (out != nullptr && p->d_timing != nullptr) {
     const int n = std::min(out_len, 18 * p->num_tasks);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

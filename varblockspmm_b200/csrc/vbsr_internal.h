@@ -15,8 +15,8 @@ vbsr_status set_error(vbsr_status s, const std::string& msg);
 void clear_error();
 
 // ---- work schedule ---------------------------------------------------------------------------
-// The plan compiles the matrix into, per CTA, a list of work items (one block row each: an h x nw
-// tile of C) and the list of their pipeline stages. A stage covers up to twelve consecutive
+// The plan compiles the matrix into, per CTA, a list of work items (one block row each, or one row
+// part of a heavy block row: an h x nw tile of C) and the list of their pipeline stages. A stage covers up to twelve consecutive
 // 8-column groups of one item (as many as fit one shared-memory slot at the item's h), possibly
 // from several blocks. Because a block row's blocks are contiguous in
 // the value array and each block stores its groups in order (h x 8 floats each), the A values of a
@@ -26,6 +26,8 @@ void clear_error();
 //   w0: bits  0..27 A start / 64 (offsets of blocks and groups are multiples of 64 floats)
 //       bits 28..31 groups - 1 (a stage holds 1..12 groups of 8 block columns)
 //       bits 32..34 h/8 - 1         bits 36..38 n0/8   bits 39..40 log2(nw/8)
+//       bits 41..43 H/8 - 1: the height of the block row; H > h for a row part of a split block
+//                   row (rows [r0, r0 + h) of H, A start then points at row r0 of the first group)
 //   w1: the item's index in the CTA's item list
 //   w2..w7: the groups' scalar columns / 8, two per word (group 2i in bits 0..27 of w[2+i],
 //           group 2i+1 in bits 32..59)

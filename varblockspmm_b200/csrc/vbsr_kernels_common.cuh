@@ -40,6 +40,13 @@ struct Stage {
   __device__ __forceinline__ int h() const { return int(((w0 >> 32) & 7u) + 1u) * 8; }
   __device__ __forceinline__ int n0() const { return int((w0 >> 36) & 7u) * 8; }
   __device__ __forceinline__ int nw() const { return 8 << int((w0 >> 39) & 3u); }
+  // height of the stage's block row; h() < H() when the item is a row part of it (groups are then
+  // H * 8 floats apart in the device format, and the part's h rows start a_start() into each)
+  __device__ __forceinline__ int H() const { return int(((w0 >> 41) & 7u) + 1u) * 8; }
+  // bytes from the stage's first A value to the end of its last group's rows
+  __device__ __forceinline__ long long a_span_bytes() const {
+    return 32ll * (H() * (groups() - 1) + h());
+  }
   __device__ __forceinline__ int group_col(int i) const {  // scalar column of group i
     const int k = i >> 1;  // selected without indexing, so the words stay in registers
     const u64 w = k == 0 ? g[0]

@@ -245,7 +245,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
       // the A values of this feeder's stage kPrefetchAhead turns later, into L2 (one TMA op)
       Stage pf;
       pf.w0 = win.word0_ahead(kPrefetchAhead);
-      if (lane == 0) bulk_prefetch_l2(p.values + pf.a_start(), uint32_t(32 * pf.h() * pf.groups()));
+      if (lane == 0) bulk_prefetch_l2(p.values + pf.a_start(), uint32_t(pf.a_span_bytes()));
     }
     win.advance(lane);
     const uint32_t full_bar = cb.full0 + 8u * s;
@@ -253,7 +253,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     // slot's critical path. A: the stage's groups are contiguous in the device format: one copy.
     // S: consecutive groups of one block have consecutive pre-pass tiles, so each run of them is
     // one copy, issued by the lane of the run's first group.
-    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.groups();
+    const int h = st.h(), nw = st.nw(), n0 = st.n0(), groups = st.groups(), H = st.H();
     const long long a0 = st.a_start();
     const uint32_t sp = slots + 4u * uint32_t(s * SF);
     const int T = stack_tile_bytes(p.rhs, RAW);
@@ -275,7 +275,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     VBSR_TRACE_ST(kk, 0);
     bool ok = true;
     if (CHECK) {
-      ok = a0 + 8ll * h * groups <= p.nvalues && n0 == 0 && nw == p.rhs &&
+      ok = a0 + st.a_span_bytes() / 4 <= p.nvalues && n0 == 0 && nw == p.rhs && h <= H &&
            groups <= stage_groups(h, p.rhs, RAW);
       for (int g = 0; g < groups; ++g) ok = ok && st.group_col(g) + 8 <= p.K;
     }
@@ -290,9 +290,14 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
       VBSR_TRACE_ST(kk, 7);
       if (lane == 0) {
         mbar_arrive_expect_tx(full_bar, tx);
-        bulk_g2s(sp, a_src, a_bytes, full_bar, pol_a);
+        if (H == h) bulk_g2s(sp, a_src, a_bytes, full_bar, pol_a);  // one contiguous range
       }
       __syncwarp();
+      // a row part: its rows of each group are a separate range (groups H * 8 floats apart); the
+      // slot holds them as consecutive h-row groups, the layout of an unsplit item of height h
+      if (H != h && lane < groups)
+        bulk_g2s(sp + uint32_t(32 * h * lane), a_src + 8ll * H * lane, uint32_t(32 * h), full_bar,
+                 pol_a);
       if (start) bulk_g2s(s_dst, s_src, s_bytes, full_bar, pol_b);
       filled |= 1u << s;
       VBSR_TRACE_ST(kk, 1);
