@@ -250,7 +250,7 @@ def run_reference_arm(args):
     host, rhs = make_workload(args.workload)
     pbytes, total_flops = problem_bytes(host, rhs)
     B = oracle.fill_uniform(SEED, oracle.STREAM_DENSE, 0, host.scalar_cols() * rhs)
-    per_step = max(0.5, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
+    per_step = max(0.5, min(3.0, 75.0 / max(1, args.steps + args.warmup)))
     med, flops, info = cpu_reference_timing(host, rhs, B, args.warmup, args.steps,
                                             min_run_s=per_step)
     est_full_s = med * total_flops / flops

@@ -146,8 +146,9 @@ def _replica_rank(rank, world, port, result_path):
     from varblockspmm_b200.replica import copy_async
     copy_async(got.data_ptr(), rep.ptr(0), 4 * K * rhs)
     torch.cuda.synchronize()
-    out["replicate_equal"] = bool(np.array_equal(got.cpu().numpy().view(np.uint32),
-                                                 B.view(np.uint32)))
+    g = got.cpu().numpy()
+    out["replicate_equal"] = bool(np.array_equal(g.view(np.uint32), B.view(np.uint32)))
+    out["replicate_mismatch"] = int(np.count_nonzero(g.view(np.uint32) != B.view(np.uint32)))
     # per-step form: own chunk from pinned host memory, the rest from the peers
     hB = torch.from_numpy(B).pin_memory()
     up = rep.upload_own_chunk(hB.data_ptr(), 1)
@@ -195,7 +196,7 @@ def test_peer_replica_two_processes(cuda, tmp_path):
     base = str(tmp_path / "rank")
     tmp.start_processes(_replica_rank, args=(2, port, base), nprocs=2, join=True,
                         start_method="spawn")
-    for r in range(2):
-        out = json.load(open(f"{base}.{r}"))
-        assert out["replicate_equal"] and out["upload_pull_equal"], out
+    outs = [json.load(open(f"{base}.{r}")) for r in range(2)]
+    for out in outs:
+        assert out["replicate_equal"] and out["upload_pull_equal"], outs
         assert out["violations"] == 0

@@ -117,10 +117,13 @@ class PeerReplica:
         return sum(self._pull(j, b, stream) for j in range(self.world) if j != self.rank)
 
     def replicate_from(self, root: int, b: int = 0, stream=None) -> int:
-        """Collective: the root's buffer b holds all of B; afterwards every rank's does. Returns the
-        bytes this rank received."""
+        """Collective: the root's buffer b holds all of B once the root's device work enqueued
+        before the call has run; afterwards every rank's does. Returns the bytes this rank
+        received."""
         import torch
         got = 0
+        torch.cuda.synchronize(self.device)
+        self.barrier()  # the root's buffer is complete before anyone reads it
         if self.rank != root:
             got += self._pull(self.rank, b, stream, src_rank=root)
         torch.cuda.synchronize(self.device)
