@@ -203,12 +203,12 @@ def _power_law_case(light_rows, heavy_rows, heavy_degree, S, seed):
 
 
 def test_power_law_rows_split_and_balance(cuda):
-    """Two block rows of degree 1024 among 8192 rows of degree 8 (RHS 8). Whole, each heavy row
-    alone is several CTAs' fair share and sets the kernel's length; cut into row parts the CTA
+    """Two block rows of degree 2048 among 16382 rows of degree 8 (RHS 8). Whole, each heavy row
+    is about three CTAs' fair share and sets the kernel's length; cut into row parts the CTA
     durations even out. Parity is checked for both schedules."""
     torch = cuda
     rhs = 8
-    host, heavy = _power_law_case(8190, 2, 1024, 8192, seed=23)
+    host, heavy = _power_law_case(16382, 2, 2048, 16384, seed=23)
     B = np.random.default_rng(4).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
     m = vb.Matrix(host)
     spread = {}
@@ -229,7 +229,7 @@ def test_power_law_rows_split_and_balance(cuda):
     assert "split_rows=2" in spread["split"][2]
     # the cut shortens the longest CTA and evens the CTAs out
     assert spread["split"][1] < 0.75 * spread["whole"][1], spread
-    assert spread["split"][0] <= 1.35, spread
+    assert spread["split"][0] <= 1.3, spread
 
 
 def test_unaligned_and_offset_buffers(cuda):
