@@ -157,6 +157,10 @@ enum {
    * bytes, exceed 64 MB and would not stay in L2. */
   VBSR_PLAN_STACKS_RAW = 1u << 3,
   VBSR_PLAN_STACKS_PRESPLIT = 1u << 4,
+  /* RHS 64 only, results identical: the SpMM reads the raw-B stack rows straight from B (16-byte
+   * asynchronous copies of each column's run of values) instead of from a pre-pass buffer, so an
+   * execute is one launch and the plan allocates no stack buffer. */
+  VBSR_PLAN_B_DIRECT = 1u << 5,
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
   VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9,   /* consumers wait for the data but compute nothing     */

@@ -103,7 +103,8 @@ def test_bounds_checked_build_and_no_split(cuda, rhs):
     assert_within_bound(host, B, rhs, c)
 
 
-STACKS = [("raw", vb.PLAN_STACKS_RAW), ("presplit", vb.PLAN_STACKS_PRESPLIT)]
+STACKS = [("raw", vb.PLAN_STACKS_RAW), ("presplit", vb.PLAN_STACKS_PRESPLIT),
+          ("direct", vb.PLAN_B_DIRECT), ("direct_checked", vb.PLAN_B_DIRECT | vb.PLAN_BOUNDS_CHECK)]
 
 
 @pytest.mark.parametrize("stacks", STACKS, ids=lambda s: s[0])
@@ -112,8 +113,8 @@ STACKS = [("raw", vb.PLAN_STACKS_RAW), ("presplit", vb.PLAN_STACKS_PRESPLIT)]
                          ids=lambda c: "r%dd%d" % (c[0], c[1]))
 def test_rhs64_stack_layouts(cuda, stacks, case):
     """RHS 64 with each operand-stack layout forced: raw-B stacks (lo rows formed in the kernel,
-    three MMAs per group) and pre-split stacks (two MMAs per group). Both meet the bound; the
-    plan names the layout it uses."""
+    three MMAs per group) from the pre-pass or read straight from B, and pre-split stacks (two
+    MMAs per group). All meet the bound; the plan names the layout it uses."""
     rows, deg, dist, local, seed = case
     rhs = 64
     host = spec_case(rows, deg, dist, local, seed)
@@ -121,6 +122,8 @@ def test_rhs64_stack_layouts(cuda, stacks, case):
     m = vb.Matrix(host)
     p = vb.Plan(m, vb.PlanOptions(rhs), stacks[1])
     assert ("raw-b" in p.describe()) == (stacks[0] == "raw")
+    assert ("direct-b" in p.describe()) == stacks[0].startswith("direct")
+    assert p.launch_count() == (1 if stacks[0].startswith("direct") else 2)
     got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
     assert_within_bound(host, B, rhs, got)
     # the bounds-checked build agrees bit for bit

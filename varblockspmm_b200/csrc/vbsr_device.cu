@@ -412,6 +412,7 @@ struct vbsr_plan {
   ItemDesc* d_items = nullptr;
   float* d_bstack = nullptr;     // B's operand stacks, rewritten by every execute
   bool raw_b = false;            // column-stacked form: raw-B stacks (see stack_rows)
+  bool direct_b = false;         // ... read from B by the SpMM itself: no pre-pass, no d_bstack
   int64_t bstack_floats = 0;
   Task* d_tasks = nullptr;
   int* d_status = nullptr;
@@ -445,12 +446,14 @@ double item_cost(int h, int nw, int64_t sum_w, int nstages) {
 cudaError_t set_kernel_attrs() {
   const int bytes = kSmemBudget + 1024;
   const void* kernels[] = {
-      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, false>),
-      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, false>),
-      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, true>),
-      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, true>),
-      reinterpret_cast<const void*>(spmm_tc_kernel<false, true, false>),
-      reinterpret_cast<const void*>(spmm_tc_kernel<true, true, false>)};
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, false, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, false, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, true, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, true, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, false, true, true>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, false, true, true>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<false, true, false, false>),
+      reinterpret_cast<const void*>(spmm_tc_kernel<true, true, false, false>)};
   for (const void* k : kernels) {
     const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
@@ -475,9 +478,11 @@ vbsr_status build_schedule(vbsr_plan* p) {
   constexpr int64_t kRawStackBytes = 64ll << 20;
   const bool big = (d.K / 8) * int64_t(stack_tile_bytes(rhs, false)) > kRawStackBytes;
   p->raw_b = !row_stacked(rhs) &&
-             ((p->flags & VBSR_PLAN_STACKS_RAW)        ? true
-              : (p->flags & VBSR_PLAN_STACKS_PRESPLIT) ? false
-                                                       : big);
+             ((p->flags & (VBSR_PLAN_STACKS_RAW | VBSR_PLAN_B_DIRECT)) ? true
+              : (p->flags & VBSR_PLAN_STACKS_PRESPLIT)                 ? false
+                                                                       : big);
+  // Raw-B stacks read straight from B by the SpMM (no pre-pass)
+  p->direct_b = p->raw_b && (p->flags & VBSR_PLAN_B_DIRECT) != 0;
   const int R = d.block_rows;
   // Work units: one per block row, or, for a block row whose cost exceeds a CTA's fair share, one
   // per row part. A row part is rows [r0, r0 + hp) of the block row (multiples of 8) over all its
@@ -635,8 +640,10 @@ vbsr_status build_schedule(vbsr_plan* p) {
                 "smem=%d sms=%d kernel=tcgen05-3xtf32-%s",
                 rhs, nunits, split_rows, stream.size(), p->num_tasks, teams, stages,
                 p->smem_bytes, num_sm,
-                row_stacked(rhs) ? "row-stacked" : (p->raw_b ? "column-stacked-raw-b"
-                                                              : "column-stacked-pre-split"));
+                row_stacked(rhs) ? "row-stacked"
+                : p->direct_b    ? "column-stacked-direct-b"
+                : p->raw_b       ? "column-stacked-raw-b"
+                                 : "column-stacked-pre-split");
   p->summary = buf;
 
   DeviceGuard guard(d.device);
@@ -645,7 +652,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
   VBSR_CUDA(cudaMalloc(&p->d_stream, std::max<size_t>(1, stream.size()) * sizeof(StageDesc)));
   VBSR_CUDA(cudaMalloc(&p->d_items, std::max<size_t>(1, items.size()) * sizeof(ItemDesc)));
   // one M x 8 tile of B's operand stack per 8-column group of B (bstack_kernel)
-  p->bstack_floats = (d.K / 8) * int64_t(stack_rows(rhs, p->raw_b)) * 8;
+  p->bstack_floats = p->direct_b ? 0 : (d.K / 8) * int64_t(stack_rows(rhs, p->raw_b)) * 8;
   if ((d.K / 8) * rhs >= (int64_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "B too large for the pre-pass index range");
   VBSR_CUDA(cudaMalloc(&p->d_bstack, size_t(std::max<int64_t>(1, p->bstack_floats)) * sizeof(float)));
@@ -687,7 +694,7 @@ void free_plan(vbsr_plan* p) {
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
   const int64_t bsg = bs_groups(kp.rhs);
   const int64_t chunks = (kp.K / 8 + bsg - 1) / bsg;  // bs_groups(rhs) groups per block iteration
-  if (chunks > 0 && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
+  if (chunks > 0 && !p->direct_b && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
     const int64_t blocks = std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM);
     switch (kp.rhs) {
       case 8: bstack_kernel<8, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
@@ -714,15 +721,19 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const bool check = (p->flags & VBSR_PLAN_BOUNDS_CHECK) != 0;
+  if (p->direct_b) cfg.numAttrs = 0;  // no pre-pass to overlap
   if (row_stacked(kp.rhs))
-    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, true, false>
-                                   : spmm_tc_kernel<false, true, false>, kp);
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, true, false, false>
+                                   : spmm_tc_kernel<false, true, false, false>, kp);
+  else if (p->direct_b)
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, true, true>
+                                   : spmm_tc_kernel<false, false, true, true>, kp);
   else if (p->raw_b)
-    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, true>
-                                   : spmm_tc_kernel<false, false, true>, kp);
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, true, false>
+                                   : spmm_tc_kernel<false, false, true, false>, kp);
   else
-    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, false>
-                                   : spmm_tc_kernel<false, false, false>, kp);
+    cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, false, false, false>
+                                   : spmm_tc_kernel<false, false, false, false>, kp);
 }
 
 // Enqueues one execute on `stream` after the plan's previous execute (on any stream) has finished
@@ -1013,7 +1024,7 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
 vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out) {
   clear_error();
   if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
-  *out = 2;  // the B pre-pass and the SpMM kernel
+  *out = p->direct_b ? 1 : 2;  // the B pre-pass (unless B is read directly) and the SpMM kernel
   return VBSR_OK;
 }
 

@@ -223,7 +223,12 @@ struct CtaBars {
 
 // Feeder warp f: fills the slots of the stages k with k % kTcFeeders == f, each once the MMAs of
 // the slot's previous stage have completed.
-template <bool CHECK, bool RAW>
+// DIRECT (column-stacked raw form only): the stacks' raw rows come straight from B instead of from
+// the pre-pass: per run of consecutive groups of one block, RHS column c's 8 * n values are
+// contiguous in column-major B, and the lanes copy them in 16-byte pieces (cp.async) into the
+// slot's swizzled stack rows; each lane's copies then arrive on the full barrier
+// (cp.async.mbarrier.arrive), which therefore expects 1 + 32 arrivals.
+template <bool CHECK, bool RAW, bool DIRECT>
 __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
                           const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
   const int D = task.stages, SF = task.stage_floats;
@@ -236,7 +241,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
   // The SpMM is launched as a programmatic dependent of the B pre-pass, so that its prologue
   // overlaps the pre-pass; the feeders are the only warps that read the pre-pass output.
-  griddep_wait();
+  if (!DIRECT) griddep_wait();
   VBSR_PROF_T0(t_all);
   for (int kk = f; kk < nst; kk += kTcFeeders) {
     const Stage st = win.get();
@@ -266,7 +271,8 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     const uint32_t s_dst = sp + uint32_t(slot_stack_bytes(h, groups) + T * lane);
     const float* s_src = p.bstack + (long long)(col >> 3) * (T / 4);
     const uint32_t s_bytes = uint32_t(T * (end - lane));
-    const uint32_t tx = uint32_t(groups * (32 * h + T)), a_bytes = uint32_t(32 * h * groups);
+    const uint32_t tx = uint32_t(groups * (32 * h + (DIRECT ? 0 : T))),
+                   a_bytes = uint32_t(32 * h * groups);
     const float* a_src = p.values + a0;
     asm volatile("" ::"r"(s_dst), "l"(s_src), "r"(s_bytes), "r"(tx), "r"(a_bytes), "l"(a_src));
     VBSR_PROF_T0(t_w);
@@ -286,6 +292,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
         if (!ok) record_status(p.status, VBSR_BOUNDS_VIOLATION, int(blockIdx.x));
         mbar_arrive(full_bar);  // release the split warp without touching memory
       }
+      if (DIRECT) mbar_arrive(full_bar);  // the lanes' copy arrivals
     } else {
       VBSR_TRACE_ST(kk, 7);
       if (lane == 0) {
@@ -298,7 +305,25 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
       if (H != h && lane < groups)
         bulk_g2s(sp + uint32_t(32 * h * lane), a_src + 8ll * H * lane, uint32_t(32 * h), full_bar,
                  pol_a);
-      if (start) bulk_g2s(s_dst, s_src, s_bytes, full_bar, pol_b);
+      if (DIRECT) {
+        // runs in order; run r: groups [r, end_r), first scalar column col_r
+        const uint32_t s0 = sp + uint32_t(slot_stack_bytes(h, groups));
+        for (uint32_t rs = starts; rs != 0; rs &= rs - 1) {
+          const int r = __ffs(rs) - 1;
+          const int n2 = 2 * (__shfl_sync(0xffffffffu, end, r) - r);  // 16-byte pieces per column
+          const float* src0 = p.B + __shfl_sync(0xffffffffu, col, r);
+          const uint32_t dst0 = s0 + uint32_t(T * r);
+          for (int i = lane; i < p.rhs * n2; i += 32) {
+            const int c = i / n2, j = i - c * n2;
+            const uint32_t dst = dst0 + uint32_t(T * (j >> 1) + 32 * c +
+                                                 16 * ((j & 1) ^ ((c >> 2) & 1)));
+            cp_async16(dst, src0 + (long long)c * p.K + 4 * j);
+          }
+        }
+        cp_async_arrive(full_bar);
+      } else if (start) {
+        bulk_g2s(s_dst, s_src, s_bytes, full_bar, pol_b);
+      }
       filled |= 1u << s;
       VBSR_TRACE_ST(kk, 1);
       lastpar = (lastpar & ~(1u << s)) | (ph << s);
@@ -598,7 +623,7 @@ __device__ void tc_epi_warp(const KernelParams& p, const Task& task, const CtaBa
 // MMA warp i (0..3): issues the stages k with k % 4 == i into its partial accumulator (TMEM columns
 // 256 * buffer + 64 * i): one MMA per group in the row-stacked form, two (S x A, S x A_lo) in the
 // column-stacked form.
-template <bool CHECK, bool TR, bool RAW>
+template <bool CHECK, bool TR, bool RAW, bool DIRECT>
 __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t slots,
                             const CtaBars& cb, uint32_t tmem_base, int i, int lane,
                             volatile int* abort_flag) {
@@ -650,6 +675,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
       VBSR_PROF_T0(t_i);
       if (lane == 0) {
         if (math) {
+          if (DIRECT) fence_proxy_async_smem();  // cp.async data, read by the tensor core
           tc_fence_after();
           const uint32_t sa = slots + 4u * uint32_t(s * SF);
           const uint32_t ss = sa + uint32_t(slot_stack_bytes(h, groups));
@@ -766,8 +792,9 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
   }
 }
 
-// TR: row-stacked form (rhs <= 32); RAW: column-stacked form with raw-B stacks.
-template <bool CHECK, bool TR, bool RAW>
+// TR: row-stacked form (rhs <= 32); RAW: column-stacked form with raw-B stacks; DIRECT: those
+// stacks' raw rows read from B itself (no pre-pass).
+template <bool CHECK, bool TR, bool RAW, bool DIRECT>
 __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t slots = (smem_addr(smem_raw) + 1023u) & ~1023u;  // 1024-aligned ring
@@ -785,7 +812,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   if (threadIdx.x == 32) {
     if (p.timing) p.timing[2 * blockIdx.x] = global_ns();
     for (int s = 0; s < task.stages; ++s) {
-      mbar_init(smem_addr(&bars[0][s]), 1u);  // TMA: one arrival + transaction bytes
+      // TMA: one arrival + transaction bytes (DIRECT: + one cp.async arrival per feeder lane)
+      mbar_init(smem_addr(&bars[0][s]), DIRECT ? 33u : 1u);
       mbar_init(smem_addr(&bars[1][s]), 1u);  // the split warp
       mbar_init(smem_addr(&bars[2][s]), 1u);  // the MMA warp's tcgen05.commit
     }
@@ -814,10 +842,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   if (warp < RL::mma0)
     tc_split_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < RL::feeder0)
-    tc_mma_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane,
-                                &abort_flag);
+    tc_mma_warp<CHECK, TR, RAW, DIRECT>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane,
+                                        &abort_flag);
   else if (warp < RL::epi0)
-    tc_feeder<CHECK, RAW>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
+    tc_feeder<CHECK, RAW, DIRECT>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
   else  // the epilogue warps: TMEM quadrant warp % 4
     tc_epi_warp<CHECK, TR, RAW>(p, task, cb, tmem_base, warp & 3, (warp - RL::epi0) >> 2, lane,
                                 &abort_flag);
