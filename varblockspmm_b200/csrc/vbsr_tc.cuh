@@ -228,7 +228,7 @@ struct CtaBars {
 // contiguous in column-major B, and the lanes copy them in 16-byte pieces (cp.async) into the
 // slot's swizzled stack rows; each lane's copies then arrive on the full barrier
 // (cp.async.mbarrier.arrive), which therefore expects 1 + 32 arrivals.
-template <bool CHECK, bool RAW, bool DIRECT, bool NO_A>
+template <bool CHECK, bool RAW, bool DIRECT>
 __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
                           const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
   const int D = task.stages, SF = task.stage_floats;
@@ -271,7 +271,7 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
     const uint32_t s_dst = sp + uint32_t(slot_stack_bytes(h, groups) + T * lane);
     const float* s_src = p.bstack + (long long)(col >> 3) * (T / 4);
     const uint32_t s_bytes = uint32_t(T * (end - lane));
-    const uint32_t tx = uint32_t(groups * ((NO_A ? 0 : 32 * h) + (DIRECT ? 0 : T))),
+    const uint32_t tx = uint32_t(groups * (32 * h + (DIRECT ? 0 : T))),
                    a_bytes = uint32_t(32 * h * groups);
     const float* a_src = p.values + a0;
     asm volatile("" ::"r"(s_dst), "l"(s_src), "r"(s_bytes), "r"(tx), "r"(a_bytes), "l"(a_src));
@@ -297,12 +297,12 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
       VBSR_TRACE_ST(kk, 7);
       if (lane == 0) {
         mbar_arrive_expect_tx(full_bar, tx);
-        if (!NO_A && H == h) bulk_g2s(sp, a_src, a_bytes, full_bar, pol_a);  // one contiguous range
+        if (H == h) bulk_g2s(sp, a_src, a_bytes, full_bar, pol_a);  // one contiguous range
       }
       __syncwarp();
       // a row part: its rows of each group are a separate range (groups H * 8 floats apart); the
       // slot holds them as consecutive h-row groups, the layout of an unsplit item of height h
-      if (!NO_A && H != h && lane < groups)
+      if (H != h && lane < groups)
         bulk_g2s(sp + uint32_t(32 * h * lane), a_src + 8ll * H * lane, uint32_t(32 * h), full_bar,
                  pol_a);
       if (DIRECT) {
@@ -535,88 +535,6 @@ __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int 
   }
 }
 
-#ifndef VBSR_TR_LDG
-#define VBSR_TR_LDG 1
-#endif
-// Row-stacked form, A through registers (kTrLdg): the split warps load each stage's A values from
-// global memory themselves (16-byte loads, one stage ahead per warp, from L2 where the feeders'
-// prefetch put them), wait only until the slot is free, and store every 8-row block u of the stage
-// with its A_lo block into the slot's interleaved layout (block u at byte 512 u, its lo 256 bytes
-// further). The feeders copy only the operand stacks. A slot's full barrier then takes the
-// feeder's arrival (with the stacks' transaction bytes) and the split warp's, and the slot is
-// occupied only from the split warp's stores to the MMAs' commit: the global-memory latency of A
-// is hidden in the split warps' registers instead of in the ring.
-constexpr bool kTrLdg = VBSR_TR_LDG != 0;
-constexpr int kLdgVec = 16;  // float4s per lane of one stage: 32 * h * G <= 8 KB (stage_groups)
-
-// Loads stage `st`'s A into x (float4 i = lane + 32 j of the stage, in the order of the slot's
-// 8-row blocks: block u = i / 16 is block u % (h/8) of group u / (h/8), whose rows start
-// a_start + (u / (h/8)) * 8 H floats in the device format).
-template <bool CHECK>
-__device__ __forceinline__ void ldg_stage(const KernelParams& p, const Stage& st, int lane,
-                                          float4 (&x)[kLdgVec]) {
-  const int h = st.h(), H = st.H(), hb = h >> 3, n = 2 * h * st.groups();
-  const float4* a = reinterpret_cast<const float4*>(p.values + st.a_start());
-  const bool ok = !CHECK || st.a_start() + st.a_span_bytes() / 4 <= p.nvalues;
-#pragma unroll
-  for (int j = 0; j < kLdgVec; ++j) {
-    const int i = lane + 32 * j, u = i >> 4;
-    const int g = u / hb;
-    if (i < n && ok) x[j] = __ldg(a + (long long)g * 2 * H + (u - g * hb) * 16 + (i & 15));
-  }
-}
-
-template <bool CHECK>
-__device__ void tc_split_warp_regs(const KernelParams& p, const Task& task, uint32_t slots,
-                                   const CtaBars& cb, int w, int lane, volatile int* abort_flag) {
-  constexpr int W = Roles<true>::split;
-  const int D = task.stages, SF = task.stage_floats;
-  const int nst = task.stage_end - task.stage_off;
-  const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
-  const bool copies = !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES);
-  // only word 0 of a stage descriptor is needed here (A start, groups, h, H): read one stage ahead
-  const uint64_t* w0s = &p.stages[task.stage_off].w[0];
-  auto word0 = [&](int k) -> uint64_t { return k < nst ? __ldg(w0s + 8ll * k) : 0ull; };
-  float4 x[kLdgVec];
-  Stage st{};
-  st.w0 = word0(w);
-  uint64_t w0_next = word0(w + W);
-  if (w < nst && copies) ldg_stage<CHECK>(p, st, lane, x);
-  int s = w;
-  uint32_t ph = 0;
-  for (int kk = w; kk < nst; kk += W) {
-    if (!wait_phase(cb.empty0 + 8u * s, ph ^ 1u, p, abort_flag, lane)) break;
-    VBSR_TRACE_ST(kk, 2);
-    if (math && copies) {
-      const uint32_t sp = slots + 4u * uint32_t(s * SF);
-      const int n = 2 * st.h() * st.groups();
-#pragma unroll
-      for (int j = 0; j < kLdgVec; ++j) {
-        const int i = lane + 32 * j;
-        if (i < n) {
-          const uint32_t d = sp + 512u * uint32_t(i >> 4) + 16u * uint32_t(i & 15);
-          sts128(d, x[j]);
-          sts128(d + 256u, lo_part4(x[j]));
-        }
-      }
-      fence_proxy_async_smem();
-    }
-    VBSR_TRACE_ST(kk, 6);
-    __syncwarp();
-    if (kk != p.drop_stage && lane == 0) mbar_arrive(cb.full0 + 8u * s);
-    VBSR_TRACE_ST(kk, 3);
-    if (kk + W < nst) {  // this warp's next stage: its loads fly while the other warps work
-      st.w0 = w0_next;
-      w0_next = word0(kk + 2 * W);
-      if (copies) ldg_stage<CHECK>(p, st, lane, x);
-    }
-    if ((s += W) >= D) {
-      s -= D;
-      ph ^= 1u;
-    }
-  }
-}
-
 // Split warp w: forms the lo parts of the stages k with k % Roles<TR>::split == w (slots w,
 // w + Roles<TR>::split, ...).
 template <bool CHECK, bool TR, bool RAW>
@@ -748,7 +666,7 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
         mph ^= 1u;
       }
       VBSR_PROF_T0(t_w);
-      if (!wait_phase((TR && kTrLdg ? cb.full0 : cb.split0) + 8u * s, par, p, abort_flag, lane)) {
+      if (!wait_phase(cb.split0 + 8u * s, par, p, abort_flag, lane)) {
         ok = false;
         break;
       }
@@ -895,8 +813,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     if (p.timing) p.timing[2 * blockIdx.x] = global_ns();
     for (int s = 0; s < task.stages; ++s) {
       // TMA: one arrival + transaction bytes (DIRECT: + one cp.async arrival per feeder lane)
-      // (row-stacked form with A through registers: + the split warp's arrival)
-      mbar_init(smem_addr(&bars[0][s]), DIRECT ? 33u : (TR && kTrLdg) ? 2u : 1u);
+      mbar_init(smem_addr(&bars[0][s]), DIRECT ? 33u : 1u);
       mbar_init(smem_addr(&bars[1][s]), 1u);  // the split warp
       mbar_init(smem_addr(&bars[2][s]), 1u);  // the MMA warp's tcgen05.commit
     }
@@ -922,18 +839,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   cb.drain0 = smem_addr(&drainbars[0]);
 
   using RL = Roles<TR>;
-  if (warp < RL::mma0) {
-    if (TR && kTrLdg)
-      tc_split_warp_regs<CHECK>(p, task, slots, cb, warp, lane, &abort_flag);
-    else
-      tc_split_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
-  }
+  if (warp < RL::mma0)
+    tc_split_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
   else if (warp < RL::feeder0)
     tc_mma_warp<CHECK, TR, RAW, DIRECT>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane,
                                         &abort_flag);
   else if (warp < RL::epi0)
-    tc_feeder<CHECK, RAW, DIRECT, TR && kTrLdg>(p, task, slots, cb, warp - RL::feeder0, lane,
-                                                &abort_flag);
+    tc_feeder<CHECK, RAW, DIRECT>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
   else  // the epilogue warps: TMEM quadrant warp % 4
     tc_epi_warp<CHECK, TR, RAW>(p, task, cb, tmem_base, warp & 3, (warp - RL::epi0) >> 2, lane,
                                 &abort_flag);
