@@ -161,6 +161,10 @@ enum {
    * asynchronous copies of each column's run of values) instead of from a pre-pass buffer, so an
    * execute is one launch and the plan allocates no stack buffer. */
   VBSR_PLAN_B_DIRECT = 1u << 5,
+  /* RHS <= 32: keep every block row on the tensor cores. By default block rows of height 8 or 16
+   * (unless heavy) are computed in plain fp32 on the CUDA cores by warps of the pre-pass launch,
+   * where they cost far less than a tensor-core pipeline stage per few hundred bytes. */
+  VBSR_PLAN_NO_CUDA_CORE_ROWS = 1u << 6,
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
   VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9,   /* consumers wait for the data but compute nothing     */
@@ -242,6 +246,14 @@ vbsr_status vbsr_plan_cta_timing(vbsr_plan* p, int enable, uint64_t* out, int ou
  * the task's most loaded team, for the first n tasks. Either output may be NULL. */
 vbsr_status vbsr_plan_task_stats(const vbsr_plan* p, int32_t* team_warps, double* model_cost,
                                  int n);
+/* How a plan divides the matrix's work (no reference counterpart; for reports and tests):
+ * block rows on the tensor-core kernel (work items, of which split_rows were cut into row parts)
+ * and on the CUDA-core path of the pre-pass launch, with their A value counts. */
+typedef struct vbsr_plan_work {
+  int64_t tc_items, tc_rows, split_rows, tc_values;
+  int64_t cc_rows, cc_values, cc_scalar_rows;
+} vbsr_plan_work;
+vbsr_status vbsr_plan_work_info(const vbsr_plan* p, vbsr_plan_work* out);
 /* Number of CTAs (tasks) one execution launches. */
 vbsr_status vbsr_plan_num_tasks(const vbsr_plan* p, int* out);
 

@@ -368,3 +368,49 @@ def test_upload_across_slices_matches_device_generation(cuda):
     got = run_plan(cuda, host, B, rhs, matrix=gen)
     assert np.array_equal(up.view(np.uint32), got.view(np.uint32))
     assert_within_bound(host, B, rhs, up)
+
+
+CC_CASES = [(1024, 8, 2, False, 41), (777, 16, 0, True, 42), (512, 4, 3, False, 43),
+            (300, 1, 1, True, 44)]
+
+
+@pytest.mark.parametrize("rhs", [8, 16, 32])
+@pytest.mark.parametrize("case", CC_CASES, ids=lambda c: "r%dd%d" % (c[0], c[1]))
+def test_cuda_core_rows(cuda, rhs, case):
+    """Short block rows (h 8 and 16) on the CUDA-core path of the pre-pass launch, the other rows on
+    the tensor cores: the result meets the bound, as does the all-tensor-core plan, and the work
+    split covers every row and value."""
+    rows, deg, dist, local, seed = case
+    host = spec_case(rows, deg, dist, local, seed)
+    B = vb.fill_uniform(seed, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    w = p.work_info()
+    short = int(np.count_nonzero(host.row_size <= 16))
+    assert 0 < w["cc_rows"] <= short
+    assert w["cc_rows"] + w["tc_rows"] == host.block_rows
+    assert w["cc_values"] + w["tc_values"] == host.values.size
+    assert_within_bound(host, B, rhs, run_plan(cuda, host, B, rhs, matrix=m, plan=p))
+    q = vb.Plan(m, vb.PlanOptions(rhs), vb.PLAN_NO_CUDA_CORE_ROWS)
+    assert q.work_info()["cc_rows"] == 0
+    assert_within_bound(host, B, rhs, run_plan(cuda, host, B, rhs, matrix=m, plan=q))
+
+
+@pytest.mark.parametrize("rhs", [8, 32])
+def test_all_rows_on_cuda_cores(cuda, rhs):
+    """A matrix whose block rows are all short (and one empty): no tensor-core CTA is launched,
+    every row is computed by the pre-pass launch, and C is complete (the empty row exactly 0)."""
+    heights = [8, 16, 8, 16, 8] * 20 + [8]
+    widths = [8, 16, 24, 32, 40, 48, 56, 64] * 4
+    rng = np.random.default_rng(5)
+    rows_cols = [sorted(rng.choice(32, 4, replace=False).tolist()) for _ in range(100)] + [[]]
+    host = _handmade(heights, widths, rows_cols, seed=rhs)
+    B = np.random.default_rng(6).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
+    m = vb.Matrix(host)
+    p = vb.Plan(m, vb.PlanOptions(rhs))
+    assert p.work_info()["cc_rows"] == host.block_rows
+    assert p.num_tasks() == 0
+    got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)
+    assert_within_bound(host, B, rhs, got)
+    C = got.reshape(rhs, host.scalar_rows())
+    assert np.all(C[:, host.row_scalar_off[100]:] == 0)

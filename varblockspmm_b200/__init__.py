@@ -149,6 +149,7 @@ _sig = {
     "vbsr_plan_set_debug": [_vp, C.c_int, C.c_int64],
     "vbsr_plan_cta_timing": [_vp, C.c_int, C.POINTER(C.c_uint64), C.c_int, _vp],
     "vbsr_plan_num_tasks": [_vp, C.POINTER(C.c_int)],
+    "vbsr_plan_work_info": [_vp, C.c_void_p],
     "vbsr_plan_task_stats": [_vp, C.POINTER(C.c_int32), C.POINTER(C.c_double), C.c_int],
     "vbsr_launch_row_owned": [C.POINTER(DeviceMatrix), _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp],
     "vbsr_launch_row_owned_scalar": [C.POINTER(DeviceMatrix), _vp, _vp, C.c_int, _vp],
@@ -185,6 +186,7 @@ PLAN_NO_SPLIT = 2
 PLAN_STACKS_RAW = 8        # RHS 64: force raw-B operand stacks (same results)
 PLAN_STACKS_PRESPLIT = 16  # RHS 64: force pre-split operand stacks (same results)
 PLAN_B_DIRECT = 32         # RHS 64: raw-B stack rows read straight from B, no pre-pass
+PLAN_NO_CUDA_CORE_ROWS = 64  # RHS <= 32: keep short block rows on the tensor cores
 PLAN_DIAG_SKIP_COPIES = 1 << 8  # diagnostics only: C is wrong
 PLAN_DIAG_SKIP_MATH = 1 << 9    # diagnostics only: C is wrong
 PLAN_DIAG_SKIP_PREPASS = 1 << 10  # timing only: reuses the previous execute's B stacks
@@ -503,6 +505,14 @@ class Plan:
 
     def set_debug(self, drop_stage: int = -1, wait_limit_cycles: int = 0):
         _check(_lib.vbsr_plan_set_debug(self._h, drop_stage, wait_limit_cycles))
+
+    def work_info(self) -> dict:
+        """How the plan divides the work: tensor-core items/rows (split_rows cut into row parts)
+        and CUDA-core rows, with their A value counts."""
+        w = (C.c_int64 * 7)()
+        _check(_lib.vbsr_plan_work_info(self._h, C.addressof(w)))
+        return dict(zip(("tc_items", "tc_rows", "split_rows", "tc_values", "cc_rows",
+                         "cc_values", "cc_scalar_rows"), list(w)))
 
     def num_tasks(self) -> int:
         n = C.c_int()

@@ -415,6 +415,9 @@ struct vbsr_plan {
   bool direct_b = false;         // ... read from B by the SpMM itself: no pre-pass, no d_bstack
   int64_t bstack_floats = 0;
   Task* d_tasks = nullptr;
+  CcItem* d_cc = nullptr;          // short block rows computed on the CUDA cores (pre-pass launch)
+  int cc_count = 0, cc_warps = 0;
+  vbsr_plan_work work{};
   int* d_status = nullptr;
   unsigned long long* d_timing = nullptr;  // allocated on first request
   bool timing_on = false;
@@ -435,7 +438,9 @@ struct vbsr_plan {
 
 namespace {
 
-constexpr int kSmemBudget = 224 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
+constexpr int kSmemBudget = 224 * 1024;
+constexpr int kCcMaxH = 16;        // block rows this short (RHS <= 32) run on the CUDA cores
+constexpr int kCcWarpsPerSm = 16;  // CUDA-core row warps of the pre-pass launch per SM  // stage bytes per CTA (dynamic allocation adds 1 KB)
 
 // Per-team time model of one item: the bytes its stages move (A and B) plus a fixed cost per stage
 // and per item, in bytes-equivalent units.
@@ -510,8 +515,25 @@ vbsr_status build_schedule(vbsr_plan* p) {
   std::vector<Unit> units;
   units.reserve(size_t(R));
   int split_rows = 0;
+  // Short rows (h <= 16) for RHS <= 32 go to the CUDA-core path of the pre-pass launch, unless
+  // they are heavy, both wider than 1024 columns and above a quarter of an SM's fair share: those
+  // stay here, where the tensor cores' throughput pays (a CUDA-core row is one warp's work).
+  const bool cc_on = row_stacked(rhs) && !(p->flags & VBSR_PLAN_NO_CUDA_CORE_ROWS);
+  std::vector<CcItem> cc;
+  std::vector<double> cc_cost;
   for (int i = 0; i < R; ++i) {
     const int H = d.h_row_size[i];
+    if (cc_on && H <= kCcMaxH && (d.h_sum_w[i] <= 1024 || row_cost[i] <= 0.25 * fair)) {
+      CcItem c{};
+      c.c_row = uint32_t(d.h_row_off[i]);
+      c.h = uint32_t(H);
+      c.b0 = uint32_t(d.h_row_ptr[i]);
+      c.b1 = uint32_t(d.h_row_ptr[i + 1]);
+      c.a_off = uint64_t(d.h_val_off_row[i]);
+      cc.push_back(c);
+      cc_cost.push_back(double(H) * double(d.h_sum_w[i]) + 64.0);
+      continue;
+    }
     int parts = 1;
     if (may_split && R > 1 && row_cost[i] > fair)
       parts = std::min(H / 8, int(std::ceil(row_cost[i] / fair)));
@@ -528,7 +550,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
     }
   }
   const int nunits = int(units.size());
-  const int teams = std::max(1, std::min(num_sm, nunits));
+  const int teams = std::min(num_sm, nunits);  // 0 when every row is on the CUDA cores
   std::vector<int> order(nunits);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(),
@@ -628,6 +650,31 @@ vbsr_status build_schedule(vbsr_plan* p) {
   }
   p->split_rows = split_rows;
   p->work_items = nunits;
+  // CUDA-core rows: the most expensive first, dealt round-robin to the warps
+  {
+    std::vector<int> ord(cc.size());
+    std::iota(ord.begin(), ord.end(), 0);
+    std::stable_sort(ord.begin(), ord.end(), [&](int a, int b) { return cc_cost[a] > cc_cost[b]; });
+    std::vector<CcItem> sorted(cc.size());
+    for (size_t j = 0; j < ord.size(); ++j) sorted[j] = cc[size_t(ord[j])];
+    cc.swap(sorted);
+  }
+  p->cc_count = int(cc.size());
+  {
+    vbsr_plan_work& wk = p->work;
+    wk.tc_items = nunits;
+    wk.split_rows = split_rows;
+    wk.cc_rows = int64_t(cc.size());
+    wk.tc_rows = R - wk.cc_rows;
+    for (const CcItem& c : cc) {
+      int64_t sw = 0;
+      for (uint32_t b = c.b0; b < c.b1; ++b) sw += int64_t((d.h_blk_desc[b] & 7u) + 1u) * 8;
+      wk.cc_values += int64_t(c.h) * sw;
+      wk.cc_scalar_rows += int64_t(c.h);
+    }
+    wk.tc_values = d.nvalues - wk.cc_values;
+  }
+  p->cc_warps = std::min(p->cc_count, num_sm * kCcWarpsPerSm);
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
   p->smem_bytes = stages * slot * 4 + kSmemTailPad + 1024;  // + alignment of the ring
@@ -636,9 +683,9 @@ vbsr_status build_schedule(vbsr_plan* p) {
 
   char buf[512];
   std::snprintf(buf, sizeof buf,
-                "rhs=%d items=%d split_rows=%d pipeline_stages=%zu tasks=%d teams=%d ring=%d "
-                "smem=%d sms=%d kernel=tcgen05-3xtf32-%s",
-                rhs, nunits, split_rows, stream.size(), p->num_tasks, teams, stages,
+                "rhs=%d items=%d split_rows=%d cuda_core_rows=%d pipeline_stages=%zu tasks=%d "
+                "teams=%d ring=%d smem=%d sms=%d kernel=tcgen05-3xtf32-%s",
+                rhs, nunits, split_rows, p->cc_count, stream.size(), p->num_tasks, teams, stages,
                 p->smem_bytes, num_sm,
                 row_stacked(rhs) ? "row-stacked"
                 : p->direct_b    ? "column-stacked-direct-b"
@@ -671,6 +718,11 @@ vbsr_status build_schedule(vbsr_plan* p) {
     VBSR_CUDA(cudaMemcpyAsync(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
                               cudaMemcpyHostToDevice, ss.s));
   VBSR_CUDA(cudaMemsetAsync(p->d_status, 0, kStatusWords * sizeof(int), ss.s));
+  if (!cc.empty()) {
+    VBSR_CUDA(cudaMalloc(&p->d_cc, cc.size() * sizeof(CcItem)));
+    VBSR_CUDA(cudaMemcpyAsync(p->d_cc, cc.data(), cc.size() * sizeof(CcItem),
+                              cudaMemcpyHostToDevice, ss.s));
+  }
   VBSR_CUDA(ss.finish());
   VBSR_CUDA(cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming));
   VBSR_CUDA(set_kernel_attrs());
@@ -686,6 +738,7 @@ void free_plan(vbsr_plan* p) {
   cudaFree(p->d_tasks);
   cudaFree(p->d_status);
   cudaFree(p->d_timing);
+  cudaFree(p->d_cc);
   if (p->done != nullptr) cudaEventDestroy(p->done);
   delete p;
 }
@@ -694,20 +747,31 @@ void free_plan(vbsr_plan* p) {
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
   const int64_t bsg = bs_groups(kp.rhs);
   const int64_t chunks = (kp.K / 8 + bsg - 1) / bsg;  // bs_groups(rhs) groups per block iteration
+  CcParams cc{};
+  cc.items = p->d_cc;
+  cc.count = p->cc_count;
+  cc.warps = p->cc_warps;
+  cc.values = kp.values;
+  cc.blk_desc = p->m->d.d_blk_desc;
+  cc.C = kp.C;
+  cc.M = kp.M;
+  const int cc_blocks = (p->cc_warps + 7) / 8;
   if (chunks > 0 && !p->direct_b && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
-    const int64_t blocks = std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM);
+    const int stack = int(std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM));
+    const unsigned blocks = unsigned(stack + cc_blocks);
     switch (kp.rhs) {
-      case 8: bstack_kernel<8, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
-      case 16: bstack_kernel<16, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
-      case 32: bstack_kernel<32, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack); break;
+      case 8: bstack_kernel<8, false><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc); break;
+      case 16: bstack_kernel<16, false><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc); break;
+      case 32: bstack_kernel<32, false><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc); break;
       default:
         if (p->raw_b)
-          bstack_kernel<64, true><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack);
+          bstack_kernel<64, true><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc);
         else
-          bstack_kernel<64, false><<<unsigned(blocks), 256, 0, stream>>>(kp.B, kp.K, p->d_bstack);
+          bstack_kernel<64, false><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc);
         break;
     }
   }
+  if (p->num_tasks == 0) return;  // every row on the CUDA cores
   // programmatic dependent launch: the SpMM's prologue overlaps the pre-pass (its feeders wait
   // for the pre-pass with griddepcontrol.wait before the first copy)
   cudaLaunchConfig_t cfg = {};
@@ -923,7 +987,7 @@ vbsr_status vbsr_plan_execute(const vbsr_plan* p, const float* B, float* C, vbsr
     vbsr_matrix_device_view(p->m, &view);
     return launch_view_kernel(&view, B, C, p->rhs, s, false);
   }
-  if (p->num_tasks == 0) return VBSR_OK;
+  if (p->num_tasks == 0 && p->cc_count == 0) return VBSR_OK;
   KernelParams kp;
   vbsr_status st = fill_params(p, B, C, p->d_status, p->timing_on ? p->d_timing : nullptr, &kp);
   if (st != VBSR_OK) return st;
@@ -993,7 +1057,7 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
     VBSR_CUDA(cudaStreamSynchronize(s));
     return VBSR_OK;
   }
-  if (p->num_tasks == 0) return VBSR_OK;
+  if (p->num_tasks == 0 && p->cc_count == 0) return VBSR_OK;
   unsigned long long* scratch = nullptr;
   vbsr_status st = noalloc_scratch(p->device, &scratch);
   if (st != VBSR_OK) return st;
@@ -1093,6 +1157,13 @@ vbsr_status vbsr_plan_task_stats(const vbsr_plan* p, int32_t* team_warps, double
     if (team_warps) team_warps[i] = p->task_warps[i];
     if (model_cost) model_cost[i] = p->task_cost[i];
   }
+  return VBSR_OK;
+}
+
+vbsr_status vbsr_plan_work_info(const vbsr_plan* p, vbsr_plan_work* out) {
+  clear_error();
+  if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
+  *out = p->work;
   return VBSR_OK;
 }
 

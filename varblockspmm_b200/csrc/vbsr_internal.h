@@ -56,6 +56,16 @@ struct alignas(16) ItemDesc {
 };
 static_assert(sizeof(ItemDesc) == 16, "ItemDesc layout");
 
+// A block row computed on the CUDA cores (short rows, h <= 16, RHS <= 32; see cc_rows in
+// vbsr_tc.cuh): its C rows, height, device-format A start and block range.
+struct alignas(16) CcItem {
+  uint32_t c_row, h;
+  uint32_t b0, b1;  // blocks [b0, b1) of the matrix (their descriptors in d_blk_desc)
+  uint64_t a_off;   // first A value of the row in the device format
+  uint64_t pad;
+};
+static_assert(sizeof(CcItem) == 32, "CcItem layout");
+
 // One CTA task: items [item_off, item_end) and stages [stage_off, stage_end) of the plan's lists.
 struct alignas(16) Task {
   int item_off, item_end, stage_off, stage_end;

@@ -776,6 +776,112 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
   }
 }
 
+// Short block rows on the CUDA cores. Rows of height 8 or 16 waste most of a tcgen05 MMA (its M
+// side is 64 rows) and pay a full pipeline stage per few hundred bytes of A, while their arithmetic
+// is small; for RHS <= 32 the plan takes them out of the tensor-core schedule and the pre-pass
+// launch computes them here, one warp per block row, in plain fp32 FMA (no operand splitting
+// needed). The warp walks the row's blocks in chunks of 16 block columns: it stages the chunk's
+// B values transposed, Bs[k][c] (row stride RHS + 1: conflict-free), and its A values, As[k][r],
+// in its own shared memory, then lane (c, row set) accumulates its column over its rows: per 8
+// block columns a fresh fp32 partial (8 FMAs), added into the row's accumulator.
+struct CcParams {
+  const CcItem* items;
+  int count;
+  int warps;  // warps working on the items (item i by warp i % warps)
+  const float* values;
+  const uint32_t* blk_desc;
+  float* C;
+  long long M;
+};
+constexpr int kCcChunk = 16;  // block columns per staged chunk
+
+template <int RHS, int H>
+__device__ void cc_row(const CcParams& q, const CcItem& it, const float* __restrict__ B, long long K,
+                       float* bs, float* as, int lane) {
+  constexpr int L = 32 / RHS;   // lanes per column (row sets)
+  constexpr int RPL = H / L;    // rows per lane
+  const int c = lane % RHS, r0 = (lane / RHS) * RPL;
+  float acc[RPL];
+#pragma unroll
+  for (int r = 0; r < RPL; ++r) acc[r] = 0.0f;
+  const float* a = q.values + it.a_off;
+  for (uint32_t b = it.b0; b < it.b1; ++b) {
+    const uint32_t desc = __ldg(q.blk_desc + b);
+    const int w = int((desc & 7u) + 1u) * 8;
+    const float* bcol = B + (long long)(desc & ~7u);
+    for (int k0 = 0; k0 < w; k0 += kCcChunk) {
+      const int ng = (w - k0) >= kCcChunk ? 2 : 1;  // 8-column groups in this chunk
+      // stage B[k0 .. k0 + 8 ng) of every column: RHS x 2 ng float4s, transposed into bs[k][c]
+#pragma unroll
+      for (int i = lane; i < RHS * 4; i += 32) {
+        const int cc = i >> 2, qd = i & 3;
+        if (qd >= 2 * ng) continue;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(bcol + (long long)cc * K + k0) + qd);
+        float* d = bs + (4 * qd) * (RHS + 1) + cc;
+        d[0] = v.x;
+        d[RHS + 1] = v.y;
+        d[2 * (RHS + 1)] = v.z;
+        d[3 * (RHS + 1)] = v.w;
+      }
+      // stage A: two 8-column groups of H rows (device format: row r's 8 values at 8 r, the
+      // 16-byte halves exchanged when bit 2 of r is set), transposed into as[k][r]
+#pragma unroll
+      for (int i = lane; i < 2 * H * 2; i += 32) {
+        const int g = i / (2 * H), rem = i % (2 * H), r = rem >> 1, u = rem & 1;
+        if (g >= ng) continue;
+        const int kq = 8 * g + 4 * (u ^ ((r >> 2) & 1));
+        const float4 v = __ldg(reinterpret_cast<const float4*>(a + (long long)H * (k0 + 8 * g)) + rem);
+        as[(kq + 0) * H + r] = v.x;
+        as[(kq + 1) * H + r] = v.y;
+        as[(kq + 2) * H + r] = v.z;
+        as[(kq + 3) * H + r] = v.w;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        if (g >= ng) break;
+        float part[RPL];
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) part[r] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int k = 8 * g + kk;
+          const float bv = bs[k * (RHS + 1) + c];
+#pragma unroll
+          for (int r = 0; r < RPL; ++r) part[r] = fmaf(as[k * H + r0 + r], bv, part[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) acc[r] += part[r];
+      }
+      __syncwarp();
+    }
+    a += (long long)H * w;
+  }
+  // lane (c, row set) owns RPL consecutive rows of column c: RPL / 4 16-byte stores
+  float4* dst = reinterpret_cast<float4*>(q.C + (long long)c * q.M + it.c_row + r0);
+#pragma unroll
+  for (int r = 0; r < RPL; r += 4) dst[r / 4] = make_float4(acc[r], acc[r + 1], acc[r + 2], acc[r + 3]);
+}
+
+// smem floats per warp: bs (16 x (RHS + 1)) + as (16 x 16)
+template <int RHS>
+__host__ __device__ constexpr int cc_warp_floats() { return kCcChunk * (RHS + 1) + kCcChunk * 16; }
+
+template <int RHS>
+__device__ void cc_rows(const CcParams& q, const float* __restrict__ B, long long K, int cc_block,
+                        float* smem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* bs = smem + warp * cc_warp_floats<RHS>();
+  float* as = bs + kCcChunk * (RHS + 1);
+  for (int i = cc_block * 8 + warp; i < q.count; i += q.warps) {
+    const CcItem it = q.items[i];
+    if (it.h == 8)
+      cc_row<RHS, 8>(q, it, B, K, bs, as, lane);
+    else
+      cc_row<RHS, 16>(q, it, B, K, bs, as, lane);
+  }
+}
+
 // Pre-pass: the operand stacks S of all 8-column groups of B (K x rhs, column-major), one tile of
 // stack_rows(rhs) rows x 8 floats per group (kg = k / 8) in the layout the MMA reads. Row-stacked
 // form (rhs <= 32): row c holds the 8 values of RHS column c (raw, i.e. hi), row rhs + c their lo
@@ -783,7 +889,8 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // c = half*q + j, row 2*half*q + half + j its lo parts. The two 16-byte halves of row r are
 // exchanged when bit 2 of r is set (32-byte swizzle). A block transposes kBsGroups consecutive
 // groups through shared memory: it reads each RHS column's 8 * kBsGroups consecutive values
-// (coalesced), then writes the kBsGroups tiles (contiguous) with 16-byte stores.
+// (coalesced), then writes the kBsGroups tiles (contiguous) with 16-byte stores. Blocks from
+// `stack_blocks` on compute the plan's short block rows on the CUDA cores instead (cc_rows).
 #ifndef VBSR_BS_GROUPS
 #define VBSR_BS_GROUPS 16
 #endif
@@ -801,15 +908,23 @@ __host__ __device__ constexpr int bs_groups(int rhs) {
 }
 template <int RHS, bool RAW>
 __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
-                                                     float* __restrict__ out) {
+                                                     float* __restrict__ out, int stack_blocks,
+                                                     const CcParams cc) {
   constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS, RAW);
   constexpr int kBsGroups = bs_groups(RHS);
   constexpr int per_col = 2 * kBsGroups;  // float4s per column run
-  __shared__ float4 buf[RHS * per_col];  // [c][kg][2 x float4]: up to 32 KB
+  constexpr int kCcFloat4s = RHS <= 32 ? 8 * cc_warp_floats<(RHS <= 32 ? RHS : 32)>() / 4 : 0;
+  // [c][kg][2 x float4] for stacking (up to 32 KB), or the CUDA-core warps' staging
+  __shared__ float4 buf[RHS * per_col > kCcFloat4s ? RHS * per_col : kCcFloat4s];
   griddep_launch_dependents();  // the SpMM may start its prologue now (it waits before reading)
+  if (RHS <= 32 && int(blockIdx.x) >= stack_blocks) {
+    cc_rows<(RHS <= 32 ? RHS : 32)>(cc, B, K, int(blockIdx.x) - stack_blocks,
+                                    reinterpret_cast<float*>(buf));
+    return;
+  }
   const long long ngroups = K >> 3;
   for (long long kg0 = (long long)blockIdx.x * kBsGroups; kg0 < ngroups;
-       kg0 += (long long)gridDim.x * kBsGroups) {
+       kg0 += (long long)stack_blocks * kBsGroups) {
     const int ng = int(ngroups - kg0 < kBsGroups ? ngroups - kg0 : kBsGroups);
     // read: each RHS column's run of 8 * kBsGroups values (coalesced)
     const float* src = B + 8 * kg0;
