@@ -416,7 +416,7 @@ struct vbsr_plan {
   int64_t bstack_floats = 0;
   Task* d_tasks = nullptr;
   CcItem* d_cc = nullptr;          // short block rows computed on the CUDA cores (pre-pass launch)
-  int cc_count = 0, cc_warps = 0;
+  int cc_count = 0;
   vbsr_plan_work work{};
   int* d_status = nullptr;
   unsigned long long* d_timing = nullptr;  // allocated on first request
@@ -674,7 +674,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
     }
     wk.tc_values = d.nvalues - wk.cc_values;
   }
-  p->cc_warps = std::min(p->cc_count, num_sm * kCcWarpsPerSm);
+
   if (stream.size() >= (size_t(1) << 31))
     return set_error(VBSR_INVALID_ARGUMENT, "schedule too large");
   p->smem_bytes = stages * slot * 4 + kSmemTailPad + 1024;  // + alignment of the ring
@@ -750,12 +750,11 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   CcParams cc{};
   cc.items = p->d_cc;
   cc.count = p->cc_count;
-  cc.warps = p->cc_warps;
   cc.values = kp.values;
   cc.blk_desc = p->m->d.d_blk_desc;
   cc.C = kp.C;
   cc.M = kp.M;
-  const int cc_blocks = (p->cc_warps + 7) / 8;
+  const int cc_blocks = p->cc_count;  // one CTA per short block row
   if (chunks > 0 && !p->direct_b && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
     const int stack = int(std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM));
     const unsigned blocks = unsigned(stack + cc_blocks);

@@ -779,107 +779,178 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // Short block rows on the CUDA cores. Rows of height 8 or 16 waste most of a tcgen05 MMA (its M
 // side is 64 rows) and pay a full pipeline stage per few hundred bytes of A, while their arithmetic
 // is small; for RHS <= 32 the plan takes them out of the tensor-core schedule and the pre-pass
-// launch computes them here, one warp per block row, in plain fp32 FMA (no operand splitting
-// needed). The warp walks the row's blocks in chunks of 16 block columns: it stages the chunk's
-// B values transposed, Bs[k][c] (row stride RHS + 1: conflict-free), and its A values, As[k][r],
-// in its own shared memory, then lane (c, row set) accumulates its column over its rows: per 8
-// block columns a fresh fp32 partial (8 FMAs), added into the row's accumulator.
+// launch computes them here in plain fp32 FMA (no operand splitting needed), one CTA of 8 warps per
+// block row: warp w takes the row's blocks w, w + 8, ... and walks each in chunks of 16 block
+// columns. A chunk's B values are staged transposed, bs[k][c] (row stride RHS + 1:
+// conflict-free), and its A values as as[k][r], in the warp's shared memory; the next chunk's
+// global loads are issued before the current chunk is computed. Lane (c, row set) accumulates its
+// column over its rows (per 8 block columns a fresh fp32 partial of 8 FMAs, added into the
+// accumulator). At the end the warps' partial tiles are summed in warp order through shared memory
+// and the CTA stores the row's h x RHS tile of C once (no atomics, no global workspace).
 struct CcParams {
   const CcItem* items;
   int count;
-  int warps;  // warps working on the items (item i by warp i % warps)
   const float* values;
   const uint32_t* blk_desc;
   float* C;
   long long M;
 };
 constexpr int kCcChunk = 16;  // block columns per staged chunk
+constexpr int kCcWarps = 8;   // warps per block row
+
+// smem floats per warp: bs (16 x (RHS + 1)) + as (16 x 16); the partial tile (16 x RHS) fits too
+template <int RHS>
+__host__ __device__ constexpr int cc_warp_floats() { return kCcChunk * (RHS + 1) + kCcChunk * 16; }
+
+// One chunk's global values in registers: lane i of B's RHS x 4 float4s (16 columns) and of A's
+// two 8-column groups of H rows (H x 4 float4s).
+template <int RHS, int H>
+struct CcChunk {
+  static constexpr int NB = (RHS * 4 + 31) / 32, NA = (H * 4 + 31) / 32;
+  float4 b[NB], a[NA];
+  int ng;  // 8-column groups in the chunk (1 or 2); 0 when there is none
+};
 
 template <int RHS, int H>
-__device__ void cc_row(const CcParams& q, const CcItem& it, const float* __restrict__ B, long long K,
-                       float* bs, float* as, int lane) {
+__device__ __forceinline__ void cc_load(CcChunk<RHS, H>& x, const float* bcol, const float* a,
+                                        long long K, int k0, int w, int lane) {
+  x.ng = w - k0 >= kCcChunk ? 2 : 1;
+#pragma unroll
+  for (int t = 0; t < x.NB; ++t) {
+    const int i = lane + 32 * t, cc = i >> 2, qd = i & 3;
+    if (i < RHS * 4 && qd < 2 * x.ng)
+      x.b[t] = __ldg(reinterpret_cast<const float4*>(bcol + (long long)cc * K + k0) + qd);
+  }
+#pragma unroll
+  for (int t = 0; t < x.NA; ++t) {
+    const int i = lane + 32 * t;  // group i / (2H), float4 i % (2H) of it
+    if (i < H * 4 && i / (2 * H) < x.ng)
+      x.a[t] = __ldg(reinterpret_cast<const float4*>(a + (long long)H * k0) + i);
+  }
+}
+
+template <int RHS, int H>
+__device__ __forceinline__ void cc_stage(const CcChunk<RHS, H>& x, float* bs, float* as, int lane) {
+#pragma unroll
+  for (int t = 0; t < x.NB; ++t) {
+    const int i = lane + 32 * t, cc = i >> 2, qd = i & 3;
+    if (i < RHS * 4 && qd < 2 * x.ng) {
+      float* d = bs + (4 * qd) * (RHS + 1) + cc;
+      d[0] = x.b[t].x;
+      d[RHS + 1] = x.b[t].y;
+      d[2 * (RHS + 1)] = x.b[t].z;
+      d[3 * (RHS + 1)] = x.b[t].w;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < x.NA; ++t) {
+    const int i = lane + 32 * t, g = i / (2 * H), rem = i % (2 * H), r = rem >> 1, u = rem & 1;
+    if (i < H * 4 && g < x.ng) {
+      // device format: row r's 8 values at 8 r, its 16-byte halves exchanged when bit 2 of r is set
+      const int kq = 8 * g + 4 * (u ^ ((r >> 2) & 1));
+      as[(kq + 0) * H + r] = x.a[t].x;
+      as[(kq + 1) * H + r] = x.a[t].y;
+      as[(kq + 2) * H + r] = x.a[t].z;
+      as[(kq + 3) * H + r] = x.a[t].w;
+    }
+  }
+}
+
+template <int RHS, int H>
+__device__ void cc_row_cta(const CcParams& q, const CcItem& it, const float* __restrict__ B,
+                           long long K, float* smem) {
   constexpr int L = 32 / RHS;   // lanes per column (row sets)
   constexpr int RPL = H / L;    // rows per lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* bs = smem + warp * cc_warp_floats<RHS>();
+  float* as = bs + kCcChunk * (RHS + 1);
   const int c = lane % RHS, r0 = (lane / RHS) * RPL;
   float acc[RPL];
 #pragma unroll
   for (int r = 0; r < RPL; ++r) acc[r] = 0.0f;
+  // this warp's chunks: blocks b0 + warp, b0 + warp + 8, ...; each in chunks of 16 columns
+  uint32_t b = it.b0 + uint32_t(warp);
   const float* a = q.values + it.a_off;
-  for (uint32_t b = it.b0; b < it.b1; ++b) {
+  for (uint32_t j = it.b0; j < b && j < it.b1; ++j)
+    a += (long long)H * int((__ldg(q.blk_desc + j) & 7u) + 1u) * 8;
+  int k0 = 0, w = 0;
+  const float* bcol = B;
+  if (b < it.b1) {
     const uint32_t desc = __ldg(q.blk_desc + b);
-    const int w = int((desc & 7u) + 1u) * 8;
-    const float* bcol = B + (long long)(desc & ~7u);
-    for (int k0 = 0; k0 < w; k0 += kCcChunk) {
-      const int ng = (w - k0) >= kCcChunk ? 2 : 1;  // 8-column groups in this chunk
-      // stage B[k0 .. k0 + 8 ng) of every column: RHS x 2 ng float4s, transposed into bs[k][c]
-#pragma unroll
-      for (int i = lane; i < RHS * 4; i += 32) {
-        const int cc = i >> 2, qd = i & 3;
-        if (qd >= 2 * ng) continue;
-        const float4 v = __ldg(reinterpret_cast<const float4*>(bcol + (long long)cc * K + k0) + qd);
-        float* d = bs + (4 * qd) * (RHS + 1) + cc;
-        d[0] = v.x;
-        d[RHS + 1] = v.y;
-        d[2 * (RHS + 1)] = v.z;
-        d[3 * (RHS + 1)] = v.w;
-      }
-      // stage A: two 8-column groups of H rows (device format: row r's 8 values at 8 r, the
-      // 16-byte halves exchanged when bit 2 of r is set), transposed into as[k][r]
-#pragma unroll
-      for (int i = lane; i < 2 * H * 2; i += 32) {
-        const int g = i / (2 * H), rem = i % (2 * H), r = rem >> 1, u = rem & 1;
-        if (g >= ng) continue;
-        const int kq = 8 * g + 4 * (u ^ ((r >> 2) & 1));
-        const float4 v = __ldg(reinterpret_cast<const float4*>(a + (long long)H * (k0 + 8 * g)) + rem);
-        as[(kq + 0) * H + r] = v.x;
-        as[(kq + 1) * H + r] = v.y;
-        as[(kq + 2) * H + r] = v.z;
-        as[(kq + 3) * H + r] = v.w;
-      }
-      __syncwarp();
-#pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        if (g >= ng) break;
-        float part[RPL];
-#pragma unroll
-        for (int r = 0; r < RPL; ++r) part[r] = 0.0f;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const int k = 8 * g + kk;
-          const float bv = bs[k * (RHS + 1) + c];
-#pragma unroll
-          for (int r = 0; r < RPL; ++r) part[r] = fmaf(as[k * H + r0 + r], bv, part[r]);
-        }
-#pragma unroll
-        for (int r = 0; r < RPL; ++r) acc[r] += part[r];
-      }
-      __syncwarp();
-    }
-    a += (long long)H * w;
+    w = int((desc & 7u) + 1u) * 8;
+    bcol = B + (long long)(desc & ~7u);
   }
-  // lane (c, row set) owns RPL consecutive rows of column c: RPL / 4 16-byte stores
-  float4* dst = reinterpret_cast<float4*>(q.C + (long long)c * q.M + it.c_row + r0);
+  CcChunk<RHS, H> cur, nxt;
+  cur.ng = 0;
+  if (b < it.b1) cc_load<RHS, H>(cur, bcol, a, K, 0, w, lane);
+  while (b < it.b1) {
+    // the next chunk of this warp: the rest of this block, or its next block
+    uint32_t nb = b;
+    int nk0 = k0 + kCcChunk, nw = w;
+    const float* na = a;
+    const float* nbcol = bcol;
+    if (nk0 >= w) {
+      na = a + (long long)H * w;
+      for (uint32_t j = b + 1; j < b + kCcWarps && j < it.b1; ++j)
+        na += (long long)H * int((__ldg(q.blk_desc + j) & 7u) + 1u) * 8;
+      nb = b + kCcWarps;
+      nk0 = 0;
+      if (nb < it.b1) {
+        const uint32_t desc = __ldg(q.blk_desc + nb);
+        nw = int((desc & 7u) + 1u) * 8;
+        nbcol = B + (long long)(desc & ~7u);
+      }
+    }
+    if (nb < it.b1) cc_load<RHS, H>(nxt, nbcol, na, K, nk0, nw, lane);
+    cc_stage<RHS, H>(cur, bs, as, lane);
+    __syncwarp();
 #pragma unroll
-  for (int r = 0; r < RPL; r += 4) dst[r / 4] = make_float4(acc[r], acc[r + 1], acc[r + 2], acc[r + 3]);
+    for (int g = 0; g < 2; ++g) {
+      if (g >= cur.ng) break;
+      float part[RPL];
+#pragma unroll
+      for (int r = 0; r < RPL; ++r) part[r] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int k = 8 * g + kk;
+        const float bv = bs[k * (RHS + 1) + c];
+#pragma unroll
+        for (int r = 0; r < RPL; ++r) part[r] = fmaf(as[k * H + r0 + r], bv, part[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < RPL; ++r) acc[r] += part[r];
+    }
+    __syncwarp();
+    b = nb;
+    k0 = nk0;
+    w = nw;
+    a = na;
+    bcol = nbcol;
+    cur = nxt;
+  }
+  // partial tiles -> shared memory (each warp's own staging area), summed in warp order
+  float* part = smem + warp * cc_warp_floats<RHS>();
+#pragma unroll
+  for (int r = 0; r < RPL; ++r) part[(r0 + r) * RHS + c] = acc[r];
+  __syncthreads();
+  for (int e = threadIdx.x; e < H * RHS; e += blockDim.x) {
+    const int r = e % H, cc = e / H;  // consecutive threads: consecutive rows of one column
+    float sum = 0.0f;
+#pragma unroll
+    for (int v = 0; v < kCcWarps; ++v) sum += smem[v * cc_warp_floats<RHS>() + r * RHS + cc];
+    q.C[(long long)cc * q.M + it.c_row + r] = sum;
+  }
+  __syncthreads();
 }
 
-// smem floats per warp: bs (16 x (RHS + 1)) + as (16 x 16)
 template <int RHS>
-__host__ __device__ constexpr int cc_warp_floats() { return kCcChunk * (RHS + 1) + kCcChunk * 16; }
-
-template <int RHS>
-__device__ void cc_rows(const CcParams& q, const float* __restrict__ B, long long K, int cc_block,
+__device__ void cc_rows(const CcParams& q, const float* __restrict__ B, long long K, int item,
                         float* smem) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* bs = smem + warp * cc_warp_floats<RHS>();
-  float* as = bs + kCcChunk * (RHS + 1);
-  for (int i = cc_block * 8 + warp; i < q.count; i += q.warps) {
-    const CcItem it = q.items[i];
-    if (it.h == 8)
-      cc_row<RHS, 8>(q, it, B, K, bs, as, lane);
-    else
-      cc_row<RHS, 16>(q, it, B, K, bs, as, lane);
-  }
+  const CcItem it = q.items[item];
+  if (it.h == 8)
+    cc_row_cta<RHS, 8>(q, it, B, K, smem);
+  else
+    cc_row_cta<RHS, 16>(q, it, B, K, smem);
 }
 
 // Pre-pass: the operand stacks S of all 8-column groups of B (K x rhs, column-major), one tile of
@@ -913,7 +984,8 @@ __global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B
   constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS, RAW);
   constexpr int kBsGroups = bs_groups(RHS);
   constexpr int per_col = 2 * kBsGroups;  // float4s per column run
-  constexpr int kCcFloat4s = RHS <= 32 ? 8 * cc_warp_floats<(RHS <= 32 ? RHS : 32)>() / 4 : 0;
+  constexpr int kCcFloat4s =
+      RHS <= 32 ? kCcWarps * cc_warp_floats<(RHS <= 32 ? RHS : 32)>() / 4 : 0;
   // [c][kg][2 x float4] for stacking (up to 32 KB), or the CUDA-core warps' staging
   __shared__ float4 buf[RHS * per_col > kCcFloat4s ? RHS * per_col : kCcFloat4s];
   griddep_launch_dependents();  // the SpMM may start its prologue now (it waits before reading)
