@@ -780,13 +780,14 @@ __device__ void tc_mma_warp(const KernelParams& p, const Task& task, uint32_t sl
 // side is 64 rows) and pay a full pipeline stage per few hundred bytes of A, while their arithmetic
 // is small; for RHS <= 32 the plan takes them out of the tensor-core schedule and the pre-pass
 // launch computes them here in plain fp32 FMA (no operand splitting needed), one CTA of 8 warps per
-// block row: warp w takes the row's blocks w, w + 8, ... and walks each in chunks of 16 block
-// columns. A chunk's B values are staged transposed, bs[k][c] (row stride RHS + 1:
-// conflict-free), and its A values as as[k][r], in the warp's shared memory; the next chunk's
-// global loads are issued before the current chunk is computed. Lane (c, row set) accumulates its
-// column over its rows (per 8 block columns a fresh fp32 partial of 8 FMAs, added into the
-// accumulator). At the end the warps' partial tiles are summed in warp order through shared memory
-// and the CTA stores the row's h x RHS tile of C once (no atomics, no global workspace).
+// block row. A warp owns 8 rows of the tile (a 16-row block row has two row halves of 4 warps
+// each) and a share of the row's blocks (every 8th, or every 4th for a row half), and walks them
+// in 8-column groups: the group's B values are staged transposed, bs[k][c] (row stride RHS + 1:
+// conflict-free), and its A values as as[k][r] in the warp's shared memory, while the next group's
+// global loads are already in flight. Lane (c, row set) accumulates its column over its rows (per
+// group a fresh fp32 partial of 8 FMAs, added into the accumulator). At the end the warps' partial
+// tiles are summed in warp order through shared memory and the CTA stores the row's h x RHS tile
+// of C once (no atomics, no global workspace).
 struct CcParams {
   const CcItem* items;
   int count;
@@ -795,149 +796,140 @@ struct CcParams {
   float* C;
   long long M;
 };
-constexpr int kCcChunk = 16;  // block columns per staged chunk
-constexpr int kCcWarps = 8;   // warps per block row
+constexpr int kCcWarps = 8;  // warps per block row
 
-// smem floats per warp: bs (16 x (RHS + 1)) + as (16 x 16); the partial tile (16 x RHS) fits too
+// smem floats per warp: bs (8 x (RHS + 1)) + as (8 x 8); the partial tile (8 x RHS) as well
 template <int RHS>
-__host__ __device__ constexpr int cc_warp_floats() { return kCcChunk * (RHS + 1) + kCcChunk * 16; }
+__host__ __device__ constexpr int cc_warp_floats() {
+  return 8 * (RHS + 1) + 64 > 8 * RHS ? 8 * (RHS + 1) + 64 : 8 * RHS;
+}
 
-// One chunk's global values in registers: lane i of B's RHS x 4 float4s (16 columns) and of A's
-// two 8-column groups of H rows (H x 4 float4s).
-template <int RHS, int H>
-struct CcChunk {
-  static constexpr int NB = (RHS * 4 + 31) / 32, NA = (H * 4 + 31) / 32;
-  float4 b[NB], a[NA];
-  int ng;  // 8-column groups in the chunk (1 or 2); 0 when there is none
+// One 8-column group's global values in registers: lane i < 2 RHS holds float4 i of B (column
+// i / 2, half i % 2; RHS 32: columns 16 + i / 2 in b1 as well), lane i < 16 float4 i of the
+// warp's 8 A rows (row i / 2, storage half i % 2).
+struct CcGroup {
+  float4 b0, b1, a;
 };
 
-template <int RHS, int H>
-__device__ __forceinline__ void cc_load(CcChunk<RHS, H>& x, const float* bcol, const float* a,
-                                        long long K, int k0, int w, int lane) {
-  x.ng = w - k0 >= kCcChunk ? 2 : 1;
-#pragma unroll
-  for (int t = 0; t < x.NB; ++t) {
-    const int i = lane + 32 * t, cc = i >> 2, qd = i & 3;
-    if (i < RHS * 4 && qd < 2 * x.ng)
-      x.b[t] = __ldg(reinterpret_cast<const float4*>(bcol + (long long)cc * K + k0) + qd);
+template <int RHS>
+__device__ __forceinline__ void cc_load(CcGroup& x, const float* bcol, const float* ag,
+                                        long long K, int lane) {
+  const int cl = lane >> 1;
+  if (lane < 2 * (RHS == 32 ? 16 : RHS))
+    x.b0 = __ldg(reinterpret_cast<const float4*>(bcol + (long long)cl * K) + (lane & 1));
+  if (RHS == 32)
+    x.b1 = __ldg(reinterpret_cast<const float4*>(bcol + (long long)(16 + cl) * K) + (lane & 1));
+  if (lane < 16) x.a = __ldg(reinterpret_cast<const float4*>(ag) + lane);
+}
+
+template <int RHS>
+__device__ __forceinline__ void cc_stage(const CcGroup& x, float* bs, float* as, int lane) {
+  if (lane < 2 * (RHS == 32 ? 16 : RHS)) {
+    float* d = bs + (4 * (lane & 1)) * (RHS + 1) + (lane >> 1);
+    d[0] = x.b0.x;
+    d[RHS + 1] = x.b0.y;
+    d[2 * (RHS + 1)] = x.b0.z;
+    d[3 * (RHS + 1)] = x.b0.w;
   }
-#pragma unroll
-  for (int t = 0; t < x.NA; ++t) {
-    const int i = lane + 32 * t;  // group i / (2H), float4 i % (2H) of it
-    if (i < H * 4 && i / (2 * H) < x.ng)
-      x.a[t] = __ldg(reinterpret_cast<const float4*>(a + (long long)H * k0) + i);
+  if (RHS == 32) {
+    float* d = bs + (4 * (lane & 1)) * (RHS + 1) + 16 + (lane >> 1);
+    d[0] = x.b1.x;
+    d[RHS + 1] = x.b1.y;
+    d[2 * (RHS + 1)] = x.b1.z;
+    d[3 * (RHS + 1)] = x.b1.w;
+  }
+  if (lane < 16) {
+    // device format: row r's 8 values at 8 r, its 16-byte halves exchanged when bit 2 of r is set
+    const int r = lane >> 1, kq = 4 * ((lane & 1) ^ ((r >> 2) & 1));
+    as[(kq + 0) * 8 + r] = x.a.x;
+    as[(kq + 1) * 8 + r] = x.a.y;
+    as[(kq + 2) * 8 + r] = x.a.z;
+    as[(kq + 3) * 8 + r] = x.a.w;
   }
 }
 
-template <int RHS, int H>
-__device__ __forceinline__ void cc_stage(const CcChunk<RHS, H>& x, float* bs, float* as, int lane) {
-#pragma unroll
-  for (int t = 0; t < x.NB; ++t) {
-    const int i = lane + 32 * t, cc = i >> 2, qd = i & 3;
-    if (i < RHS * 4 && qd < 2 * x.ng) {
-      float* d = bs + (4 * qd) * (RHS + 1) + cc;
-      d[0] = x.b[t].x;
-      d[RHS + 1] = x.b[t].y;
-      d[2 * (RHS + 1)] = x.b[t].z;
-      d[3 * (RHS + 1)] = x.b[t].w;
-    }
-  }
-#pragma unroll
-  for (int t = 0; t < x.NA; ++t) {
-    const int i = lane + 32 * t, g = i / (2 * H), rem = i % (2 * H), r = rem >> 1, u = rem & 1;
-    if (i < H * 4 && g < x.ng) {
-      // device format: row r's 8 values at 8 r, its 16-byte halves exchanged when bit 2 of r is set
-      const int kq = 8 * g + 4 * (u ^ ((r >> 2) & 1));
-      as[(kq + 0) * H + r] = x.a[t].x;
-      as[(kq + 1) * H + r] = x.a[t].y;
-      as[(kq + 2) * H + r] = x.a[t].z;
-      as[(kq + 3) * H + r] = x.a[t].w;
-    }
-  }
-}
-
-template <int RHS, int H>
+template <int RHS>
 __device__ void cc_row_cta(const CcParams& q, const CcItem& it, const float* __restrict__ B,
                            long long K, float* smem) {
-  constexpr int L = 32 / RHS;   // lanes per column (row sets)
-  constexpr int RPL = H / L;    // rows per lane
+  constexpr int L = 32 / RHS;  // lanes per column (row sets)
+  constexpr int RPL = 8 / L;   // rows per lane (of the warp's 8)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = int(it.h);
+  const int halves = H / 8, stride = kCcWarps / halves;  // warps per row half = block stride
+  const int half = warp / stride, first = warp % stride;
   float* bs = smem + warp * cc_warp_floats<RHS>();
-  float* as = bs + kCcChunk * (RHS + 1);
+  float* as = bs + 8 * (RHS + 1);
   const int c = lane % RHS, r0 = (lane / RHS) * RPL;
   float acc[RPL];
 #pragma unroll
   for (int r = 0; r < RPL; ++r) acc[r] = 0.0f;
-  // this warp's chunks: blocks b0 + warp, b0 + warp + 8, ...; each in chunks of 16 columns
-  uint32_t b = it.b0 + uint32_t(warp);
+  // this warp's groups: blocks b0 + first + stride j, each w / 8 groups; A of group g of a block at
+  // (block start) + 8 H g floats, the warp's rows 8 half ... 8 half + 7 at + 64 half
+  uint32_t b = it.b0 + uint32_t(first);
   const float* a = q.values + it.a_off;
   for (uint32_t j = it.b0; j < b && j < it.b1; ++j)
     a += (long long)H * int((__ldg(q.blk_desc + j) & 7u) + 1u) * 8;
-  int k0 = 0, w = 0;
+  int g = 0, ngr = 0;
   const float* bcol = B;
   if (b < it.b1) {
     const uint32_t desc = __ldg(q.blk_desc + b);
-    w = int((desc & 7u) + 1u) * 8;
+    ngr = int((desc & 7u) + 1u);
     bcol = B + (long long)(desc & ~7u);
   }
-  CcChunk<RHS, H> cur, nxt;
-  cur.ng = 0;
-  if (b < it.b1) cc_load<RHS, H>(cur, bcol, a, K, 0, w, lane);
+  CcGroup cur, nxt;
+  if (b < it.b1) cc_load<RHS>(cur, bcol, a + 64 * half, K, lane);
   while (b < it.b1) {
-    // the next chunk of this warp: the rest of this block, or its next block
+    // the next group of this warp: the next one of this block, or the first of its next block
     uint32_t nb = b;
-    int nk0 = k0 + kCcChunk, nw = w;
+    int ng = g + 1, nngr = ngr;
     const float* na = a;
     const float* nbcol = bcol;
-    if (nk0 >= w) {
-      na = a + (long long)H * w;
-      for (uint32_t j = b + 1; j < b + kCcWarps && j < it.b1; ++j)
+    if (ng == ngr) {
+      na = a + (long long)H * 8 * ngr;
+      for (uint32_t j = b + 1; j < b + uint32_t(stride) && j < it.b1; ++j)
         na += (long long)H * int((__ldg(q.blk_desc + j) & 7u) + 1u) * 8;
-      nb = b + kCcWarps;
-      nk0 = 0;
+      nb = b + uint32_t(stride);
+      ng = 0;
       if (nb < it.b1) {
         const uint32_t desc = __ldg(q.blk_desc + nb);
-        nw = int((desc & 7u) + 1u) * 8;
+        nngr = int((desc & 7u) + 1u);
         nbcol = B + (long long)(desc & ~7u);
       }
     }
-    if (nb < it.b1) cc_load<RHS, H>(nxt, nbcol, na, K, nk0, nw, lane);
-    cc_stage<RHS, H>(cur, bs, as, lane);
+    if (nb < it.b1)
+      cc_load<RHS>(nxt, nbcol + 8 * ng, na + (long long)H * 8 * ng + 64 * half, K, lane);
+    cc_stage<RHS>(cur, bs, as, lane);
     __syncwarp();
+    float part[RPL];
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      if (g >= cur.ng) break;
-      float part[RPL];
+    for (int r = 0; r < RPL; ++r) part[r] = 0.0f;
 #pragma unroll
-      for (int r = 0; r < RPL; ++r) part[r] = 0.0f;
+    for (int k = 0; k < 8; ++k) {
+      const float bv = bs[k * (RHS + 1) + c];
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int k = 8 * g + kk;
-        const float bv = bs[k * (RHS + 1) + c];
-#pragma unroll
-        for (int r = 0; r < RPL; ++r) part[r] = fmaf(as[k * H + r0 + r], bv, part[r]);
-      }
-#pragma unroll
-      for (int r = 0; r < RPL; ++r) acc[r] += part[r];
+      for (int r = 0; r < RPL; ++r) part[r] = fmaf(as[k * 8 + r0 + r], bv, part[r]);
     }
+#pragma unroll
+    for (int r = 0; r < RPL; ++r) acc[r] += part[r];
     __syncwarp();
     b = nb;
-    k0 = nk0;
-    w = nw;
+    g = ng;
+    ngr = nngr;
     a = na;
     bcol = nbcol;
     cur = nxt;
   }
-  // partial tiles -> shared memory (each warp's own staging area), summed in warp order
+  // partial tiles (8 rows x RHS) -> each warp's staging area; summed per row half in warp order
   float* part = smem + warp * cc_warp_floats<RHS>();
 #pragma unroll
   for (int r = 0; r < RPL; ++r) part[(r0 + r) * RHS + c] = acc[r];
   __syncthreads();
   for (int e = threadIdx.x; e < H * RHS; e += blockDim.x) {
     const int r = e % H, cc = e / H;  // consecutive threads: consecutive rows of one column
+    const int hh = r >> 3;
     float sum = 0.0f;
-#pragma unroll
-    for (int v = 0; v < kCcWarps; ++v) sum += smem[v * cc_warp_floats<RHS>() + r * RHS + cc];
+    for (int v = hh * stride; v < (hh + 1) * stride; ++v)
+      sum += smem[v * cc_warp_floats<RHS>() + (r & 7) * RHS + cc];
     q.C[(long long)cc * q.M + it.c_row + r] = sum;
   }
   __syncthreads();
@@ -946,11 +938,7 @@ __device__ void cc_row_cta(const CcParams& q, const CcItem& it, const float* __r
 template <int RHS>
 __device__ void cc_rows(const CcParams& q, const float* __restrict__ B, long long K, int item,
                         float* smem) {
-  const CcItem it = q.items[item];
-  if (it.h == 8)
-    cc_row_cta<RHS, 8>(q, it, B, K, smem);
-  else
-    cc_row_cta<RHS, 16>(q, it, B, K, smem);
+  cc_row_cta<RHS>(q, q.items[item], B, K, smem);
 }
 
 // Pre-pass: the operand stacks S of all 8-column groups of B (K x rhs, column-major), one tile of
@@ -978,7 +966,7 @@ __host__ __device__ constexpr int bs_groups(int rhs) {
   return rhs <= 32 ? VBSR_BS_GROUPS_NARROW : VBSR_BS_GROUPS;
 }
 template <int RHS, bool RAW>
-__global__ void __launch_bounds__(256) bstack_kernel(const float* __restrict__ B, long long K,
+__global__ void __launch_bounds__(256, 4) bstack_kernel(const float* __restrict__ B, long long K,
                                                      float* __restrict__ out, int stack_blocks,
                                                      const CcParams cc) {
   constexpr int M = stack_m(RHS), half = M / 8, rows = stack_rows(RHS, RAW);
