@@ -161,10 +161,12 @@ enum {
    * asynchronous copies of each column's run of values) instead of from a pre-pass buffer, so an
    * execute is one launch and the plan allocates no stack buffer. */
   VBSR_PLAN_B_DIRECT = 1u << 5,
-  /* RHS <= 32: keep every block row on the tensor cores. By default block rows of height 8 or 16
-   * (unless heavy) are computed in plain fp32 on the CUDA cores by warps of the pre-pass launch,
-   * where they cost far less than a tensor-core pipeline stage per few hundred bytes. */
-  VBSR_PLAN_NO_CUDA_CORE_ROWS = 1u << 6,
+  /* RHS <= 32, results within the same bound: block rows of height 8 or 16 (unless heavy) are
+   * computed in plain fp32 on the CUDA cores by CTAs of the pre-pass launch instead of on the
+   * tensor cores. The tensor-core kernel then gets shorter (headline: 75 -> 54 us), but the
+   * pre-pass launch gets longer by more than that (its latency-bound CUDA-core rows run before the
+   * SpMM), so it is off by default. */
+  VBSR_PLAN_CUDA_CORE_ROWS = 1u << 6,
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
   VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9,   /* consumers wait for the data but compute nothing     */

@@ -384,14 +384,14 @@ def test_cuda_core_rows(cuda, rhs, case):
     host = spec_case(rows, deg, dist, local, seed)
     B = vb.fill_uniform(seed, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
     m = vb.Matrix(host)
-    p = vb.Plan(m, vb.PlanOptions(rhs))
+    p = vb.Plan(m, vb.PlanOptions(rhs), vb.PLAN_CUDA_CORE_ROWS)
     w = p.work_info()
     short = int(np.count_nonzero(host.row_size <= 16))  # every short row here is light
     assert w["cc_rows"] == short
     assert w["cc_rows"] + w["tc_rows"] == host.block_rows
     assert w["cc_values"] + w["tc_values"] == host.values.size
     assert_within_bound(host, B, rhs, run_plan(cuda, host, B, rhs, matrix=m, plan=p))
-    q = vb.Plan(m, vb.PlanOptions(rhs), vb.PLAN_NO_CUDA_CORE_ROWS)
+    q = vb.Plan(m, vb.PlanOptions(rhs))  # default: every row on the tensor cores
     assert q.work_info()["cc_rows"] == 0
     assert_within_bound(host, B, rhs, run_plan(cuda, host, B, rhs, matrix=m, plan=q))
 
@@ -407,7 +407,7 @@ def test_all_rows_on_cuda_cores(cuda, rhs):
     host = _handmade(heights, widths, rows_cols, seed=rhs)
     B = np.random.default_rng(6).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
     m = vb.Matrix(host)
-    p = vb.Plan(m, vb.PlanOptions(rhs))
+    p = vb.Plan(m, vb.PlanOptions(rhs), vb.PLAN_CUDA_CORE_ROWS)
     assert p.work_info()["cc_rows"] == host.block_rows
     assert p.num_tasks() == 0
     got = run_plan(cuda, host, B, rhs, matrix=m, plan=p)

@@ -515,10 +515,11 @@ vbsr_status build_schedule(vbsr_plan* p) {
   std::vector<Unit> units;
   units.reserve(size_t(R));
   int split_rows = 0;
-  // Short rows (h <= 16) for RHS <= 32 go to the CUDA-core path of the pre-pass launch, unless
+  // With VBSR_PLAN_CUDA_CORE_ROWS, short rows (h <= 16, RHS <= 32) go to the CUDA-core path of
+  // the pre-pass launch, unless
   // they are heavy, both wider than 1024 columns and above a quarter of an SM's fair share: those
   // stay here, where the tensor cores' throughput pays (a CUDA-core row is one warp's work).
-  const bool cc_on = row_stacked(rhs) && !(p->flags & VBSR_PLAN_NO_CUDA_CORE_ROWS);
+  const bool cc_on = row_stacked(rhs) && (p->flags & VBSR_PLAN_CUDA_CORE_ROWS) != 0;
   std::vector<CcItem> cc;
   std::vector<double> cc_cost;
   for (int i = 0; i < R; ++i) {
