@@ -627,6 +627,23 @@ def run_gpu_arm(args):
                      "its own rank against the oracle (values regenerated by the oracle library "
                      "slice by slice), |C - C_ref| <= 1e-5 * sum|a||b| per element"}
 
+    upload = None
+    if args.host_upload:
+        # Matrix construction from host values, the path a user with a host matrix takes
+        t_g = time.perf_counter()
+        hv = host.row_slice(r0, r1, values_seed=SEED)
+        gen_s = time.perf_counter() - t_g
+        torch.cuda.synchronize()
+        t_u = time.perf_counter()
+        mu = vb.Matrix(hv, device=local)
+        up_s = time.perf_counter() - t_u
+        upload = {"host_values_bytes": 4 * int(hv.values.size), "host_generate_s": gen_s,
+                  "matrix_create_s": up_s,
+                  "GBps": 4 * hv.values.size / up_s / 1e9,
+                  "how": "vb.Matrix(host rows with values): pinned staging slices, H2D copy and "
+                         "on-device relayout pipelined on private streams"}
+        del mu, hv
+
     headline = None
     cpu = None
     if world == 1:
@@ -693,6 +710,8 @@ def run_gpu_arm(args):
         }
         if replicate:
             line["replicate"] = replicate
+        if upload:
+            line["matrix_upload"] = upload
         if gathered:
             line["gathered_parity"] = gathered
         if headline:
@@ -714,6 +733,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="large")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--host-upload", action="store_true",
+                    help="also time building the rank's Matrix from host values (generated on the "
+                         "host, then uploaded and re-laid-out on the device)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
