@@ -62,15 +62,10 @@ namespace vbsr_b200 {
 // Epilogue warps come last and start at a multiple of 4 (a warp reaches the TMEM lanes
 // 32 (warp % 4) ... only); epilogue set e stores the items j with j % sets == e. Every slot
 // count is a multiple of each role's warp count (kTcRingMultiple).
-#ifndef VBSR_TR_SPLIT_TEAM
-#define VBSR_TR_SPLIT_TEAM 1
-#endif
-// Row-stacked form: a stage is split by a team of kTrSplitTeam warps (1 or 2)
-constexpr int kTrSplitTeam = VBSR_TR_SPLIT_TEAM;
 template <bool TR>
 struct Roles {
-  static constexpr int split = TR ? 4 * kTrSplitTeam : 8;
-  static constexpr int epi_sets = TR ? (kTrSplitTeam == 1 ? 2 : 1) : 1;
+  static constexpr int split = TR ? 4 : 8;
+  static constexpr int epi_sets = TR ? 2 : 1;
   static constexpr int mma0 = split, feeder0 = split + 4, epi0 = split + 8;
   static_assert(epi0 % 4 == 0 && epi0 + 4 * epi_sets == 20, "role layout");
 };
@@ -502,49 +497,6 @@ __device__ __forceinline__ void split_stage_rows(uint32_t sp, int groups, int h,
   }
 }
 
-// AND of `ok` over the two warps of pair barrier `bar_id` (both warps arrive, after bounded waits,
-// so the pair takes the same decision and neither can be left alone at a later pair barrier).
-__device__ __forceinline__ bool pair_all(bool ok, int bar_id) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred q;\n setp.ne.u32 q, %1, 0;\n bar.red.and.pred q, %2, 64, q;\n"
-      " selp.u32 %0, 1, 0, q;\n}\n"
-      : "=r"(r)
-      : "r"(uint32_t(ok)), "r"(bar_id)
-      : "memory");
-  return r != 0;
-}
-
-// split_stage_rows by a team of two warps (member m of pair barrier `bar_id`): each pass covers 32
-// blocks, member m loads and stores blocks u0 + 16 m ... ; both members' loads of a pass complete
-// (named barrier) before either stores, which is what the in-place spread needs.
-__device__ __forceinline__ void split_stage_rows_pair(uint32_t sp, int groups, int h, int lane,
-                                                      int m, int bar_id) {
-  const int units = (h >> 3) * groups;
-  constexpr int kPassUnits = 32;
-  for (int top = units; top > 0; top -= kPassUnits) {
-    const int u0 = top > kPassUnits ? top - kPassUnits : 0;
-    const int ub = u0 + 16 * m;  // this member's first block of the pass
-    float4 x[8];
-#pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const int i = 32 * v + lane;  // float4 i of the member's part: block ub + i / 16
-      if (ub + (i >> 4) < top) x[v] = lds128(sp + 256u * uint32_t(ub) + 16u * uint32_t(i));
-    }
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-#pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const int i = 32 * v + lane, u = ub + (i >> 4);
-      if (u < top) {
-        const uint32_t d = sp + 512u * uint32_t(u) + 16u * uint32_t(i & 15);
-        if (u > 0) sts128(d, x[v]);
-        sts128(d + 256u, lo_part4(x[v]));
-      }
-    }
-    asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory");
-  }
-}
-
 // lo parts of n float4s at shared address sp, written lo_off bytes further.
 __device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, int lane) {
   for (int i0 = 0; i0 < n; i0 += 128) {
@@ -589,16 +541,12 @@ template <bool CHECK, bool TR, bool RAW>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
-  // teams: row-stacked form with kTrSplitTeam == 2 splits each stage with a pair of warps
-  constexpr int kTeam = TR ? kTrSplitTeam : 1;
-  constexpr int kTcSplitWarps = Roles<TR>::split / kTeam;  // teams
-  const int member = w % kTeam;
-  w /= kTeam;
+  constexpr int kTcSplitWarps = Roles<TR>::split;
   const int D = task.stages, SF = task.stage_floats;
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
-  int kk = w;      // this team's next stage
-  int ms = w;      // its slot
+  int kk = w;      // this warp's next stage
+  int ms = w;      // its slot (this warp's slots are w, w + 8, ...)
   uint32_t mph = 0;
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
   bool ok = true;
@@ -616,9 +564,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
         mph ^= 1u;
       }
       VBSR_PROF_T0(t_w);
-      bool got = wait_phase(cb.full0 + 8u * s, par, p, abort_flag, lane);
-      if (kTeam == 2) got = pair_all(got, 1 + w);
-      if (!got) {
+      if (!wait_phase(cb.full0 + 8u * s, par, p, abort_flag, lane)) {
         ok = false;
         break;
       }
@@ -627,10 +573,7 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
       VBSR_PROF_T0(t_s);
       if (math) {
         if (TR) {
-          if (kTeam == 2)
-            split_stage_rows_pair(slots + 4u * uint32_t(s * SF), groups, h, lane, member, 1 + w);
-          else
-            split_stage_rows(slots + 4u * uint32_t(s * SF), groups, h, lane);
+          split_stage_rows(slots + 4u * uint32_t(s * SF), groups, h, lane);
         } else {
           split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
           if (RAW) {  // the stacks' lo rows: the raw rows (T per group) are followed by theirs
@@ -1046,7 +989,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     for (int s = 0; s < task.stages; ++s) {
       // TMA: one arrival + transaction bytes (DIRECT: + one cp.async arrival per feeder lane)
       mbar_init(smem_addr(&bars[0][s]), DIRECT ? 33u : 1u);
-      mbar_init(smem_addr(&bars[1][s]), TR ? uint32_t(kTrSplitTeam) : 1u);  // the split team
+      mbar_init(smem_addr(&bars[1][s]), 1u);  // the split warp
       mbar_init(smem_addr(&bars[2][s]), 1u);  // the MMA warp's tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
