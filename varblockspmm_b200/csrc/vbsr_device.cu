@@ -757,7 +757,7 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   cc.M = kp.M;
   const int cc_blocks = p->cc_count;  // one CTA per short block row
   if (chunks > 0 && !p->direct_b && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
-    const int stack = int(std::min<int64_t>(chunks, 148 * VBSR_BS_BLOCKS_PER_SM));
+    const int stack = int(std::min<int64_t>(chunks, 148 * kBsBlocksPerSm));
     const unsigned blocks = unsigned(stack + cc_blocks);
     switch (kp.rhs) {
       case 8: bstack_kernel<8, false><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc); break;

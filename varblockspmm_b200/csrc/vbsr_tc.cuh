@@ -72,10 +72,7 @@ struct Roles {
 constexpr int kTcMmaWarps = 4;  // MMA-issuing warps
 constexpr int kTcFeeders = 4;   // feeder warps
 constexpr int kTcRingMultiple = 8;
-#ifndef VBSR_PREFETCH
-#define VBSR_PREFETCH 2
-#endif
-constexpr int kPrefetchAhead = VBSR_PREFETCH;  // A is prefetched into L2 this many own stages ahead
+constexpr int kPrefetchAhead = 2;  // A is prefetched into L2 this many own stages ahead
 constexpr int kTcWarps = 20;
 constexpr int kTcThreads = 32 * kTcWarps;
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
@@ -103,14 +100,8 @@ __host__ __device__ constexpr int stack_slot_bytes(int rhs, bool raw) {
 // 32 h G; row-stacked form: per group, 8-row blocks of raw A and of A_lo alternating), then their
 // operand stacks S (stack_tile_bytes each) from byte 64 h G. A stage takes as many consecutive
 // groups of its item as fit, at most kMaxStageGroups: G = stage_groups(h, rhs).
-#ifndef VBSR_SLOT_KB
-#define VBSR_SLOT_KB 26
-#endif
-#ifndef VBSR_MAX_GROUPS
-#define VBSR_MAX_GROUPS 8
-#endif
-constexpr int kSlotBytes = VBSR_SLOT_KB * 1024;
-constexpr int kMaxStageGroups = VBSR_MAX_GROUPS;
+constexpr int kSlotBytes = 26 * 1024;
+constexpr int kMaxStageGroups = 8;
 __host__ __device__ constexpr int slot_floats(int rhs) { return (void)rhs, kSlotBytes / 4; }
 __host__ __device__ constexpr int stage_groups(int h, int rhs, bool raw) {
   return kSlotBytes / (64 * h + stack_slot_bytes(rhs, raw)) < kMaxStageGroups
@@ -121,10 +112,7 @@ __host__ __device__ constexpr int slot_stack_bytes(int h, int groups) { return 6
 // The row-stacked MMA reads M = 64 or 128 rows from a group's first byte, up to 1.5 KB beyond the
 // group's 64 h bytes (rows it does not use); the shared memory allocation ends with this pad.
 constexpr int kSmemTailPad = 2048;
-#ifndef VBSR_TR_M64_MAX_H
-#define VBSR_TR_M64_MAX_H 32
-#endif
-constexpr int kTrM64MaxH = VBSR_TR_M64_MAX_H;  // row-stacked items with h <= this use M = 64
+constexpr int kTrM64MaxH = 32;  // row-stacked items with h <= this use M = 64
 // TMEM: 2 accumulator buffers (items alternate) x 4 partials (one per MMA warp) x 64 columns.
 constexpr int kTmemAlloc = 512;
 
@@ -893,20 +881,11 @@ __device__ void cc_rows(const CcParams& q, const float* __restrict__ B, long lon
 // groups through shared memory: it reads each RHS column's 8 * kBsGroups consecutive values
 // (coalesced), then writes the kBsGroups tiles (contiguous) with 16-byte stores. Blocks from
 // `stack_blocks` on compute the plan's short block rows on the CUDA cores instead (cc_rows).
-#ifndef VBSR_BS_GROUPS
-#define VBSR_BS_GROUPS 16
-#endif
-#ifndef VBSR_BS_BLOCKS_PER_SM
-#define VBSR_BS_BLOCKS_PER_SM 8
-#endif
-#ifndef VBSR_BS_GROUPS_NARROW
-#define VBSR_BS_GROUPS_NARROW 32
-#endif
-// Groups per block iteration: for rhs <= 32 (B in L2 after the first touch at the headline's size,
-// the pre-pass latency-bound) more, so that each thread has more loads in flight; for rhs = 64 (at
-// DRAM bandwidth) 8.
+constexpr int kBsGroupsWide = 16;    // groups per block iteration, rhs = 64 (at DRAM bandwidth)
+constexpr int kBsGroupsNarrow = 32;  // rhs <= 32: more loads in flight per thread (latency-bound)
+constexpr int kBsBlocksPerSm = 8;    // stacking blocks per SM of the pre-pass grid
 __host__ __device__ constexpr int bs_groups(int rhs) {
-  return rhs <= 32 ? VBSR_BS_GROUPS_NARROW : VBSR_BS_GROUPS;
+  return rhs <= 32 ? kBsGroupsNarrow : kBsGroupsWide;
 }
 template <int RHS, bool RAW>
 __global__ void __launch_bounds__(256, 4) bstack_kernel(const float* __restrict__ B, long long K,
