@@ -753,6 +753,7 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   cc.count = p->cc_count;
   cc.values = kp.values;
   cc.blk_desc = p->m->d.d_blk_desc;
+  cc.value_off = p->m->d.d_value_off;
   cc.C = kp.C;
   cc.M = kp.M;
   const int cc_blocks = p->cc_count;  // one CTA per short block row

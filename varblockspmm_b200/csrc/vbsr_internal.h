@@ -61,7 +61,7 @@ static_assert(sizeof(ItemDesc) == 16, "ItemDesc layout");
 struct alignas(16) CcItem {
   uint32_t c_row, h;
   uint32_t b0, b1;  // blocks [b0, b1) of the matrix (their descriptors in d_blk_desc)
-  uint64_t a_off;   // first A value of the row in the device format
+  uint64_t a_off;   // first A value of the row in the device format (blocks: value_off)
   uint64_t pad;
 };
 static_assert(sizeof(CcItem) == 32, "CcItem layout");

@@ -730,6 +730,7 @@ struct CcParams {
   int count;
   const float* values;
   const uint32_t* blk_desc;
+  const int64_t* value_off;  // each block's first value (the device format keeps the offsets)
   float* C;
   long long M;
 };
@@ -803,15 +804,14 @@ __device__ void cc_row_cta(const CcParams& q, const CcItem& it, const float* __r
   // this warp's groups: blocks b0 + first + stride j, each w / 8 groups; A of group g of a block at
   // (block start) + 8 H g floats, the warp's rows 8 half ... 8 half + 7 at + 64 half
   uint32_t b = it.b0 + uint32_t(first);
-  const float* a = q.values + it.a_off;
-  for (uint32_t j = it.b0; j < b && j < it.b1; ++j)
-    a += (long long)H * int((__ldg(q.blk_desc + j) & 7u) + 1u) * 8;
+  const float* a = q.values;
   int g = 0, ngr = 0;
   const float* bcol = B;
   if (b < it.b1) {
     const uint32_t desc = __ldg(q.blk_desc + b);
     ngr = int((desc & 7u) + 1u);
     bcol = B + (long long)(desc & ~7u);
+    a = q.values + __ldg(q.value_off + b);
   }
   CcGroup cur, nxt;
   if (b < it.b1) cc_load<RHS>(cur, bcol, a + 64 * half, K, lane);
@@ -822,15 +822,13 @@ __device__ void cc_row_cta(const CcParams& q, const CcItem& it, const float* __r
     const float* na = a;
     const float* nbcol = bcol;
     if (ng == ngr) {
-      na = a + (long long)H * 8 * ngr;
-      for (uint32_t j = b + 1; j < b + uint32_t(stride) && j < it.b1; ++j)
-        na += (long long)H * int((__ldg(q.blk_desc + j) & 7u) + 1u) * 8;
       nb = b + uint32_t(stride);
       ng = 0;
       if (nb < it.b1) {
         const uint32_t desc = __ldg(q.blk_desc + nb);
         nngr = int((desc & 7u) + 1u);
         nbcol = B + (long long)(desc & ~7u);
+        na = q.values + __ldg(q.value_off + nb);
       }
     }
     if (nb < it.b1)
