@@ -228,10 +228,8 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   uint32_t filled = 0, lastpar = 0;
   const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
   // The SpMM is launched as a programmatic dependent of the B pre-pass, so that its prologue
-  // overlaps the pre-pass; the feeders are the only warps that read the pre-pass output, and they
-  // wait for it (griddepcontrol.wait) only before their first stack copy: the A copies of their
-  // first stages, which do not depend on the pre-pass, are already in flight by then.
-  bool waited = DIRECT;
+  // overlaps the pre-pass; the feeders are the only warps that read the pre-pass output.
+  if (!DIRECT) griddep_wait();
   VBSR_PROF_T0(t_all);
   for (int kk = f; kk < nst; kk += kTcFeeders) {
     const Stage st = win.get();
@@ -295,10 +293,6 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
       if (H != h && lane < groups)
         bulk_g2s(sp + uint32_t(32 * h * lane), a_src + 8ll * H * lane, uint32_t(32 * h), full_bar,
                  pol_a);
-      if (!waited) {
-        griddep_wait();
-        waited = true;
-      }
       if (DIRECT) {
         // runs in order; run r: groups [r, end_r), first scalar column col_r
         const uint32_t s0 = sp + uint32_t(slot_stack_bytes(h, groups));
