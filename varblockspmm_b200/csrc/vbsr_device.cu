@@ -438,9 +438,8 @@ struct vbsr_plan {
 
 namespace {
 
-constexpr int kSmemBudget = 224 * 1024;
-constexpr int kCcMaxH = 16;        // block rows this short (RHS <= 32) run on the CUDA cores
-constexpr int kCcWarpsPerSm = 16;  // CUDA-core row warps of the pre-pass launch per SM  // stage bytes per CTA (dynamic allocation adds 1 KB)
+constexpr int kSmemBudget = 224 * 1024;  // stage bytes per CTA (dynamic allocation adds 1 KB)
+constexpr int kCcMaxH = 16;  // block rows this short (RHS <= 32) may run on the CUDA cores
 
 // Per-team time model of one item: the bytes its stages move (A and B) plus a fixed cost per stage
 // and per item, in bytes-equivalent units.
