@@ -88,6 +88,14 @@ struct GeneratorOptions {
 /** Generates a validated matrix; equal options give equal matrices. */
 HostMatrix generate(const GeneratorOptions&);
 
+/** Real matrices (no reference counterpart): a scalar CSR matrix as VBSR for a block partition
+ * (vbsr_host_matrix_from_csr), and the binary VBSR file (vbsr_host_matrix_save / _load). */
+HostMatrix from_csr(int64_t rows, int64_t cols, const std::vector<int64_t>& row_ptr,
+                    const std::vector<int64_t>& col_idx, const std::vector<float>& values,
+                    const std::vector<int32_t>& row_sizes, const std::vector<int32_t>& col_sizes);
+void save_matrix(const HostMatrix&, const char* path);
+HostMatrix load_matrix(const char* path);
+
 /** C = A*B on the CPU with double accumulation per block (the oracle; see header comment). */
 std::vector<float> cpu_reference(const HostMatrix&, const std::vector<float>& B, int rhs);
 

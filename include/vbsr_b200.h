@@ -307,6 +307,23 @@ vbsr_status vbsr_generate(const vbsr_generator_options* opts, vbsr_host_matrix**
 vbsr_status vbsr_host_matrix_view_get(const vbsr_host_matrix* h, vbsr_host_matrix_view* out);
 vbsr_status vbsr_host_matrix_free(vbsr_host_matrix* h);
 
+/* ---- Real matrices: CSR conversion and the on-disk format -------------------------------- */
+
+/* No reference counterpart: the reference has no loader or file format. Converts a scalar CSR
+ * matrix (rows x cols; row_ptr has rows + 1 entries, col_idx / values row_ptr[rows]) into the VBSR
+ * host format for the given block partition (row_sizes sum to rows, col_sizes to cols; every size
+ * a multiple of 8 in [8, 64]): every block containing a nonzero becomes a dense block, zeros
+ * elsewhere, duplicates summed. */
+vbsr_status vbsr_host_matrix_from_csr(int64_t rows, int64_t cols, const int64_t* row_ptr,
+                                      const int64_t* col_idx, const float* values,
+                                      int32_t block_rows, const int32_t* row_sizes,
+                                      int32_t block_cols, const int32_t* col_sizes,
+                                      vbsr_host_matrix** out);
+/* Binary VBSR file (magic "VBSRMAT1", then the HostMatrix arrays; layout in vbsr_io.cpp). Save
+ * validates the matrix first; load validates what it read. */
+vbsr_status vbsr_host_matrix_save(const vbsr_host_matrix_view* host, const char* path);
+vbsr_status vbsr_host_matrix_load(const char* path, vbsr_host_matrix** out);
+
 /* Counter-based U[-1,1) generator: out[i] = f(seed, stream, first + i). Used for PROFILE_SPEC
  * values (stream VBSR_STREAM_VALUES) and dense panels (VBSR_STREAM_DENSE). Host version; the
  * device version below gives bit-identical floats. */

@@ -162,7 +162,7 @@ static int run_parallel(job_t* base, int threads, double* max_ratio, double* max
 
 static int setup(job_t* j, const vbsr_host_matrix_view* v, const float* B, int rhs, int32_t r0,
                  int32_t r1) {
-  if (!v || !B || !v->values || r0 < 0 || r1 > v->block_rows || r0 > r1) return -1;
+  if (!v || !B || (!v->values && v->values_len) || r0 < 0 || r1 > v->block_rows || r0 > r1) return -1;
   if (rhs != 8 && rhs != 16 && rhs != 32 && rhs != 64) return -1;
   memset(j, 0, sizeof *j);
   j->v = v;

@@ -13,6 +13,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <string>
 #include <functional>
 #include <random>
 #include <stdexcept>
@@ -194,9 +195,46 @@ void ownership_and_streams() {
   cudaStreamDestroy(s1);
 }
 
+// A small scalar CSR matrix through from_csr, the VBSR file and back, then Plan::execute.
+void csr_and_file(const char* dir) {
+  const int64_t rows = 48, cols = 40;
+  std::vector<int64_t> row_ptr{0}, col_idx;
+  std::vector<float> vals;
+  std::mt19937 eng{3};
+  std::uniform_real_distribution<float> u(-1.0f, 1.0f);
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t c = 0; c < cols; ++c)
+      if ((r * 7 + c * 3) % 11 == 0) {
+        col_idx.push_back(c);
+        vals.push_back(u(eng));
+      }
+    row_ptr.push_back(int64_t(col_idx.size()));
+  }
+  const vbsr::HostMatrix a = vbsr::from_csr(rows, cols, row_ptr, col_idx, vals, {16, 32}, {8, 32});
+  const std::string path = std::string(dir) + "/dropin_test.vbsr";
+  vbsr::save_matrix(a, path.c_str());
+  const vbsr::HostMatrix b = vbsr::load_matrix(path.c_str());
+  std::remove(path.c_str());
+  if (b.values != a.values || b.block_col != a.block_col || b.value_off != a.value_off)
+    throw std::runtime_error("VBSR file round trip changed the matrix");
+  const int rhs = 16;
+  const std::vector<float> B = dense_input(cols * rhs, 4);
+  vbsr::Matrix m(b);
+  vbsr::Plan plan(m, {rhs, vbsr::Kernel::Auto});
+  DeviceBuffer dB(B.size()), dC(size_t(rows) * rhs);
+  dB.upload(B);
+  cudaStream_t s;
+  cuda(cudaStreamCreate(&s), "stream");
+  run_and_check([&](cudaStream_t st) { plan.execute(dB.p, dC.p, st); }, s, dC,
+                vbsr::cpu_reference(b, B, rhs), "from_csr + file + Plan");
+  cudaStreamDestroy(s);
+  expect_invalid([&] { vbsr::load_matrix((std::string(dir) + "/missing.vbsr").c_str()); },
+                 "missing VBSR file");
+}
+
 }  // namespace
 
-int main() {
+int main(int argc, char** argv) {
   try {
     negative_cases();
     const vbsr::Distribution dists[] = {vbsr::Distribution::Uniform,
@@ -211,6 +249,7 @@ int main() {
           ++seed;
         }
     ownership_and_streams();
+    csr_and_file(argc > 1 ? argv[1] : ".");
     std::printf("PASS: %d checks (64 parameter cases x 6 paths on non-default streams, negative "
                 "cases, moved Matrix, one plan on two streams)\n", checks);
     return 0;

@@ -1,6 +1,7 @@
 """The C++ drop-in API, compiled and run as a program (tests/cxx/test_dropin.cpp): the reference's
 own test binary (tests/test_main.cpp:14-177) rewritten against include/varblockspmm/vbsr.hpp, with
-the engine's libvbsr_b200_cxx.so and the oracle's cpu_reference. The build is checked on any
+the engine's libvbsr_b200_cxx.so and the oracle's cpu_reference, plus a scalar CSR matrix
+through from_csr and the VBSR file. The build is checked on any
 machine; running it needs the GPU."""
 import os
 import subprocess
@@ -34,6 +35,6 @@ def test_cxx_dropin_program_builds(tmp_path):
 @pytest.mark.gpu
 def test_cxx_dropin_program_runs(cuda, tmp_path):
     exe = _build(tmp_path)
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=600)
+    r = subprocess.run([exe, str(tmp_path)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "PASS" in r.stdout

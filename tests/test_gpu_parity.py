@@ -414,3 +414,24 @@ def test_all_rows_on_cuda_cores(cuda, rhs):
     assert_within_bound(host, B, rhs, got)
     C = got.reshape(rhs, host.scalar_rows())
     assert np.all(C[:, host.row_scalar_off[100]:] == 0)
+
+
+@pytest.mark.parametrize("rhs", [8, 32, 64])
+def test_matrix_market_through_the_engine(cuda, rhs, tmp_path):
+    """A scalar sparse matrix from a Matrix Market file, cut into 32 x 24 blocks (padded to
+    multiples of 8), saved to and reloaded from a VBSR file, multiplied on the GPU: C meets the
+    bound against the oracle, and its top-left block is the dense product of the file's matrix."""
+    import scipy.io
+    import scipy.sparse as sp
+    a = sp.random(1003, 870, density=0.01, random_state=rhs, format="coo", dtype=np.float32)
+    mtx = str(tmp_path / "a.mtx")
+    scipy.io.mmwrite(mtx, a)
+    m0, (rows, cols) = vb.load_matrix_market(mtx, row_block=32, col_block=24)
+    m0.save(str(tmp_path / "a.vbsr"))
+    host = vb.load_matrix(str(tmp_path / "a.vbsr"))
+    B = np.random.default_rng(rhs).uniform(-1, 1, host.scalar_cols() * rhs).astype(np.float32)
+    got = run_plan(cuda, host, B, rhs)
+    assert_within_bound(host, B, rhs, got)
+    Cm = got.reshape(rhs, host.scalar_rows()).T[:rows]
+    ref = a.toarray().astype(np.float64) @ B.reshape(rhs, host.scalar_cols()).T[:cols]
+    assert np.allclose(Cm, ref, rtol=0, atol=1e-4)

@@ -159,6 +159,10 @@ _sig = {
     "vbsr_fill_uniform": [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, _pf, C.c_int],
     "vbsr_fill_uniform_device": [C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, _vp, _vp],
     "vbsr_fill_mt19937": [C.c_uint32, C.c_uint64, _pf],
+    "vbsr_host_matrix_from_csr": [C.c_int64, C.c_int64, _vp, _vp, _vp, C.c_int32, _vp, C.c_int32,
+                                  _vp, C.POINTER(_vp)],
+    "vbsr_host_matrix_save": [C.POINTER(HostView), C.c_char_p],
+    "vbsr_host_matrix_load": [C.c_char_p, C.POINTER(_vp)],
     "vbsr_partition_rows": [C.POINTER(HostView), C.c_int, C.c_int, _p32],
     "vbsr_compulsory_bytes": [C.POINTER(HostView), C.c_int32, C.c_int32, C.c_int,
                               C.POINTER(C.c_double), C.POINTER(C.c_double)],
@@ -267,6 +271,11 @@ class HostMatrix:
         v.values_len = self.values.size
         return v
 
+    def save(self, path: str) -> None:
+        """Writes the matrix to a binary VBSR file (see vbsr_host_matrix_save)."""
+        v = self.view()
+        _check(_lib.vbsr_host_matrix_save(C.byref(v), os.fsencode(path)))
+
     def validate(self):
         """HostMatrix::validate (reference src/format/vbsr.cpp:29-82)."""
         v = self.view()
@@ -317,6 +326,11 @@ def generate(opts: GeneratorOptions, with_values: bool = True, threads: int = 0)
                 int(opts.profile), int(bool(with_values)), int(threads))
     h = _vp()
     _check(_lib.vbsr_generate(C.byref(o), C.byref(h)))
+    return _take_host(h)
+
+
+def _take_host(h) -> "HostMatrix":
+    """Copies a library-owned host matrix into a HostMatrix and frees it."""
     try:
         v = HostView()
         _check(_lib.vbsr_host_matrix_view_get(h, C.byref(v)))
@@ -338,6 +352,56 @@ def generate(opts: GeneratorOptions, with_values: bool = True, threads: int = 0)
     finally:
         _lib.vbsr_host_matrix_free(h)
     return m
+
+
+def load_matrix(path: str) -> HostMatrix:
+    """Reads a binary VBSR file written by HostMatrix.save (validated on load)."""
+    h = _vp()
+    _check(_lib.vbsr_host_matrix_load(os.fsencode(path), C.byref(h)))
+    return _take_host(h)
+
+
+def block_sizes(n: int, size: int = 32) -> np.ndarray:
+    """A block partition of n scalars (n a multiple of 8): blocks of `size` (a multiple of 8 in
+    [8, 64]) and a last block of the remainder."""
+    if n <= 0 or n % 8 or size % 8 or not 8 <= size <= 64:
+        raise InvalidArgument("n must be a positive multiple of 8, size a multiple of 8 in [8, 64]")
+    sizes = [size] * (n // size)
+    if n % size:
+        sizes.append(n % size)
+    return np.asarray(sizes, dtype=np.int32)
+
+
+def from_csr(shape, indptr, indices, data, row_sizes, col_sizes) -> HostMatrix:
+    """A scalar CSR matrix as a VBSR host matrix for the given block partition (every block that
+    holds a nonzero becomes a dense block; see vbsr_host_matrix_from_csr)."""
+    rows, cols = int(shape[0]), int(shape[1])
+    ip = np.ascontiguousarray(indptr, dtype=np.int64)
+    ix = np.ascontiguousarray(indices, dtype=np.int64)
+    dv = np.ascontiguousarray(data, dtype=np.float32)
+    rs = np.ascontiguousarray(row_sizes, dtype=np.int32)
+    cs = np.ascontiguousarray(col_sizes, dtype=np.int32)
+    h = _vp()
+    _check(_lib.vbsr_host_matrix_from_csr(rows, cols, ip.ctypes.data, ix.ctypes.data,
+                                          dv.ctypes.data, rs.size, rs.ctypes.data, cs.size,
+                                          cs.ctypes.data, C.byref(h)))
+    return _take_host(h)
+
+
+def load_matrix_market(path: str, row_block: int = 32, col_block: int = 32):
+    """Reads a Matrix Market file (scipy.io.mmread) into a VBSR host matrix: the scalar dimensions
+    are padded with zero rows / columns up to multiples of 8, then cut into blocks of row_block x
+    col_block (a smaller last block). Returns (HostMatrix, (rows, cols) of the file)."""
+    import scipy.io
+    import scipy.sparse
+    a = scipy.sparse.csr_matrix(scipy.io.mmread(path), dtype=np.float32)
+    a.sum_duplicates()
+    rows, cols = a.shape
+    pr, pc = -(-rows // 8) * 8, -(-cols // 8) * 8
+    indptr = np.concatenate([a.indptr, np.full(pr - rows, a.indptr[-1], dtype=a.indptr.dtype)])
+    m = from_csr((pr, pc), indptr, a.indices, a.data, block_sizes(pr, row_block),
+                 block_sizes(pc, col_block))
+    return m, (rows, cols)
 
 
 def fill_uniform(seed: int, stream: int, first: int, count: int, threads: int = 0) -> np.ndarray:
@@ -665,6 +729,7 @@ __all__ = [
     "HostMatrix", "DeviceMatrix", "Matrix", "Distribution", "Profile", "GeneratorOptions",
     "generate", "Kernel", "PlanOptions", "Plan", "launch_row_owned", "launch_row_owned_scalar",
     "partition_rows", "compulsory_bytes", "fill_uniform", "fill_uniform_device", "fill_mt19937",
+    "from_csr", "load_matrix_market", "load_matrix", "block_sizes",
     "InvalidArgument", "CudaError", "VbsrError", "TimeoutError_", "BoundsViolation", "last_error",
     "STREAM_VALUES", "STREAM_DENSE", "PLAN_BOUNDS_CHECK", "PLAN_NO_SPLIT", "LIB_PATH",
 ]

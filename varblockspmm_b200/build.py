@@ -25,7 +25,7 @@ COMMON = [*os.environ.get("VBSR_EXTRA_FLAGS", "").split(),
           "-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall",
           "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 
-SOURCES = ["vbsr_host.cpp", "vbsr_device.cu", "vbsr_multi.cpp"]
+SOURCES = ["vbsr_host.cpp", "vbsr_device.cu", "vbsr_multi.cpp", "vbsr_io.cpp"]
 
 
 def _run(cmd):

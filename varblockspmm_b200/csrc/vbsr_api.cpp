@@ -17,6 +17,25 @@ void check(vbsr_status s) {
   throw std::runtime_error(msg);
 }
 
+// Copies a library-owned host matrix into a HostMatrix and frees it.
+HostMatrix take(vbsr_host_matrix* h) {
+  vbsr_host_matrix_view v{};
+  vbsr_host_matrix_view_get(h, &v);
+  HostMatrix m;
+  m.block_rows = v.block_rows;
+  m.block_cols = v.block_cols;
+  m.row_ptr.assign(v.row_ptr, v.row_ptr + v.row_ptr_len);
+  m.block_col.assign(v.block_col, v.block_col + v.block_col_len);
+  m.row_size.assign(v.row_size, v.row_size + v.row_size_len);
+  m.col_size.assign(v.col_size, v.col_size + v.col_size_len);
+  m.row_scalar_off.assign(v.row_scalar_off, v.row_scalar_off + v.row_scalar_off_len);
+  m.col_scalar_off.assign(v.col_scalar_off, v.col_scalar_off + v.col_scalar_off_len);
+  m.value_off.assign(v.value_off, v.value_off + v.value_off_len);
+  if (v.values_len) m.values.assign(v.values, v.values + v.values_len);
+  vbsr_host_matrix_free(h);
+  return m;
+}
+
 vbsr_device_matrix to_c(const DeviceMatrix& a) {
   vbsr_device_matrix v{};
   v.block_rows = a.block_rows;
@@ -93,21 +112,31 @@ HostMatrix generate(const GeneratorOptions& o) {
   c.threads = 0;
   vbsr_host_matrix* h = nullptr;
   check(vbsr_generate(&c, &h));
-  vbsr_host_matrix_view v{};
-  vbsr_host_matrix_view_get(h, &v);
-  HostMatrix m;
-  m.block_rows = v.block_rows;
-  m.block_cols = v.block_cols;
-  m.row_ptr.assign(v.row_ptr, v.row_ptr + v.row_ptr_len);
-  m.block_col.assign(v.block_col, v.block_col + v.block_col_len);
-  m.row_size.assign(v.row_size, v.row_size + v.row_size_len);
-  m.col_size.assign(v.col_size, v.col_size + v.col_size_len);
-  m.row_scalar_off.assign(v.row_scalar_off, v.row_scalar_off + v.row_scalar_off_len);
-  m.col_scalar_off.assign(v.col_scalar_off, v.col_scalar_off + v.col_scalar_off_len);
-  m.value_off.assign(v.value_off, v.value_off + v.value_off_len);
-  m.values.assign(v.values, v.values + v.values_len);
-  vbsr_host_matrix_free(h);
-  return m;
+  return take(h);
+}
+
+HostMatrix from_csr(int64_t rows, int64_t cols, const std::vector<int64_t>& row_ptr,
+                    const std::vector<int64_t>& col_idx, const std::vector<float>& values,
+                    const std::vector<int32_t>& row_sizes, const std::vector<int32_t>& col_sizes) {
+  if (row_ptr.size() != size_t(rows) + 1 || col_idx.size() != values.size() ||
+      col_idx.size() != size_t(row_ptr.back()))
+    throw std::invalid_argument("CSR arrays do not match the dimensions");
+  vbsr_host_matrix* h = nullptr;
+  check(vbsr_host_matrix_from_csr(rows, cols, row_ptr.data(), col_idx.data(), values.data(),
+                                  int32_t(row_sizes.size()), row_sizes.data(),
+                                  int32_t(col_sizes.size()), col_sizes.data(), &h));
+  return take(h);
+}
+
+void save_matrix(const HostMatrix& m, const char* path) {
+  const vbsr_host_matrix_view v = detail::view_of(m);
+  check(vbsr_host_matrix_save(&v, path));
+}
+
+HostMatrix load_matrix(const char* path) {
+  vbsr_host_matrix* h = nullptr;
+  check(vbsr_host_matrix_load(path, &h));
+  return take(h);
 }
 
 Plan::Plan(const Matrix& matrix, PlanOptions options) : options_(options) {
