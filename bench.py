@@ -77,7 +77,9 @@ def traffic_from_profiles(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+    """nvidia-smi clock/throttle samples every 20 ms while the timed region runs (the multi-GPU
+    steps are a few ms each, so a 200 ms period could miss a short region). Entering waits for the
+    sampler's first line, so the samples that count start before the timed work."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -92,12 +94,16 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.QUERY,
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t = time.time()
+            while not self.lines and time.time() - t < 3.0:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
+        self.first = len(self.lines)
         return self
 
     def _read(self):
@@ -115,7 +121,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[max(0, getattr(self, "first", 1) - 1):]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
