@@ -69,6 +69,10 @@ struct Roles {
   static constexpr int mma0 = split, feeder0 = split + 4, epi0 = split + 8;
   static_assert(epi0 % 4 == 0 && epi0 + 4 * epi_sets == 20, "role layout");
 };
+#ifndef VBSR_CS_SPLIT_TEAM
+#define VBSR_CS_SPLIT_TEAM 2
+#endif
+constexpr int kCsSplitTeam = VBSR_CS_SPLIT_TEAM;  // column-stacked form: warps per stage split
 constexpr int kTcMmaWarps = 4;  // MMA-issuing warps
 constexpr int kTcFeeders = 4;   // feeder warps
 constexpr int kTcRingMultiple = 8;
@@ -485,9 +489,11 @@ __device__ __forceinline__ void split_stage_rows(uint32_t sp, int groups, int h,
   }
 }
 
-// lo parts of n float4s at shared address sp, written lo_off bytes further.
-__device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, int lane) {
-  for (int i0 = 0; i0 < n; i0 += 128) {
+// lo parts of n float4s at shared address sp, written lo_off bytes further (the chunks of 128
+// float4s with index % parts == part).
+__device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, int lane,
+                                           int part = 0, int parts = 1) {
+  for (int i0 = 128 * part; i0 < n; i0 += 128 * parts) {
     float4 x[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -505,10 +511,11 @@ __device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, 
 // Column-stacked form: A_lo of a whole stage at shared address sp: the stage's A (2h float4s per
 // group, groups one after another) at sp, its A_lo at the same offsets 32 h G bytes further. Eight
 // loads per lane are in flight before their stores.
-__device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane) {
+__device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane,
+                                            int part = 0, int parts = 1) {
   const int n = 2 * h * groups;  // float4s
   const uint32_t lo = uint32_t(32 * h * groups);
-  for (int i0 = 0; i0 < n; i0 += 256) {
+  for (int i0 = 256 * part; i0 < n; i0 += 256 * parts) {
     float4 x[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -529,12 +536,18 @@ template <bool CHECK, bool TR, bool RAW>
 __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t slots,
                               const CtaBars& cb, uint32_t tmem_base, int w, int lane,
                               volatile int* abort_flag) {
-  constexpr int kTcSplitWarps = Roles<TR>::split;
+  // Column-stacked form: a stage is split by a team of kCsSplitTeam warps, each taking every
+  // kCsSplitTeam-th chunk of the A and B_lo work (no chunk is read by another member, so the
+  // members need no barrier between them; each arrives on the slot's split barrier).
+  constexpr int kTeam = TR ? 1 : kCsSplitTeam;
+  constexpr int kTcSplitWarps = Roles<TR>::split / kTeam;  // teams
+  const int member = w % kTeam;
+  w /= kTeam;
   const int D = task.stages, SF = task.stage_floats;
   ItemWin iw;
   iw.init(p.items + task.item_off, task.item_end - task.item_off, lane);
-  int kk = w;      // this warp's next stage
-  int ms = w;      // its slot (this warp's slots are w, w + 8, ...)
+  int kk = w;      // this team's next stage
+  int ms = w;      // its slot
   uint32_t mph = 0;
   const bool math = !(p.diag & VBSR_PLAN_DIAG_SKIP_MATH);
   bool ok = true;
@@ -563,11 +576,11 @@ __device__ void tc_split_warp(const KernelParams& p, const Task& task, uint32_t 
         if (TR) {
           split_stage_rows(slots + 4u * uint32_t(s * SF), groups, h, lane);
         } else {
-          split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane);
+          split_stage(slots + 4u * uint32_t(s * SF), groups, h, lane, member, kTeam);
           if (RAW) {  // the stacks' lo rows: the raw rows (T per group) are followed by theirs
             const int T = stack_tile_bytes(p.rhs, RAW);
             split_flat(slots + 4u * uint32_t(s * SF) + uint32_t(slot_stack_bytes(h, groups)),
-                       T * groups / 16, uint32_t(T * groups), lane);
+                       T * groups / 16, uint32_t(T * groups), lane, member, kTeam);
           }
         }
         VBSR_TRACE_ST(kk, 6);
@@ -966,7 +979,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     for (int s = 0; s < task.stages; ++s) {
       // TMA: one arrival + transaction bytes (DIRECT: + one cp.async arrival per feeder lane)
       mbar_init(smem_addr(&bars[0][s]), DIRECT ? 33u : 1u);
-      mbar_init(smem_addr(&bars[1][s]), 1u);  // the split warp
+      mbar_init(smem_addr(&bars[1][s]), TR ? 1u : uint32_t(kCsSplitTeam));  // the split team
       mbar_init(smem_addr(&bars[2][s]), 1u);  // the MMA warp's tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
