@@ -167,6 +167,13 @@ enum {
    * pre-pass launch gets longer by more than that (its latency-bound CUDA-core rows run before the
    * SpMM), so it is off by default. */
   VBSR_PLAN_CUDA_CORE_ROWS = 1u << 6,
+  /* Results identical: B's operand stacks are formed by the SpMM's own CTAs before their
+   * pipelines start (a grid-wide arrival count in device memory, bounded waits), so an execute is
+   * one launch instead of the pre-pass launch plus the SpMM. Off by default: it is slower (headline
+   * 92 against 85 us, large config 15.8 against 14.5 ms), because the SpMM's pipelines cannot start
+   * before every CTA's share of the stacks is done, while the separate pre-pass already overlaps
+   * the SpMM's prologue (programmatic dependent launch). */
+  VBSR_PLAN_FUSED_PREPASS = 1u << 7,
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
   VBSR_PLAN_DIAG_SKIP_MATH = 1u << 9,   /* consumers wait for the data but compute nothing     */

@@ -131,6 +131,29 @@ def test_rhs64_stack_layouts(cuda, stacks, case):
     assert np.array_equal(got.view(np.uint32), chk.view(np.uint32))
 
 
+FUSED_FORMS = [(8, 0), (16, 0), (32, 0), (64, vb.PLAN_STACKS_RAW), (64, vb.PLAN_STACKS_PRESPLIT),
+               (32, vb.PLAN_CUDA_CORE_ROWS), (64, vb.PLAN_STACKS_RAW | vb.PLAN_BOUNDS_CHECK)]
+
+
+@pytest.mark.parametrize("form", FUSED_FORMS, ids=lambda f: "r%d_%x" % f)
+def test_fused_prepass(cuda, form):
+    """VBSR_PLAN_FUSED_PREPASS: the SpMM's CTAs form the operand stacks themselves (one launch
+    unless short rows run on the CUDA cores). C is bit-identical to the two-launch execute, also
+    over repeated executes with changing B (the grid arrival word resets itself each launch)."""
+    rhs, flags = form
+    host = spec_case(700, 8, 3, False, 21)
+    m = vb.Matrix(host)
+    sep = vb.Plan(m, vb.PlanOptions(rhs), flags)
+    fused = vb.Plan(m, vb.PlanOptions(rhs), flags | vb.PLAN_FUSED_PREPASS)
+    assert fused.launch_count() == (2 if flags & vb.PLAN_CUDA_CORE_ROWS else 1)
+    for it in range(3):
+        B = vb.fill_uniform(21 + it, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
+        a = run_plan(cuda, host, B, rhs, matrix=m, plan=sep)
+        b = run_plan(cuda, host, B, rhs, matrix=m, plan=fused)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert_within_bound(host, B, rhs, b)
+
+
 def _handmade(heights, widths, rows_cols, seed=0):
     """A matrix from explicit per-row block column lists (possibly empty rows)."""
     rng = np.random.default_rng(seed)

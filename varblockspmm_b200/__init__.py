@@ -191,6 +191,7 @@ PLAN_STACKS_RAW = 8        # RHS 64: force raw-B operand stacks (same results)
 PLAN_STACKS_PRESPLIT = 16  # RHS 64: force pre-split operand stacks (same results)
 PLAN_B_DIRECT = 32         # RHS 64: raw-B stack rows read straight from B, no pre-pass
 PLAN_CUDA_CORE_ROWS = 64  # RHS <= 32: short block rows on the CUDA cores in the pre-pass launch
+PLAN_FUSED_PREPASS = 128  # B stacks formed by the SpMM's CTAs (one launch; slower, off by default)
 PLAN_DIAG_SKIP_COPIES = 1 << 8  # diagnostics only: C is wrong
 PLAN_DIAG_SKIP_MATH = 1 << 9    # diagnostics only: C is wrong
 PLAN_DIAG_SKIP_PREPASS = 1 << 10  # timing only: reuses the previous execute's B stacks

@@ -413,6 +413,8 @@ struct vbsr_plan {
   float* d_bstack = nullptr;     // B's operand stacks, rewritten by every execute
   bool raw_b = false;            // column-stacked form: raw-B stacks (see stack_rows)
   bool direct_b = false;         // ... read from B by the SpMM itself: no pre-pass, no d_bstack
+  bool fused_stack = false;      // the SpMM's CTAs form the stacks (no separate pre-pass launch)
+  uint32_t* d_stack_flag = nullptr;  // their grid arrival word (stack_arrive)
   int64_t bstack_floats = 0;
   Task* d_tasks = nullptr;
   CcItem* d_cc = nullptr;          // short block rows computed on the CUDA cores (pre-pass launch)
@@ -487,6 +489,7 @@ vbsr_status build_schedule(vbsr_plan* p) {
                                                                        : big);
   // Raw-B stacks read straight from B by the SpMM (no pre-pass)
   p->direct_b = p->raw_b && (p->flags & VBSR_PLAN_B_DIRECT) != 0;
+  p->fused_stack = !p->direct_b && (p->flags & VBSR_PLAN_FUSED_PREPASS) != 0;
   const int R = d.block_rows;
   // Work units: one per block row, or, for a block row whose cost exceeds a CTA's fair share, one
   // per row part. A row part is rows [r0, r0 + hp) of the block row (multiples of 8) over all its
@@ -718,6 +721,8 @@ vbsr_status build_schedule(vbsr_plan* p) {
     VBSR_CUDA(cudaMemcpyAsync(p->d_tasks, h_tasks.data(), h_tasks.size() * sizeof(Task),
                               cudaMemcpyHostToDevice, ss.s));
   VBSR_CUDA(cudaMemsetAsync(p->d_status, 0, kStatusWords * sizeof(int), ss.s));
+  VBSR_CUDA(cudaMalloc(&p->d_stack_flag, sizeof(uint32_t)));
+  VBSR_CUDA(cudaMemsetAsync(p->d_stack_flag, 0, sizeof(uint32_t), ss.s));
   if (!cc.empty()) {
     VBSR_CUDA(cudaMalloc(&p->d_cc, cc.size() * sizeof(CcItem)));
     VBSR_CUDA(cudaMemcpyAsync(p->d_cc, cc.data(), cc.size() * sizeof(CcItem),
@@ -737,13 +742,16 @@ void free_plan(vbsr_plan* p) {
   cudaFree(p->d_bstack);
   cudaFree(p->d_tasks);
   cudaFree(p->d_status);
+  cudaFree(p->d_stack_flag);
   cudaFree(p->d_timing);
   cudaFree(p->d_cc);
   if (p->done != nullptr) cudaEventDestroy(p->done);
   delete p;
 }
 
-// One execute: the B pre-pass, then the SpMM kernel, both on `stream`.
+// One execute on `stream`: the B pre-pass launch and then the SpMM, or only the SpMM kernel, which
+// then forms B's operand stacks itself (VBSR_PLAN_FUSED_PREPASS). The short block rows on the CUDA cores
+// (VBSR_PLAN_CUDA_CORE_ROWS) are CTAs of a pre-pass launch either way.
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
   const int64_t bsg = bs_groups(kp.rhs);
   const int64_t chunks = (kp.K / 8 + bsg - 1) / bsg;  // bs_groups(rhs) groups per block iteration
@@ -756,8 +764,11 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   cc.C = kp.C;
   cc.M = kp.M;
   const int cc_blocks = p->cc_count;  // one CTA per short block row
-  if (chunks > 0 && !p->direct_b && !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS)) {
-    const int stack = int(std::min<int64_t>(chunks, 148 * kBsBlocksPerSm));
+  const bool separate = !p->direct_b && !p->fused_stack && chunks > 0 &&
+                        !(p->flags & VBSR_PLAN_DIAG_SKIP_PREPASS);
+  const bool prepass = separate || cc_blocks > 0;
+  if (prepass) {
+    const int stack = separate ? int(std::min<int64_t>(chunks, 148 * kBsBlocksPerSm)) : 0;
     const unsigned blocks = unsigned(stack + cc_blocks);
     switch (kp.rhs) {
       case 8: bstack_kernel<8, false><<<blocks, 256, 0, stream>>>(kp.B, kp.K, p->d_bstack, stack, cc); break;
@@ -785,7 +796,7 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const bool check = (p->flags & VBSR_PLAN_BOUNDS_CHECK) != 0;
-  if (p->direct_b) cfg.numAttrs = 0;  // no pre-pass to overlap
+  if (!prepass) cfg.numAttrs = 0;  // no pre-pass launch to overlap
   if (row_stacked(kp.rhs))
     cudaLaunchKernelEx(&cfg, check ? spmm_tc_kernel<true, true, false, false>
                                    : spmm_tc_kernel<false, true, false, false>, kp);
@@ -840,7 +851,9 @@ vbsr_status fill_params(const vbsr_plan* p, const float* B, float* C, int* statu
   kp->timing = timing;
   // per-CTA cycle counters of instrumented builds follow the timestamps (plan-owned buffer only)
   kp->prof = (timing != nullptr && timing == p->d_timing) ? timing + 2 * p->num_tasks : nullptr;
-  kp->diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH));
+  kp->diag = int(p->flags & (VBSR_PLAN_DIAG_SKIP_COPIES | VBSR_PLAN_DIAG_SKIP_MATH |
+                             VBSR_PLAN_DIAG_SKIP_PREPASS));
+  kp->stack_flag = p->fused_stack ? p->d_stack_flag : nullptr;
   return VBSR_OK;
 }
 
@@ -1088,7 +1101,9 @@ vbsr_status vbsr_plan_execute_noalloc(const vbsr_plan* p, const float* B, float*
 vbsr_status vbsr_plan_launch_count(const vbsr_plan* p, int* out) {
   clear_error();
   if (p == nullptr || out == nullptr) return set_error(VBSR_INVALID_ARGUMENT, "null argument");
-  *out = p->direct_b ? 1 : 2;  // the B pre-pass (unless B is read directly) and the SpMM kernel
+  // the SpMM kernel, plus the pre-pass launch when the stacks are formed separately or short rows
+  // run on the CUDA cores
+  *out = 1 + ((!p->direct_b && !p->fused_stack) || p->cc_count > 0 ? 1 : 0);
   return VBSR_OK;
 }
 

@@ -29,6 +29,9 @@ struct KernelParams {
   u64* timing;          // optional: per CTA (start, end) global timer in ns
   u64* prof;            // instrumented builds only (VBSR_PROF): 16 cycle counters per CTA
   int diag;             // VBSR_PLAN_DIAG_* bits (performance analysis only)
+  // Fused pre-pass: the SpMM's own CTAs form the operand stacks, then arrive on this word (a
+  // self-resetting grid arrival counter, see stack_arrive); nullptr: a separate pre-pass launch.
+  uint32_t* stack_flag;
 };
 
 // ---- stage descriptors -----------------------------------------------------------------------------

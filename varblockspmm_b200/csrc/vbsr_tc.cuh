@@ -200,6 +200,98 @@ __device__ __forceinline__ float4 lo_part4(float4 x) {
   return make_float4(lo_part(x.x), lo_part(x.y), lo_part(x.z), lo_part(x.w));
 }
 
+// ---- fused pre-pass ------------------------------------------------------------------------------
+//
+// With VBSR_PLAN_FUSED_PREPASS the SpMM's own CTAs form B's operand stacks (the same tiles
+// bstack_kernel writes) before their pipelines start, so an execute is one launch. Work is flat over the 16-byte pieces of the tiles' raw (hi) rows:
+// piece f is half (f & 1) of column c = (f >> 1) mod rhs in tile g = f / (2 rhs). Lanes take
+// consecutive pieces, so a warp's stores fill 512 contiguous bytes of a tile (and the lo piece of a
+// hi piece, its row's lo row, 512 more), and each lane pair reads one whole 32-byte sector of a
+// column of B. Each lane keeps kStackUnroll pieces in flight.
+constexpr int kStackUnroll = 4;
+template <bool TR, bool RAW>
+__device__ __forceinline__ void stack_rows_of(int c, int rhs, int& hi, int& lo) {
+  if (TR) {  // rows c: raw B of column c; rows rhs + c: its lo part
+    hi = c;
+    lo = rhs + c;
+  } else if (RAW) {  // raw rows only
+    hi = c;
+    lo = -1;
+  } else {  // pre-split, per quadrant q of 16 columns: 16 rows of hi, then 16 of lo
+    hi = 32 * (c >> 4) + (c & 15);
+    lo = hi + 16;
+  }
+}
+template <bool TR, bool RAW>
+__device__ void stack_fused(const KernelParams& p, long long gw, long long nwarps, int lane) {
+  const long long ngroups = p.K >> 3;
+  const int rhs = p.rhs, lg = __ffs(rhs) - 1, rows = stack_rows(rhs, RAW);
+  const long long pieces = ngroups << (lg + 1), k4 = p.K >> 2;
+  const float4* B4 = reinterpret_cast<const float4*>(p.B);
+  float4* out = reinterpret_cast<float4*>(const_cast<float*>(p.bstack));
+  for (long long u0 = gw; (u0 << 5) < pieces; u0 += nwarps * kStackUnroll) {
+    float4 v[kStackUnroll];
+    long long dst[kStackUnroll];
+    int lo_off[kStackUnroll];
+#pragma unroll
+    for (int k = 0; k < kStackUnroll; ++k) {
+      const long long f = ((u0 + nwarps * k) << 5) + lane;
+      dst[k] = -1;
+      if (f < pieces) {
+        const long long g = f >> (lg + 1);
+        const int c = int(f >> 1) & (rhs - 1), pos = int(f & 1);
+        int hi, lo;
+        stack_rows_of<TR, RAW>(c, rhs, hi, lo);
+        // the swizzle: the 16-byte half u of the row's 32 bytes sits at position u ^ ((row >> 2) & 1)
+        // (a lo row has the same parity as its hi row)
+        const int u = pos ^ ((hi >> 2) & 1);
+        v[k] = __ldcs(B4 + c * k4 + 2 * g + u);
+        dst[k] = g * (2 * rows) + 2 * hi + pos;
+        lo_off[k] = lo >= 0 ? 2 * (lo - hi) : 0;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kStackUnroll; ++k) {
+      if (dst[k] < 0) continue;
+      out[dst[k]] = v[k];
+      if (lo_off[k] != 0) out[dst[k] + lo_off[k]] = lo_part4(v[k]);
+    }
+  }
+}
+// Grid arrival on p.stack_flag, once per CTA after all its stack stores (by one thread, after a
+// CTA barrier). CTA 0 adds 2^31 - (grid - 1), every other CTA 1: the word's top bit flips exactly
+// when the last CTA arrives, and its low bits are back where they started, so the word needs no
+// reset between executes (executes of one plan never overlap). Returns the top bit seen before
+// this CTA's arrival; the stacks are complete once the word's top bit differs from it.
+__device__ __forceinline__ uint32_t stack_arrive(const KernelParams& p) {
+  __threadfence();
+  const uint32_t add = blockIdx.x == 0 ? 0x80000000u - (gridDim.x - 1u) : 1u;
+  return atomicAdd(p.stack_flag, add) & 0x80000000u;
+}
+// Bounded wait (lane 0 polls) for every CTA's stacks; false after a timeout or another warp's abort.
+__device__ __forceinline__ bool wait_stacks(const KernelParams& p, uint32_t sense,
+                                            volatile int* abort_flag, int lane) {
+  int ok = 1;
+  if (lane == 0) {
+    const long long t0 = clock64();
+    while (((ld_acquire_gpu(p.stack_flag) ^ sense) & 0x80000000u) == 0u) {
+      if (*abort_flag) {
+        ok = 0;
+        break;
+      }
+      if (clock64() - t0 > p.wait_limit) {
+        record_status(p.status, VBSR_TIMEOUT, int(blockIdx.x));
+        *abort_flag = 1;
+        ok = 0;
+        break;
+      }
+      __nanosleep(256);
+    }
+    fence_proxy_async_global();  // the bulk copies that follow read what the other CTAs stored
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // ---- CTA pieces ----------------------------------------------------------------------------------
 
 // Barriers (shared-memory addresses).
@@ -222,7 +314,8 @@ struct CtaBars {
 // (cp.async.mbarrier.arrive), which therefore expects 1 + 32 arrivals.
 template <bool CHECK, bool RAW, bool DIRECT>
 __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slots,
-                          const CtaBars& cb, int f, int lane, volatile int* abort_flag) {
+                          const CtaBars& cb, int f, int lane, volatile int* abort_flag,
+                          uint32_t stack_sense) {
   const int D = task.stages, SF = task.stage_floats;
   const int nst = task.stage_end - task.stage_off;
   StageWin win;
@@ -231,11 +324,18 @@ __device__ void tc_feeder(const KernelParams& p, const Task& task, uint32_t slot
   uint32_t ph = 0;
   uint32_t filled = 0, lastpar = 0;
   const uint64_t pol_a = policy_evict_first(), pol_b = policy_evict_last();
-  // The SpMM is launched as a programmatic dependent of the B pre-pass, so that its prologue
-  // overlaps the pre-pass; the feeders are the only warps that read the pre-pass output.
-  if (!DIRECT) griddep_wait();
+  // The feeders are the only warps that read the stacks. Fused pre-pass: wait for every CTA's
+  // share of them. Separate pre-pass launch: the SpMM is its programmatic dependent, so that its
+  // prologue overlaps the pre-pass, and waits for it here.
+  bool go = true;
+  if (!DIRECT) {
+    if (p.stack_flag != nullptr)
+      go = wait_stacks(p, stack_sense, abort_flag, lane);
+    else
+      griddep_wait();
+  }
   VBSR_PROF_T0(t_all);
-  for (int kk = f; kk < nst; kk += kTcFeeders) {
+  for (int kk = f; go && kk < nst; kk += kTcFeeders) {
     const Stage st = win.get();
     if (kPrefetchAhead > 0 && win.has_ahead(kPrefetchAhead) &&
         !(p.diag & VBSR_PLAN_DIAG_SKIP_COPIES)) {
@@ -968,6 +1068,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   __shared__ __align__(8) uint64_t drainbars[kTcMmaWarps];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
+  __shared__ uint32_t stack_sense;
   const Task task = p.tasks[blockIdx.x];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
@@ -1003,6 +1104,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
   cb.accfree0 = smem_addr(&accbars[1][0]);
   cb.drain0 = smem_addr(&drainbars[0]);
 
+  if (!DIRECT && p.stack_flag != nullptr) {  // fused pre-pass: every warp stacks its share of B
+    if (!(p.diag & VBSR_PLAN_DIAG_SKIP_PREPASS))
+      stack_fused<TR, RAW>(p, (long long)blockIdx.x * kTcWarps + warp,
+                           (long long)gridDim.x * kTcWarps, lane);
+    fence_proxy_async_global();
+    __syncthreads();
+    if (threadIdx.x == 0) stack_sense = stack_arrive(p);
+    __syncthreads();
+  }
+
   using RL = Roles<TR>;
   if (warp < RL::mma0)
     tc_split_warp<CHECK, TR, RAW>(p, task, slots, cb, tmem_base, warp, lane, &abort_flag);
@@ -1010,7 +1121,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     tc_mma_warp<CHECK, TR, RAW, DIRECT>(p, task, slots, cb, tmem_base, warp - RL::mma0, lane,
                                         &abort_flag);
   else if (warp < RL::epi0)
-    tc_feeder<CHECK, RAW, DIRECT>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag);
+    tc_feeder<CHECK, RAW, DIRECT>(p, task, slots, cb, warp - RL::feeder0, lane, &abort_flag,
+                                  stack_sense);
   else  // the epilogue warps: TMEM quadrant warp % 4
     tc_epi_warp<CHECK, TR, RAW>(p, task, cb, tmem_base, warp & 3, (warp - RL::epi0) >> 2, lane,
                                 &abort_flag);
