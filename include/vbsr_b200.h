@@ -172,7 +172,9 @@ enum {
    * one launch instead of the pre-pass launch plus the SpMM. Off by default: it is slower (headline
    * 92 against 85 us, large config 15.8 against 14.5 ms), because the SpMM's pipelines cannot start
    * before every CTA's share of the stacks is done, while the separate pre-pass already overlaps
-   * the SpMM's prologue (programmatic dependent launch). */
+   * the SpMM's prologue (programmatic dependent launch). The CTAs wait for one another, so they
+   * must all be resident (one per SM, at most one per SM of the device); a concurrent kernel that
+   * holds SMs for longer than the plan's wait limit makes the execute report VBSR_TIMEOUT. */
   VBSR_PLAN_FUSED_PREPASS = 1u << 7,
   /* Diagnostics for performance analysis only; C is WRONG with either flag set: */
   VBSR_PLAN_DIAG_SKIP_COPIES = 1u << 8, /* producers arm the stages without copying any data  */
