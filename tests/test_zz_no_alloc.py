@@ -18,13 +18,14 @@ from helpers import assert_within_bound, spec_case
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("flags", [0, vb.PLAN_FUSED_PREPASS], ids=["two_launches", "fused"])
 @pytest.mark.parametrize("rhs", [32, 64])
-def test_noalloc_matches_execute_twice(cuda, rhs):
+def test_noalloc_matches_execute_twice(cuda, rhs, flags):
     torch = cuda
     host = spec_case(1024, 8, 2, False, 21)
     B = vb.fill_uniform(21, vb.STREAM_DENSE, 0, host.scalar_cols() * rhs)
     m = vb.Matrix(host)
-    p = vb.Plan(m, vb.PlanOptions(rhs))
+    p = vb.Plan(m, vb.PlanOptions(rhs), flags)
     dB = torch.from_numpy(B).cuda()
     n = host.scalar_rows() * rhs
     ref = torch.full((n,), float("nan"), device="cuda")
