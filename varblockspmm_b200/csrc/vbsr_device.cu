@@ -643,12 +643,12 @@ vbsr_status build_schedule(vbsr_plan* p) {
     }
     task.item_end = int(items.size());
     task.stage_end = int(stream.size());
-    task.team_warps = kTcWarps;
+    task.team_warps = tc_warps(row_stacked(rhs));
     task.stage_floats = slot;
     task.stage_cols = 8 * kMaxStageGroups;
     task.stages = stages;
     h_tasks.push_back(task);
-    p->task_warps.push_back(kTcWarps);
+    p->task_warps.push_back(tc_warps(row_stacked(rhs)));
     p->task_cost.push_back(load[t]);
   }
   p->split_rows = split_rows;
@@ -787,7 +787,7 @@ void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream
   // for the pre-pass with griddepcontrol.wait before the first copy)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(p->num_tasks));
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3(32 * tc_warps(row_stacked(kp.rhs)));
   cfg.dynamicSmemBytes = size_t(p->smem_bytes);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

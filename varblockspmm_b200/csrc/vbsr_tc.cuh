@@ -24,10 +24,12 @@
 // column 16q + j, so they land in lanes j and 16 + j of quadrant q. Either way a warp adds the
 // pair with one shuffle.
 //
-// CTA = twenty warps, one CTA per SM:
-//   warps 0..3   split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4,
-//                which forms A_lo (row-stacked: spreads the stage's A in place into alternating
-//                A / A_lo blocks), fences the writes for the async proxy and hands the slot on;
+// One CTA per SM; warp numbers below are the row-stacked form's (the column-stacked form has 12
+// split warps, then MMA warps 12..15, feeders 16..19 and one epilogue set, warps 20..23):
+//   warps 0..3   split warps: stage k (the CTA's k-th non-empty stage) is split by warp k % 4
+//                (column-stacked: by team k % 4 of three warps), which forms A_lo (row-stacked:
+//                spreads the stage's A in place into alternating A / A_lo blocks), fences the
+//                writes for the async proxy and hands the slot on;
 //   warps 4..7   MMA warps: stage k is issued by MMA warp k % 4 into the warp's own accumulator,
 //                and the slot is released with tcgen05.commit;
 //   warps 8..11  feeders: stage k is copied by feeder k % 4 with cp.async.bulk: the stage's A in
@@ -55,30 +57,28 @@
 
 namespace vbsr_b200 {
 
-// Warp roles (20 warps, one CTA per SM), per form (template parameter TR of the kernel):
-//                     split   MMA   feeders   epilogue
-//   row-stacked         4      4       4       8 (two sets)
-//   column-stacked      8      4       4       4 (one set; its split warps also form B_lo)
+// Warp roles (one CTA per SM), per form (template parameter TR of the kernel):
+//                     split   MMA   feeders   epilogue   warps   registers (at most)
+//   row-stacked         4      4       4       8 (two sets)  20       96
+//   column-stacked     12      4       4       4 (one set)   24       80
+// The column-stacked split warps also form B_lo, in teams of three per stage.
 // Epilogue warps come last and start at a multiple of 4 (a warp reaches the TMEM lanes
 // 32 (warp % 4) ... only); epilogue set e stores the items j with j % sets == e. Every slot
 // count is a multiple of each role's warp count (kTcRingMultiple).
 template <bool TR>
 struct Roles {
-  static constexpr int split = TR ? 4 : 8;
+  static constexpr int split = TR ? 4 : 12;
   static constexpr int epi_sets = TR ? 2 : 1;
   static constexpr int mma0 = split, feeder0 = split + 4, epi0 = split + 8;
-  static_assert(epi0 % 4 == 0 && epi0 + 4 * epi_sets == 20, "role layout");
+  static constexpr int warps = epi0 + 4 * epi_sets;
+  static_assert(epi0 % 4 == 0, "role layout");
 };
-#ifndef VBSR_CS_SPLIT_TEAM
-#define VBSR_CS_SPLIT_TEAM 2
-#endif
-constexpr int kCsSplitTeam = VBSR_CS_SPLIT_TEAM;  // column-stacked form: warps per stage split
+constexpr int kCsSplitTeam = 3;  // column-stacked form: warps that split one stage
 constexpr int kTcMmaWarps = 4;  // MMA-issuing warps
 constexpr int kTcFeeders = 4;   // feeder warps
 constexpr int kTcRingMultiple = 8;
 constexpr int kPrefetchAhead = 2;  // A is prefetched into L2 this many own stages ahead
-constexpr int kTcWarps = 20;
-constexpr int kTcThreads = 32 * kTcWarps;
+__host__ __device__ constexpr int tc_warps(bool tr) { return tr ? Roles<true>::warps : Roles<false>::warps; }
 __host__ __device__ constexpr int stack_m(int nw) { return nw > 32 ? 128 : 64; }
 // RHS widths up to 32 use the row-stacked form (one MMA per group, the operand stack S on the N
 // side); width 64 the column-stacked form (two MMAs per group, S on the M side). S has
@@ -590,18 +590,20 @@ __device__ __forceinline__ void split_stage_rows(uint32_t sp, int groups, int h,
 }
 
 // lo parts of n float4s at shared address sp, written lo_off bytes further (the chunks of 128
-// float4s with index % parts == part).
+// float4s with index % parts == part; 2 KB chunks measured as fast as 1 KB ones here, 512 B ones
+// slower).
 __device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, int lane,
                                            int part = 0, int parts = 1) {
-  for (int i0 = 128 * part; i0 < n; i0 += 128 * parts) {
-    float4 x[4];
+  constexpr int U = 4;
+  for (int i0 = 32 * U * part; i0 < n; i0 += 32 * U * parts) {
+    float4 x[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int i = i0 + 32 * u + lane;
       if (i < n) x[u] = lds128(sp + 16u * i);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int i = i0 + 32 * u + lane;
       if (i < n) sts128(sp + lo_off + 16u * i, lo_part4(x[u]));
     }
@@ -1063,7 +1065,7 @@ __global__ void __launch_bounds__(256, 4) bstack_kernel(const float* __restrict_
 // TR: row-stacked form (rhs <= 32); RAW: column-stacked form with raw-B stacks; DIRECT: those
 // stacks' raw rows read from B itself (no pre-pass).
 template <bool CHECK, bool TR, bool RAW, bool DIRECT>
-__global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
+__global__ void __launch_bounds__(32 * Roles<TR>::warps, 1) spmm_tc_kernel(const __grid_constant__ KernelParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t slots = (smem_addr(smem_raw) + 1023u) & ~1023u;  // 1024-aligned ring
   __shared__ __align__(8) uint64_t bars[3][kMaxStages];  // full, split, empty
@@ -1109,8 +1111,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
 
   if (!DIRECT && p.stack_flag != nullptr) {  // fused pre-pass: every warp stacks its share of B
     if (!(p.diag & VBSR_PLAN_DIAG_SKIP_PREPASS))
-      stack_fused<TR, RAW>(p, (long long)blockIdx.x * kTcWarps + warp,
-                           (long long)gridDim.x * kTcWarps, lane);
+      stack_fused<TR, RAW>(p, (long long)blockIdx.x * Roles<TR>::warps + warp,
+                           (long long)gridDim.x * Roles<TR>::warps, lane);
     fence_proxy_async_global();
     __syncthreads();
     if (threadIdx.x == 0) stack_sense = stack_arrive(p);
