@@ -613,7 +613,7 @@ __device__ __forceinline__ void split_flat(uint32_t sp, int n, uint32_t lo_off, 
 // Column-stacked form: A_lo of a whole stage at shared address sp: the stage's A (2h float4s per
 // group, groups one after another) at sp, its A_lo at the same offsets 32 h G bytes further. The
 // chunks are 64 float4s (two loads per lane in flight before their stores): a stage's A is only
-// 2-5 KB, and chunks this small share it evenly between the two warps of a team (with 4 KB chunks
+// 2-5 KB, and chunks this small share it evenly among the warps of a team (with 4 KB chunks
 // one warp often had nearly all of it; large config kernel 12.06 -> 11.59 ms).
 __device__ __forceinline__ void split_stage(uint32_t sp, int groups, int h, int lane,
                                             int part = 0, int parts = 1) {
