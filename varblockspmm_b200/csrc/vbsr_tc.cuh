@@ -203,8 +203,9 @@ __device__ __forceinline__ float4 lo_part4(float4 x) {
 // ---- fused pre-pass ------------------------------------------------------------------------------
 //
 // With VBSR_PLAN_FUSED_PREPASS the SpMM's own CTAs form B's operand stacks (the same tiles
-// bstack_kernel writes) before their pipelines start, so an execute is one launch. Work is flat over the 16-byte pieces of the tiles' raw (hi) rows:
-// piece f is half (f & 1) of column c = (f >> 1) mod rhs in tile g = f / (2 rhs). Lanes take
+// bstack_kernel writes) before their pipelines start, so an execute is one launch. Work is flat
+// over the 16-byte pieces of the tiles' raw (hi) rows: piece f is half (f & 1) of column
+// c = (f >> 1) mod rhs in tile g = f / (2 rhs). Lanes take
 // consecutive pieces, so a warp's stores fill 512 contiguous bytes of a tile (and the lo piece of a
 // hi piece, its row's lo row, 512 more), and each lane pair reads one whole 32-byte sector of a
 // column of B. Each lane keeps kStackUnroll pieces in flight.
