@@ -749,9 +749,9 @@ void free_plan(vbsr_plan* p) {
   delete p;
 }
 
-// One execute on `stream`: the B pre-pass launch and then the SpMM, or only the SpMM kernel, which
-// then forms B's operand stacks itself (VBSR_PLAN_FUSED_PREPASS). The short block rows on the CUDA cores
-// (VBSR_PLAN_CUDA_CORE_ROWS) are CTAs of a pre-pass launch either way.
+// One execute on `stream`: the B pre-pass launch and then the SpMM, or only the SpMM kernel,
+// which then forms B's operand stacks itself (VBSR_PLAN_FUSED_PREPASS). The short block rows on
+// the CUDA cores (VBSR_PLAN_CUDA_CORE_ROWS) are CTAs of a pre-pass launch either way.
 void launch_spmm(const vbsr_plan* p, const KernelParams& kp, cudaStream_t stream) {
   const int64_t bsg = bs_groups(kp.rhs);
   const int64_t chunks = (kp.K / 8 + bsg - 1) / bsg;  // bs_groups(rhs) groups per block iteration
