@@ -166,3 +166,25 @@ def test_compulsory_bytes_formula():
               + 4 * S + 8 * (S + 1) + 4 * K * N + 4 * M * N)
     by, fl = vb.compulsory_bytes(m, N)
     assert by == expect and fl == 2 * m.values.size * N
+
+
+@pytest.mark.parametrize("grid", [1, 2, 3, 7, 148])
+def test_fused_prepass_arrival_word(grid):
+    """The fused pre-pass's grid arrival (stack_arrive in vbsr_tc.cuh), restated on uint32: CTA 0
+    adds 2^31 - (grid - 1), every other CTA adds 1, in any order. Over many launches from any
+    starting low bits of 0, the top bit differs from the one each CTA saw at its own arrival
+    exactly once every CTA has arrived, and the word's low bits return to 0 after each launch, so
+    it needs no reset between executes."""
+    rng = np.random.default_rng(grid)
+    word = 0
+    for launch in range(6):
+        order = rng.permutation(grid)
+        seen = {}
+        for n, cta in enumerate(order):
+            add = (0x80000000 - (grid - 1)) if cta == 0 else 1
+            seen[cta] = word & 0x80000000
+            word = (word + add) & 0xFFFFFFFF
+            done = all(((word ^ seen[c]) & 0x80000000) != 0 for c in seen)
+            # no waiter may pass before the last arrival; every waiter passes at it
+            assert done == (n == grid - 1), (launch, n)
+        assert word & 0x7FFFFFFF == 0
